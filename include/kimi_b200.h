@@ -1,0 +1,193 @@
+/*
+ * kimi_b200.h - C ABI of the B200 (sm_100a) quantized decode hot path.
+ *
+ * Every entry point takes plain device pointers, element counts, element
+ * strides and a CUDA stream passed as `void*` (a cudaStream_t; NULL is the
+ * legacy default stream).  No torch or CUDA type appears in a signature.
+ * Nothing here allocates device memory except where a function says so;
+ * callers that need scratch memory pass it in and size it with the matching
+ * *_workspace_size() function.
+ *
+ * Data formats follow the reference codec (engine/quant/w4a16.py:1-6, 98-99):
+ *   - packed INT4 weights: uint8 [N, K/2] row-major (grouped banks: [E, N, K/2]);
+ *     the code of the even reduction index k sits in the low nibble, the odd
+ *     one in the high nibble; a nibble >= 8 decodes to nibble - 16.
+ *   - scales: bf16 [N, K/group] (banks: [E, N, K/group]); group is 32 (the
+ *     reference format) or 128 (the restated format); any group of 32 times a
+ *     power of two that divides K is accepted.
+ *   - decoded weight = bf16(float(code) * float(scale)), products and sums in
+ *     fp32, every projection output rounded to bf16 (w4a16_gemv.py:146-158).
+ *   - bf16 values travel as uint16_t bit patterns.
+ *
+ * Return value: KB_OK (0) or a kb_status code.  kb_last_error() returns a
+ * human-readable message for the last failing call on the calling thread.
+ * Arguments are validated before any launch; a failing call launches nothing.
+ * No entry point throws, aborts or traps.
+ */
+#ifndef KIMI_B200_H
+#define KIMI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KB_API __attribute__((visibility("default")))
+#else
+#define KB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum kb_status {
+  KB_OK = 0,
+  KB_ERR_NULL_POINTER = 1,     /* a required pointer is NULL                    */
+  KB_ERR_BAD_SHAPE = 2,        /* a dimension is negative, zero or inconsistent */
+  KB_ERR_BAD_GROUP = 3,        /* group size is not a multiple of 32 dividing K */
+  KB_ERR_ALIGNMENT = 4,        /* a pointer or stride breaks the 16-byte rule   */
+  KB_ERR_WORKSPACE = 5,        /* workspace missing or smaller than required    */
+  KB_ERR_UNSUPPORTED = 6,      /* a size above a documented limit               */
+  KB_ERR_LAUNCH = 7,           /* the CUDA runtime rejected a launch            */
+  KB_ERR_DEVICE = 8            /* a device-side check recorded an error         */
+} kb_status;
+
+/* Library version, major*10000 + minor*100 + patch. */
+KB_API int kb_version(void);
+
+/* Message for the last failing call on this thread ("" after success). */
+KB_API const char* kb_last_error(void);
+
+/* Programmatic dependent launch: when enabled (the default), kernels are
+ * launched with the programmatic-stream-serialization attribute so that a
+ * kernel's prologue overlaps the tail of the kernel before it on the stream. */
+KB_API void kb_set_pdl(int enabled);
+KB_API int kb_get_pdl(void);
+
+/* Device-side error word.  Kernels that meet an input they cannot process
+ * safely (an expert index outside [0, E)) substitute a safe value (expert 0)
+ * and set a bit here.
+ * kb_device_errors() copies the word to the host (synchronizes the stream)
+ * and clears it.  Bit 0: expert index out of range. */
+KB_API int kb_device_errors(void* stream, uint32_t* out_bits);
+
+/* ------------------------------------------------------------------------- */
+/* Codec (engine/quant/w4a16.py:68-105 quantise).                              */
+/* ------------------------------------------------------------------------- */
+
+/* Quantise bf16 W[N,K] (row stride w_stride elements) into packed [N,K/2]
+ * and scales [N,K/group]: scale = bf16(absmax/7) (1 for an all-zero group,
+ * else clamped to the smallest normal bf16), code = clamp(rint(w/scale),-7,7).
+ * Non-finite inputs set *nonfinite_flag (device int32, may be NULL) to 1. */
+KB_API int kb_w4a16_quantise(const uint16_t* w, int64_t w_stride, int64_t N, int64_t K,
+                      int64_t group, uint8_t* packed, uint16_t* scales,
+                      int32_t* nonfinite_flag, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Dense W4A16 projection.                                                     */
+/* Replaces the registry op `w4a16_dense` (engine/kernels/__init__.py:92-125,  */
+/* shipped variant engine/kernels/w4a16_dense_gemv.py:312-336, reference       */
+/* engine/quant/triton_w4a16.py:151-188).  y[M,N] = x[M,K] . dequant(W)^T.     */
+/* x: bf16 [M,K] with row stride x_stride (elements, unit stride along K);     */
+/* y: bf16 [M,N] with row stride y_stride.  M == 0 is a no-op.                 */
+/* ------------------------------------------------------------------------- */
+KB_API int kb_w4a16_dense(const uint16_t* x, int64_t x_stride, int64_t M, int64_t K,
+                   const uint8_t* packed, const uint16_t* scales, int64_t N,
+                   int64_t group, uint16_t* y, int64_t y_stride, void* stream);
+
+/* Up to KB_MAX_DENSE_PROBLEMS independent dense projections in one launch,
+ * each with its own x, K, N, weights and output.  Replaces the unwired
+ * `fused_qkv_w4a16` (engine/kernels/w4a16_fused_qkv.py:342-389), which is the
+ * three-problem case with one shared x. */
+#define KB_MAX_DENSE_PROBLEMS 8
+typedef struct kb_dense_problem {
+  const uint16_t* x; int64_t x_stride; int64_t M; int64_t K;
+  const uint8_t* packed; const uint16_t* scales; int64_t N; int64_t group;
+  uint16_t* y; int64_t y_stride;
+} kb_dense_problem;
+KB_API int kb_w4a16_dense_multi(const kb_dense_problem* problems, int count, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Grouped (expert-indexed) W4A16 projection.                                  */
+/* Replaces the registry op `w4a16_grouped` (engine/kernels/__init__.py:26-79; */
+/* shipped engine/kernels/w4a16_gemv.py:610-635, reference                     */
+/* engine/kernels/w4a16_grouped.py:121-194).                                   */
+/* y[t,r,:] = x[t,:] . dequant(W[idx[t,r]])^T for every token t < T and route  */
+/* r < R.  x: bf16 [T,K] (row stride x_stride); idx: int64 [T,R] contiguous;   */
+/* packed: uint8 [E,N,K/2]; scales: bf16 [E,N,K/group]; y: bf16 [T,R,N]        */
+/* contiguous.  Assignments sharing an expert read that expert's weights once. */
+/* An index outside [0,E) is computed as expert 0 (never read out of bounds)  */
+/* and sets device error bit 0.  T*R must not exceed KB_MAX_ASSIGNMENTS.        */
+/* ------------------------------------------------------------------------- */
+#define KB_MAX_ASSIGNMENTS 4096
+KB_API int kb_w4a16_grouped(const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
+                     const int64_t* idx, int64_t R, const uint8_t* packed,
+                     const uint16_t* scales, int64_t E, int64_t N, int64_t group,
+                     uint16_t* y, void* stream);
+
+/* Fused gate/up + SwiGLU.  Replaces the registry op `w4a16_swiglu`
+ * (engine/kernels/__init__.py:164-218; fused variant
+ * engine/kernels/w4a16_gemv.py:772-790).  y[t,r,n] =
+ * bf16( bf16(silu(bf16(g))) * bf16(u) ) with g = x[t].W1[e]^T, u = x[t].W3[e]^T
+ * (the F.silu(gate)*up contract, w4a16_gemv.py:214-221). */
+KB_API int kb_w4a16_swiglu(const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
+                    const int64_t* idx, int64_t R, const uint8_t* w1_packed,
+                    const uint16_t* w1_scales, const uint8_t* w3_packed,
+                    const uint16_t* w3_scales, int64_t E, int64_t N, int64_t group,
+                    uint16_t* y, void* stream);
+
+/* Down projection + routing-weighted combine.  Replaces `fused_w2_combine`
+ * (engine/kernels/moe_combine.py:264-324; reference sequence
+ * engine/klinear/moe.py:317-334 and moe_combine.py:209-261):
+ *   o[t,r]  = bf16( activated[t,r,:] . dequant(W2[idx[t,r]])^T )
+ *   out[t]  = bf16( sum_{r<R-1} float(o[t,r]) * weights[t,r] ) + o[t,R-1]
+ * (bf16 add; the last route is the shared expert, weight 1, its weights entry
+ * ignored).  activated: bf16 [T,R,K] contiguous; idx int64 [T,R]; weights fp32
+ * [T,R] with row stride w_stride (>= R-1); out bf16 [T,N].  The per-route
+ * outputs and arrival counters live in `workspace` (device memory of at least
+ * kb_w4a16_w2_combine_workspace_size(T,R,N) bytes, zero-filled before its
+ * first use; every call leaves the counters at zero again). */
+KB_API size_t kb_w4a16_w2_combine_workspace_size(int64_t T, int64_t R, int64_t N);
+KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, int64_t K,
+                        const int64_t* idx, const float* weights, int64_t w_stride,
+                        const uint8_t* w2_packed, const uint16_t* w2_scales,
+                        int64_t E, int64_t N, int64_t group, uint16_t* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Router (engine/klinear/router.py:47-85, sigmoid path, one expert group).   */
+/* logits = float(hidden) . float(W)^T; scores = sigmoid(logits);              */
+/* choice = scores + bias; top_k by (choice desc, index asc);                  */
+/* w = scores[idx] / (sum + 1e-20) (if renormalize) * scaling.                 */
+/* hidden bf16 [T,K] (row stride h_stride); weight bf16 [E,K]; bias fp32 [E]   */
+/* (NULL = zeros); idx_out int64 [T,top_k]; w_out fp32 [T,top_k].  A NaN       */
+/* choice score ranks below every number, so indices stay in [0,E).            */
+/* Limits: E <= 1024, top_k <= 32.                                             */
+/* ------------------------------------------------------------------------- */
+KB_API size_t kb_router_workspace_size(int64_t T, int64_t E);
+KB_API int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t K,
+                   const uint16_t* weight, const float* bias, int64_t E,
+                   int64_t top_k, int renormalize, float scaling,
+                   int64_t* idx_out, float* w_out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* KDA recurrent decode step.  Replaces kda_decode_step                        */
+/* (engine/kernels/kda_step.py:273-293, reference :173-196).  fp32 throughout: */
+/*   S' = S * exp(decay)[:,None];  p = S'^T k;  d = v - p;                      */
+/*   S  <- S' + (beta*k) d^T  (in place);  o = S^T (q*scale).                  */
+/* state [B,H,Dk,Dv] with element strides (sb,sh,sk) and unit stride along Dv; */
+/* q,k,decay [B,H,Dk], v [B,H,Dv], beta [B,H], out [B,H,Dv] contiguous.        */
+/* out_bf16 (may be NULL) additionally receives bf16(o).  Dk,Dv <= 256.        */
+/* ------------------------------------------------------------------------- */
+KB_API int kb_kda_decode_step(float* state, int64_t sb, int64_t sh, int64_t sk,
+                       const float* q, const float* k, const float* v,
+                       const float* decay, const float* beta, int64_t B,
+                       int64_t H, int64_t Dk, int64_t Dv, float scale,
+                       float* out, uint16_t* out_bf16, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KIMI_B200_H */

@@ -1,0 +1,137 @@
+"""CPU restatements of the hot-path operators (test oracle, not product code).
+
+Each function cites the reference it restates.  Decoded weights are
+bf16(code * scale) (engine/kernels/w4a16_gemv.py:146-158,
+engine/quant/triton_w4a16.py:105-113); products and sums run in fp32 on the
+CPU; every projection output is rounded to bf16 (w4a16_gemv.py:533-539).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .codec import decode_bf16
+
+
+def dense(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """x[M,K] . dequant(W[N,K])^T -> bf16 [M,N]  (registry op w4a16_dense,
+    engine/kernels/__init__.py:92-125; the same test oracle as
+    tests/test_w4a16_dense_gemv.py:7-22 with bf16-rounded decode)."""
+    w = decode_bf16(packed, scales)
+    return F.linear(x.float(), w).to(torch.bfloat16)
+
+
+def grouped(
+    x: torch.Tensor, idx: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor
+) -> torch.Tensor:
+    """y[t,r] = x[t] . dequant(W[idx[t,r]])^T -> bf16 [T,R,N]
+    (engine/kernels/w4a16_grouped.py:121-194, w4a16_gemv.py:610-635)."""
+    t, r = idx.shape
+    n = packed.shape[1]
+    out = torch.empty((t, r, n), dtype=torch.bfloat16)
+    xf = x.float()
+    for e in torch.unique(idx).tolist():
+        tok, route = torch.where(idx == e)
+        w = decode_bf16(packed[e], scales[e])
+        out[tok, route] = F.linear(xf[tok], w).to(torch.bfloat16)
+    return out
+
+
+def swiglu(
+    x: torch.Tensor,
+    idx: torch.Tensor,
+    w1p: torch.Tensor,
+    w1s: torch.Tensor,
+    w3p: torch.Tensor,
+    w3s: torch.Tensor,
+) -> torch.Tensor:
+    """F.silu(grouped(w1)) * grouped(w3) in bf16 (engine/kernels/__init__.py:182-197)."""
+    gate = grouped(x, idx, w1p, w1s)
+    up = grouped(x, idx, w3p, w3s)
+    return F.silu(gate) * up
+
+
+def w2_combine(
+    activated: torch.Tensor,
+    idx: torch.Tensor,
+    weights: torch.Tensor,
+    w2p: torch.Tensor,
+    w2s: torch.Tensor,
+) -> torch.Tensor:
+    """Down projection of every route + combine (engine/kernels/moe_combine.py:209-261).
+
+    ``weights`` has R columns (last ignored) or R-1 columns (routed only).
+    """
+    t, r, k = activated.shape
+    outputs = torch.empty((t, r, w2p.shape[1]), dtype=torch.bfloat16)
+    for route in range(r):
+        outputs[:, route] = grouped(activated[:, route], idx[:, route : route + 1], w2p, w2s)[:, 0]
+    routed = (
+        outputs[:, : r - 1].float().mul(weights[:, : r - 1].float().unsqueeze(-1)).sum(dim=1)
+    ).to(torch.bfloat16)
+    return routed + outputs[:, r - 1]
+
+
+def fused_qkv(x, qp, qs, kp, ks, vp, vs):
+    """Three dense projections (engine/kernels/w4a16_fused_qkv.py:257-271)."""
+    return dense(x, qp, qs), dense(x, kp, ks), dense(x, vp, vs)
+
+
+def router_logits(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """fp32 logits (engine/klinear/router.py:51)."""
+    return F.linear(hidden.reshape(-1, hidden.shape[-1]).float(), weight.float())
+
+
+def router_topk(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    top_k: int,
+    *,
+    renormalize: bool = True,
+    scaling: float = 1.0,
+    logits: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Sigmoid top-k with ties broken by the lower index (engine/klinear/router.py:47-85).
+
+    The reference calls torch.topk(sorted=False), whose tie order is
+    unspecified; this restatement orders by (choice desc, index asc) with a
+    stable sort.  Returns (indices [T,k] in that order, weights [T,k] fp32,
+    choice scores [T,E]).
+    """
+    lg = router_logits(hidden, weight) if logits is None else logits
+    scores = lg.sigmoid()
+    choice = scores + (bias.float().unsqueeze(0) if bias is not None else 0.0)
+    order = torch.sort(choice, dim=-1, descending=True, stable=True).indices
+    idx = order[:, :top_k]
+    w = scores.gather(1, idx)
+    if top_k > 1 and renormalize:
+        w = w / (w.sum(dim=-1, keepdim=True) + 1e-20)
+    return idx, w * scaling, choice
+
+
+def shape_stable_indices(idx: torch.Tensor, shared_id: int) -> torch.Tensor:
+    """Append the shared expert as the last route (engine/klinear/moe.py:23-36)."""
+    shared = torch.full((idx.shape[0], 1), shared_id, dtype=idx.dtype)
+    return torch.cat((idx, shared), dim=1)
+
+
+def kda_step(
+    state: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    decay: torch.Tensor,
+    beta: torch.Tensor,
+    *,
+    scale: float,
+) -> torch.Tensor:
+    """KDA recurrence, mutating ``state`` (engine/kernels/kda_step.py:173-196)."""
+    candidate = state * torch.exp(decay).unsqueeze(-1)
+    prediction = (candidate * k.unsqueeze(-1)).sum(dim=-2)
+    delta = v - prediction
+    candidate = candidate + (beta.unsqueeze(-1).unsqueeze(-1) * k.unsqueeze(-1) * delta.unsqueeze(-2))
+    output = (candidate * (q * scale).unsqueeze(-1)).sum(dim=-2)
+    state.copy_(candidate)
+    return output

@@ -1,0 +1,66 @@
+"""Shared test configuration.
+
+Markers: ``gpu`` tests need a CUDA device (run on a B200 with ``-m gpu``);
+everything else runs on the CPU.  GPU tests call the CUDA kernels through the
+C ABI (``local_kimi_b200._lib``) via the torch-facing ``ops`` layer and check
+them against the CPU oracle in ``oracle/``.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+GOLDEN = ROOT / "tests" / "golden" / "reference_g32.pt"
+
+# Tolerance of the north-star parity contract: an element passes when it is
+# within 2e-2 relative OR 1e-3 absolute of the fp32-accumulated oracle.
+REL_TOL = 2e-2
+ABS_TOL = 1e-3
+
+
+def pytest_configure(config: pytest.Config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def golden() -> dict:
+    return torch.load(GOLDEN, weights_only=True)
+
+
+@pytest.fixture(scope="session")
+def cuda() -> torch.device:
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    return torch.device("cuda", 0)
+
+
+def close_mask(actual: torch.Tensor, expected: torch.Tensor, rel: float = REL_TOL,
+               abs_: float = ABS_TOL) -> torch.Tensor:
+    a = actual.detach().float().cpu()
+    e = expected.detach().float().cpu()
+    diff = (a - e).abs()
+    return (diff <= abs_) | (diff <= rel * e.abs()) | ((a == e) & torch.isfinite(e)) | (
+        torch.isnan(a) & torch.isnan(e))
+
+
+def assert_close(actual: torch.Tensor, expected: torch.Tensor, rel: float = REL_TOL,
+                 abs_: float = ABS_TOL, what: str = "") -> None:
+    assert actual.shape == expected.shape, f"{what}: shape {tuple(actual.shape)} != {tuple(expected.shape)}"
+    ok = close_mask(actual, expected, rel, abs_)
+    if not bool(ok.all()):
+        bad = (~ok).nonzero()
+        first = tuple(bad[0].tolist())
+        a = actual.detach().float().cpu()[first].item()
+        e = expected.detach().float().cpu()[first].item()
+        raise AssertionError(
+            f"{what}: {int((~ok).sum())} of {ok.numel()} elements outside rel {rel} / abs {abs_}; "
+            f"first at {first}: got {a}, expected {e}"
+        )
