@@ -146,7 +146,10 @@ KB_API int kb_w4a16_swiglu(const uint16_t* x, int64_t x_stride, int64_t T, int64
  * [T,R] with row stride w_stride (>= R-1); out bf16 [T,N].  The per-route
  * outputs and arrival counters live in `workspace` (device memory of at least
  * kb_w4a16_w2_combine_workspace_size(T,R,N) bytes, zero-filled before its
- * first use; every call leaves the counters at zero again). */
+ * first use; every call leaves its counters at zero again, so a buffer may be
+ * reused for calls of the same (T,R,N) without clearing; where the counters
+ * sit depends on (T,R,N), so zero the buffer again before using it for another
+ * shape).  Calls that share a workspace must not overlap on the GPU. */
 KB_API size_t kb_w4a16_w2_combine_workspace_size(int64_t T, int64_t R, int64_t N);
 KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, int64_t K,
                         const int64_t* idx, const float* weights, int64_t w_stride,
@@ -160,7 +163,10 @@ KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, 
 /* choice = scores + bias; top_k by (choice desc, index asc);                  */
 /* w = scores[idx] / (sum + 1e-20) (if renormalize) * scaling.                 */
 /* hidden bf16 [T,K] (row stride h_stride); weight bf16 [E,K]; bias fp32 [E]   */
-/* (NULL = zeros); idx_out int64 [T,top_k]; w_out fp32 [T,top_k].  A NaN       */
+/* (NULL = zeros); idx_out int64 [T,top_k]; w_out fp32 [T,top_k].  The         */
+/* workspace (kb_router_workspace_size bytes) follows the same rules as the    */
+/* down+combine workspace: zero before first use, reuse for the same (T,E).    */
+/* A NaN                                                                       */
 /* choice score ranks below every number, so indices stay in [0,E).            */
 /* Limits: E <= 1024, top_k <= 32.                                             */
 /* ------------------------------------------------------------------------- */

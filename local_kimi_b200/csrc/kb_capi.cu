@@ -56,16 +56,13 @@ uint32_t* device_error_word(int device) {
 }
 
 int bind_stream_device(void* stream) {
+  // The library's runtime follows the context current on the calling thread,
+  // which is the device the caller (torch) made current.  No stream query is
+  // made here: stream queries are not permitted while a stream is capturing.
+  (void)stream;
   int cur = 0;
   cudaGetDevice(&cur);
-  if (stream == nullptr) return cur;
-  int dev = cur;
-  if (cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &dev) != cudaSuccess) {
-    cudaGetLastError();
-    return cur;
-  }
-  if (dev != cur) cudaSetDevice(dev);
-  return dev;
+  return cur;
 }
 
 }  // namespace kb

@@ -78,19 +78,23 @@ def _dense_contig(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() and t.data_ptr() % 16 == 0 else t.contiguous()
 
 
-_WORKSPACES: dict[tuple[str, int, int], torch.Tensor] = {}
+_WORKSPACES: dict[tuple, torch.Tensor] = {}
 
 
-def _workspace(kind: str, device: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-filled scratch kept per (kind, device, stream).
+def _workspace(kind: str, device: torch.device, nbytes: int, shape: tuple) -> torch.Tensor:
+    """Zero-filled scratch kept per (kind, device, stream, problem shape).
 
-    The router and down+combine kernels leave their arrival counters at zero
-    after every call, so the buffer is zeroed only when it is created or grown.
+    The router and down+combine kernels keep arrival counters in their scratch
+    and leave them at zero after every call.  The counters' position depends on
+    the problem shape, so a buffer is reused only for the same shape: a buffer
+    shared between shapes could place one shape's counters on another shape's
+    leftover data.
     """
     stream = torch.cuda.current_stream(device).cuda_stream
-    key = (kind, device.index if device.index is not None else torch.cuda.current_device(), stream)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (kind, index, stream, shape)
     ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes:
+    if ws is None:
         ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws
@@ -374,7 +378,7 @@ def _down_combine(
     p2, s2 = _dense_contig(w2_packed), _dense_contig(w2_scales)
     lib = _lib.lib()
     need = int(lib.kb_w4a16_w2_combine_workspace_size(t, r, n))
-    ws = _workspace("w2_combine", act.device, need)
+    ws = _workspace("w2_combine", act.device, need, (t, r, n))
     _lib.call(
         "kb_w4a16_w2_combine",
         _p(act), c_int64(t), c_int64(r), c_int64(k), _p(idx), _p(cw), c_int64(cw.stride(0)),
@@ -461,7 +465,7 @@ def moe_router(
         b = bias.detach().to(device=flat.device, dtype=torch.float32).contiguous()
     lib = _lib.lib()
     need = int(lib.kb_router_workspace_size(tokens, experts))
-    ws = _workspace("router", flat.device, need)
+    ws = _workspace("router", flat.device, need, (tokens, experts))
     _lib.call(
         "kb_router_topk",
         _p(x), c_int64(x.stride(0)), c_int64(tokens), c_int64(hidden), _p(w), _p(b),

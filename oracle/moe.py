@@ -34,8 +34,12 @@ class MoEBanks:
         return self.router_weight.shape[0]
 
 
-def moe_layer(hidden: torch.Tensor, banks: MoEBanks) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """hidden bf16 [T, H] -> (output bf16 [T, H], indices [T, k], weights fp32 [T, k])."""
+def moe_layer(hidden: torch.Tensor, banks: MoEBanks, *, return_parts: bool = False):
+    """hidden bf16 [T, H] -> (output bf16 [T, H], indices [T, k], weights fp32 [T, k]).
+
+    With ``return_parts`` a fourth element gives the per-element rounding bound
+    of the combine (ops.combine_rounding_bound).
+    """
     idx, weights, _ = ops.router_topk(
         hidden, banks.router_weight, banks.router_bias, banks.top_k, scaling=banks.scaling
     )
@@ -43,5 +47,9 @@ def moe_layer(hidden: torch.Tensor, banks: MoEBanks) -> tuple[torch.Tensor, torc
     activated = ops.swiglu(
         hidden, stable, banks.w1_packed, banks.w1_scales, banks.w3_packed, banks.w3_scales
     )
-    out = ops.w2_combine(activated, stable, weights, banks.w2_packed, banks.w2_scales)
+    out, bound = ops.w2_combine(
+        activated, stable, weights, banks.w2_packed, banks.w2_scales, return_parts=True
+    )
+    if return_parts:
+        return out, idx, weights, bound
     return out, idx, weights

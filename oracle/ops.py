@@ -58,10 +58,14 @@ def w2_combine(
     weights: torch.Tensor,
     w2p: torch.Tensor,
     w2s: torch.Tensor,
-) -> torch.Tensor:
+    *,
+    return_parts: bool = False,
+):
     """Down projection of every route + combine (engine/kernels/moe_combine.py:209-261).
 
     ``weights`` has R columns (last ignored) or R-1 columns (routed only).
+    With ``return_parts`` also returns the bf16 routed sum and shared output
+    whose bf16 sum is the result.
     """
     t, r, k = activated.shape
     outputs = torch.empty((t, r, w2p.shape[1]), dtype=torch.bfloat16)
@@ -70,7 +74,33 @@ def w2_combine(
     routed = (
         outputs[:, : r - 1].float().mul(weights[:, : r - 1].float().unsqueeze(-1)).sum(dim=1)
     ).to(torch.bfloat16)
-    return routed + outputs[:, r - 1]
+    out = routed + outputs[:, r - 1]
+    if return_parts:
+        return out, combine_rounding_bound(outputs, weights, routed)
+    return out
+
+
+def bf16_spacing(values: torch.Tensor) -> torch.Tensor:
+    """Distance between adjacent bf16 numbers at |values| (8 significant bits)."""
+    m = values.float().abs().clamp_min(torch.finfo(torch.float32).tiny)
+    return torch.exp2(torch.floor(torch.log2(m)) - 7)
+
+
+def combine_rounding_bound(outputs: torch.Tensor, weights: torch.Tensor,
+                           routed: torch.Tensor) -> torch.Tensor:
+    """One bf16 spacing of every rounded term the combined output is built from.
+
+    out = bf16(sum_r w_r y_r) + y_shared, each y_r a bf16-rounded dot product.
+    An implementation whose fp32 sums differ from this oracle's only in order
+    may land each rounded term on the neighbouring bf16 value; this bound is
+    the sum of those spacings (weighted by |w_r| for the routed terms).  It
+    matters only where routed and shared cancel.
+    """
+    r = outputs.shape[1]
+    bound = bf16_spacing(routed) + bf16_spacing(outputs[:, r - 1])
+    bound = bound + (weights[:, : r - 1].float().abs().unsqueeze(-1)
+                     * bf16_spacing(outputs[:, : r - 1])).sum(dim=1)
+    return bound
 
 
 def fused_qkv(x, qp, qs, kp, ks, vp, vs):

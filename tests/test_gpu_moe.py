@@ -68,9 +68,11 @@ def test_moe_layer_matches_oracle(cuda, tokens, group, skew):
     out, idx, w = kmoe.moe_forward(hidden, layer)
     used = torch.unique(torch.cat((idx.flatten().cpu(), torch.tensor([256]))))
     banks = _oracle_layer(layer, used)
-    ref_out, ref_idx, ref_w = omoe.moe_layer(hidden.cpu(), banks)
+    ref_out, ref_idx, ref_w, bound = omoe.moe_layer(hidden.cpu(), banks, return_parts=True)
     assert torch.equal(idx.cpu(), ref_idx), "router indices differ"
     torch.testing.assert_close(w.cpu(), ref_w, rtol=1e-5, atol=1e-6)
-    assert_close(out, ref_out, what=f"moe layer T={tokens} g{group}")
+    # Where the routed sum and the shared output cancel, each element is also
+    # allowed the rounding bound of the oracle's bf16 intermediates.
+    assert_close(out, ref_out, what=f"moe layer T={tokens} g{group}", allowance=bound)
     again, _, _ = kmoe.moe_forward(hidden, layer)
     assert torch.equal(out, again)

@@ -226,10 +226,11 @@ def test_combine_decode_shapes_and_repeat(cuda, tokens):
     remap = torch.full((257,), -1, dtype=torch.long)
     remap[used] = torch.arange(used.numel())
     sel = used.to(cuda)
-    expected = oref.w2_combine(act.cpu(), remap[idx], weights, w2p[sel].cpu(), w2s[sel].cpu())
+    expected, bound = oref.w2_combine(act.cpu(), remap[idx], weights, w2p[sel].cpu(),
+                                      w2s[sel].cpu(), return_parts=True)
     out1 = ops.fused_w2_combine(act, idx.to(cuda), weights.to(cuda), w2p, w2s)
     out2 = ops.fused_w2_combine(act, idx.to(cuda), weights.to(cuda), w2p, w2s)
-    assert_close(out1, expected, what=f"combine T={tokens}")
+    assert_close(out1, expected, what=f"combine T={tokens}", allowance=bound)
     assert torch.equal(out1, out2), "second call differs: arrival counters not reset"
     # routed-only weights [T, 8] through the layer-facing entry point
     out3 = ops.moe_down_combine(act, idx.to(cuda), weights[:, :8].contiguous().to(cuda), w2p, w2s)
