@@ -1,0 +1,541 @@
+#!/usr/bin/env python
+"""Decode-throughput benchmark of the Kimi-Linear-48B-A3B W4A16 hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+
+A step is one decode step of the hot path (local_kimi_b200.decode): for all
+27 layers the INT4 attention projections, the KDA recurrent-state step, the
+MoE router/experts/combine, then the INT4 lm_head, over B tokens, with
+random-init weights of the real shapes (about 25 GB, resident in HBM).  The
+step is captured once in a CUDA graph (as the reference engine captures its
+decode step, engine/klinear/generate.py:226-276) and replayed.
+
+Printed: one JSON line.  ``value`` = tokens/s over all ranks with inputs
+resident in HBM (device-timed, max over ranks); ``e2e`` = the same metric
+with a host->device copy of the step input and a device->host copy of the
+logits inside the timed region; ``roofline`` = achieved HBM bandwidth of the
+W4A16 projection engine launches of one step, timed alone in their own graph;
+``cpu_baseline`` = the CPU oracle on a bounded sample of the same step.
+Every step reads ~1.8 GB of weights, far more than the 126 MB L2, so no L2
+flush is needed between steps.
+
+``--impl reference`` times the reference's CPU path restated in ``oracle/``
+(the reference is pure Python/torch and does not exist on the GPU box) on all
+host cores, on a bounded per-step sample, and prints the same metric.
+With torchrun (N > 1) each rank runs its own replica of the step (weak
+scaling; the expert-parallel exchange is not part of this benchmark).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "decode tok/s Kimi-Linear-48B W4A16 (hot path step)"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def _args() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--group", type=int, default=128)
+    ap.add_argument("--layers", type=int, default=None, help="fewer layers (testing only)")
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true")
+    return ap.parse_args()
+
+
+def _peak_hbm() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period: float = 0.02) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.period = period
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._nvml = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = int(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = statistics.median(s[0] for s in self.samples)
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = [name for name, bit in self.REASONS.items() if seen & bit]
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle on a bounded sample of the step
+# ---------------------------------------------------------------------------
+
+
+class CpuSample:
+    """CPU tensors for one KDA+MoE layer, one MLA+MoE layer, the dense layer 0
+    and 1/8 of the lm_head rows, from the GPU model or generated on the CPU."""
+
+    LM_HEAD_FRACTION = 8
+
+    def __init__(self, batch: int, group: int, model=None, seed: int = 0) -> None:
+        from local_kimi_b200.decode import KimiLinearShape
+        from oracle import codec, synth
+
+        s = model.shape if model is not None else KimiLinearShape()
+        self.shape, self.batch, self.group = s, batch, group
+        B, H, D = batch, s.kda_heads, s.kda_head_dim
+        proj = H * D
+        if model is not None:
+            self.x = model.x0.cpu()
+            self.q, self.k, self.v = model.kda_q.cpu(), model.kda_k.cpu(), model.kda_v.cpu()
+            self.decay, self.beta = model.kda_decay.cpu(), model.kda_beta.cpu()
+            self.latent, self.attn = model.mla_latent.cpu(), model.mla_attn.cpu()
+            kl = next(lw for lw in model.layers if lw.kind == "kda" and lw.moe is not None)
+            ml = next(lw for lw in model.layers if lw.kind == "mla")
+            self.qkv = [(p.cpu(), sc.cpu()) for p, sc in kl.qkv]
+            self.kda_o = tuple(t.cpu() for t in kl.o_proj)
+            self.state = kl.kda_state.cpu()
+            self.mla_q = tuple(t.cpu() for t in ml.q_proj)
+            self.kv_b = tuple(t.cpu() for t in ml.kv_b)
+            self.mla_o = tuple(t.cpu() for t in ml.o_proj)
+            self._moe_src = {"kda": kl.moe, "mla": ml.moe}
+            l0 = model.layers[0].dense_mlp
+            self.dense = [t.cpu() for pair in l0 for t in pair]
+            rows = s.vocab_size // self.LM_HEAD_FRACTION
+            self.lm_head = (model.lm_head[0][:rows].cpu(), model.lm_head[1][:rows].cpu())
+            self.n_kda = sum(1 for lw in model.layers if lw.kind == "kda" and lw.moe is not None)
+            self.n_mla = sum(1 for lw in model.layers if lw.kind == "mla")
+        else:
+            gen = synth.generator(seed)
+            act = synth.generator(seed + 1)
+            self.x = synth.activations((B, s.hidden), act)
+            self.q = torch.nn.functional.normalize(torch.randn((B, H, D), generator=act), dim=-1)
+            self.k = torch.nn.functional.normalize(torch.randn((B, H, D), generator=act), dim=-1)
+            self.v = 0.2 * torch.randn((B, H, D), generator=act)
+            self.decay = -(0.005 + 0.075 * torch.rand((B, H, D), generator=act))
+            self.beta = torch.sigmoid(torch.randn((B, H), generator=act))
+            self.latent = synth.activations((B, s.kv_lora_rank), act)
+            self.attn = synth.activations((B, s.mla_heads * s.mla_v_head_dim), act)
+            q = lambda n, k: synth.quantised(n, k, group, gen)  # noqa: E731
+            self.qkv = [q(proj, s.hidden) for _ in range(3)]
+            self.kda_o = q(s.hidden, proj)
+            self.state = 0.05 * torch.randn((B, H, D, D), generator=gen)
+            self.mla_q = q(s.mla_heads * s.mla_q_head_dim, s.hidden)
+            self.kv_b = q(s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
+            self.mla_o = q(s.hidden, s.mla_heads * s.mla_v_head_dim)
+            self._moe_src = {"kda": None, "mla": None}
+            self._gen = gen
+            w1, w3 = q(s.dense_intermediate, s.hidden), q(s.dense_intermediate, s.hidden)
+            w2 = q(s.hidden, s.dense_intermediate)
+            self.dense = [w1[0][None], w1[1][None], w3[0][None], w3[1][None], w2[0], w2[1]]
+            self.lm_head = q(s.vocab_size // self.LM_HEAD_FRACTION, s.hidden)
+            self.n_kda = sum(1 for i in range(s.layers) if not s.is_mla(i)) - s.first_k_dense
+            self.n_mla = sum(1 for i in range(s.layers) if s.is_mla(i))
+        self.codec = codec
+
+    def moe_banks(self, kind: str, hidden: torch.Tensor):
+        """Oracle banks holding exactly the experts this hidden state routes to."""
+        from oracle import moe as omoe
+        from oracle import ops as oref
+        from oracle import synth
+
+        s = self.shape
+        m = self._moe_src[kind]
+        if m is not None:
+            router, bias = m.router_weight.cpu(), m.router_bias.cpu()
+        else:
+            router, bias = synth.weight((s.experts, s.hidden), self._gen), torch.zeros(s.experts)
+        idx, _, _ = oref.router_topk(hidden, router, bias, s.top_k,
+                                     scaling=s.routed_scaling_factor)
+        used = torch.unique(torch.cat((idx.flatten(), torch.tensor([s.experts]))))
+        dims = {0: (s.moe_intermediate, s.hidden), 1: (s.hidden, s.moe_intermediate),
+                2: (s.moe_intermediate, s.hidden)}
+        banks = []
+        for j in range(3):
+            n, k = dims[j]
+            p = torch.zeros((s.experts + 1, n, k // 2), dtype=torch.uint8)
+            sc = torch.zeros((s.experts + 1, n, k // self.group), dtype=torch.bfloat16)
+            if m is not None:
+                srcp = (m.w1_packed, m.w2_packed, m.w3_packed)[j]
+                srcs = (m.w1_scales, m.w2_scales, m.w3_scales)[j]
+                p[used] = srcp[used.to(srcp.device)].cpu()
+                sc[used] = srcs[used.to(srcs.device)].cpu()
+            else:
+                for e in used.tolist():
+                    p[e], sc[e] = synth.quantised(n, k, self.group, self._gen)
+            banks += [p, sc]
+        return omoe.MoEBanks(router, bias, *banks, s.top_k, s.routed_scaling_factor)
+
+    def seconds_per_step(self) -> tuple[float, str, int]:
+        from oracle import moe as omoe
+        from oracle import ops as oref
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        s, B = self.shape, self.batch
+        scale = s.kda_head_dim ** -0.5
+        # Routing inputs of the sampled layers (computed before timing).
+        st = self.state.clone()
+        o = oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
+        h_kda = oref.dense(o.reshape(B, -1).to(torch.bfloat16), *self.kda_o)
+        banks_kda = self.moe_banks("kda", h_kda)
+        h_mla = oref.dense(self.attn, *self.mla_o)
+        banks_mla = self.moe_banks("mla", h_mla)
+
+        t0 = time.perf_counter()
+        oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
+        st = self.state.clone()
+        o = oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
+        h = oref.dense(o.reshape(B, -1).to(torch.bfloat16), *self.kda_o)
+        omoe.moe_layer(h, banks_kda)
+        t_kda = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.mla_q)
+        oref.dense(self.latent, *self.kv_b)
+        h = oref.dense(self.attn, *self.mla_o)
+        omoe.moe_layer(h, banks_mla)
+        t_mla = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        d = self.dense
+        a = oref.swiglu(self.x, torch.zeros((B, 1), dtype=torch.long), d[0], d[1], d[2], d[3])
+        oref.dense(a.view(B, -1), d[4], d[5])
+        t_dense = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.lm_head)
+        t_head = (time.perf_counter() - t0) * self.LM_HEAD_FRACTION
+
+        total = t_kda * self.n_kda + t_mla * self.n_mla + t_dense + t_head
+        sample = (f"oracle (torch CPU, {torch.get_num_threads()} threads) on 1 KDA+MoE layer, "
+                  f"1 MLA+MoE layer, the dense layer 0 and 1/{self.LM_HEAD_FRACTION} of the "
+                  f"lm_head rows at batch {B}; per-step time extrapolated to {self.n_kda} "
+                  f"KDA+MoE + {self.n_mla} MLA+MoE layers + layer 0 + the full lm_head")
+        return total, sample, torch.get_num_threads()
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+
+def _capture(fn, x):
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(x)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = fn(x)
+    torch.cuda.synchronize()
+    return g, out
+
+
+def _time_graph(g, steps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / 1e3 / steps
+
+
+def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import __graft_entry__ as entry
+
+    entry.build()
+    from local_kimi_b200 import _lib, ops
+    from local_kimi_b200.decode import HotPathDecoder
+    from local_kimi_b200.moe import moe_forward  # noqa: F401
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    _lib.set_pdl(not args.no_pdl)
+
+    model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
+    counts = model.touched_experts(model.x0)
+    static_x = model.x0.clone()
+    graph, static_out = _capture(model.step, static_x)
+
+    # Engine-only graph: the same W4A16 projection launches with routing fixed
+    # to what the step computes, for the roofline of the projection engine.
+    routes = []
+
+    def engine_only(x):
+        i = 0
+        for lw in model.layers:
+            if lw.kind == "kda":
+                ops.w4a16_dense_multi([(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
+                h = ops.w4a16_dense(model.kda_out, *lw.o_proj)
+            else:
+                _, _, h = ops.w4a16_dense_multi([(x, *lw.q_proj), (model.mla_latent, *lw.kv_b),
+                                                (model.mla_attn, *lw.o_proj)])
+            if lw.dense_mlp is not None:
+                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+                act = ops.w4a16_swiglu(h, model.dense_idx, w1p, w1s, w3p, w3s)
+                x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
+            else:
+                stable, wts = routes[i]
+                m = lw.moe
+                act = ops.w4a16_swiglu(h, stable, m.w1_packed, m.w1_scales, m.w3_packed,
+                                       m.w3_scales)
+                x = ops.moe_down_combine(act, stable, wts, m.w2_packed, m.w2_scales)
+                i += 1
+        return ops.w4a16_dense(x, *model.lm_head)
+
+    for lw in model.layers:
+        if lw.moe is not None:
+            h = (ops.w4a16_dense(model.kda_out, *lw.o_proj) if lw.kind == "kda"
+                 else ops.w4a16_dense(model.mla_attn, *lw.o_proj))
+            routes.append(ops.moe_router(h, lw.moe.router_weight, lw.moe.router_bias,
+                                         lw.moe.top_k, routed_scaling_factor=lw.moe.scaling,
+                                         append_expert=lw.moe.num_experts))
+    eng_graph, _ = _capture(engine_only, static_x)
+
+    # Timed region: K replays of the full step.
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    step_s = start.elapsed_time(end) / 1e3 / args.steps
+    if dist is not None:
+        t = torch.tensor([step_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_s = float(t.item())
+        dist.barrier()
+
+    # End to end: pinned host input in, logits out, every step.
+    host_x = torch.empty(static_x.shape, dtype=static_x.dtype, pin_memory=True)
+    host_x.copy_(model.x0.cpu())
+    host_out = torch.empty(static_out.shape, dtype=static_out.dtype, pin_memory=True)
+    for _ in range(2):
+        static_x.copy_(host_x, non_blocking=True)
+        graph.replay()
+        host_out.copy_(static_out, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_steps = max(1, args.steps)
+    start.record()
+    for _ in range(e2e_steps):
+        static_x.copy_(host_x, non_blocking=True)
+        graph.replay()
+        host_out.copy_(static_out, non_blocking=True)
+    end.record()
+    torch.cuda.synchronize()
+    e2e_s = start.elapsed_time(end) / 1e3 / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # Roofline of the projection engine (its launches alone, same inputs).
+    eng_s = _time_graph(eng_graph, max(10, args.steps // 2), 3)
+    bytes_step = model.step_bytes(counts)
+    eng_bytes = (bytes_step["dense_proj"] + bytes_step["experts"] + bytes_step["lm_head"]
+                 + bytes_step["activations"])
+    peak, peak_src = _peak_hbm()
+    achieved = eng_bytes / eng_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_s, sample, cores = CpuSample(args.batch, args.group, model).seconds_per_step()
+        cpu = {"value": round(args.batch / cpu_s, 4), "unit": "tok/s", "cores": cores,
+               "kind": "port", "sample": sample, "seconds_per_step": round(cpu_s, 3)}
+
+    launches = model.launches_per_step
+    out = {
+        "metric": METRIC,
+        "value": round(world * args.batch / step_s, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights of the real shapes, seeded)",
+        "config": {
+            "workload": ("C4 hot path: Kimi-Linear-48B-A3B W4A16 decode step, 27 layers "
+                         "(INT4 attention projections, KDA state step, MoE router + "
+                         "experts + combine, INT4 lm_head); norms, short conv, gates, MLA "
+                         "softmax attention and BF16 projections not computed"),
+            "batch": args.batch,
+            "group_size": args.group,
+            "layers": model.nlayers,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "weights_gb": round(model.weight_bytes() / 1e9, 2),
+            "bytes_per_step": bytes_step["total"],
+            "l2": "inputs larger than L2 (each step streams ~1.8 GB of weights)",
+            "cuda_graph": True,
+            "pdl": not args.no_pdl,
+        },
+        "e2e": {"value": round(world * args.batch / e2e_s, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
+                "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None, "kernel": "w4a16_engine (all INT4 projections of a step)",
+                     "peak_source": peak_src,
+                     "bytes_per_step": eng_bytes, "ms_per_step": round(eng_s * 1e3, 4),
+                     "frac_of_step": round(eng_s / step_s, 3)},
+        "gpu_launches": launches * args.steps,
+        "launches_per_step": launches,
+        "step_bytes": bytes_step,
+        "hbm_gbs_step": round(bytes_step["total"] / step_s / 1e9, 1),
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    if dist is not None:
+        del graph, eng_graph
+        dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
+def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """The reference path restated in oracle/, on the host cores (rank 0 only)."""
+    if rank != 0:
+        return None
+    sample = CpuSample(args.batch, args.group)
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        sample.seconds_per_step()
+    steps = max(1, min(args.steps, 3))
+    times, desc, cores = [], "", 1
+    for _ in range(steps):
+        t, desc, cores = sample.seconds_per_step()
+        times.append(t)
+    step_s = statistics.median(times)
+    value = round(args.batch / step_s, 4)
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": round(step_s * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights of the real shapes, seeded)",
+        "config": {"workload": "C4 hot path decode step (see the b200 arm), CPU sample",
+                   "batch": args.batch, "group_size": args.group},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    args = _args()
+    rank, world, local_rank = _dist_env()
+    if args.impl == "reference":
+        out = run_reference(args, rank, world, local_rank)
+    else:
+        out = run_b200(args, rank, world, local_rank)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

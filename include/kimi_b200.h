@@ -163,18 +163,19 @@ KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, 
 /* choice = scores + bias; top_k by (choice desc, index asc);                  */
 /* w = scores[idx] / (sum + 1e-20) (if renormalize) * scaling.                 */
 /* hidden bf16 [T,K] (row stride h_stride); weight bf16 [E,K]; bias fp32 [E]   */
-/* (NULL = zeros); idx_out int64 [T,top_k]; w_out fp32 [T,top_k].  The         */
-/* workspace (kb_router_workspace_size bytes) follows the same rules as the    */
-/* down+combine workspace: zero before first use, reuse for the same (T,E).    */
-/* A NaN                                                                       */
-/* choice score ranks below every number, so indices stay in [0,E).            */
-/* Limits: E <= 1024, top_k <= 32.                                             */
+/* (NULL = zeros); w_out fp32 [T,top_k]; idx_out int64 [T,top_k], or           */
+/* [T,top_k+1] with append_id in the last column when append_id >= 0 (the      */
+/* shared-expert route of engine/klinear/moe.py:23-36).  The workspace         */
+/* (kb_router_workspace_size bytes) holds logits and arrival counters: zero it */
+/* before first use; every call leaves its counters at zero, so it may be      */
+/* reused for the same (T,E) without clearing.  A NaN choice ranks below every */
+/* number, so indices stay in [0,E).  Limits: E <= 1024, top_k <= 32.          */
 /* ------------------------------------------------------------------------- */
 KB_API size_t kb_router_workspace_size(int64_t T, int64_t E);
 KB_API int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t K,
                    const uint16_t* weight, const float* bias, int64_t E,
                    int64_t top_k, int renormalize, float scaling,
-                   int64_t* idx_out, float* w_out, void* workspace,
+                   int64_t* idx_out, int64_t append_id, float* w_out, void* workspace,
                    size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------- */

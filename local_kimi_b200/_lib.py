@@ -84,7 +84,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kb_router_topk": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
-         c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
+         c_float, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p],
     ),
     "kb_kda_decode_step": (
         c_int,

@@ -9,35 +9,55 @@
 // chosen experts, renormalised by (sum + 1e-20) and multiplied by the scaling
 // factor.
 //
-// Phase 1: CTA (expert block, token block) computes 8 experts x up to 8
-// tokens of logits, one warp per expert, with a fixed reduction order (each
-// lane sums its strided 8-element pieces in order, then a xor butterfly), so
-// logits are identical run to run.  Phase 2: the CTA that completes a token
-// block (arrival counter) selects the top_k for its tokens, one warp per
-// token, and resets the counter.
+// Phase 1: CTA (expert block, token block) computes 4 experts x up to 8 tokens
+// of logits, one warp per expert, with a fixed reduction order (each lane sums
+// its strided 16-byte pieces in order, then a xor butterfly), so logits are
+// identical run to run.  Phase 2: the CTA that completes a token block
+// (arrival counter, one publishing thread) selects the top_k of its tokens,
+// one warp per token, and resets the counter.  For E <= 256 every lane sorts
+// its eight candidates once with a sorting network and each pick is two
+// warp reductions (max key, then min index among the lanes holding it).
 #include "kb_common.cuh"
 
 namespace kb {
 
-constexpr int RT_WARPS = 8;      // experts per CTA
-constexpr int RT_TOK = 8;        // tokens per CTA
+constexpr int RT_WARPS = 4;  // experts per CTA
+constexpr int RT_TOK = 8;    // tokens per CTA
 
-__device__ __forceinline__ bool choice_better(float a, int ia, float b, int ib) {
-  // NaN ranks below every number; ties go to the lower index.
-  const bool an = a != a, bn = b != b;
-  if (an != bn) return bn;
-  if (!an && a != b) return a > b;
-  return ia < ib;
+// Order-preserving map of a choice score to uint32 (larger is better); NaN
+// maps to 0, below every number, and -0 is folded into +0.
+__device__ __forceinline__ uint32_t choice_key(float x) {
+  if (x != x) return 0u;
+  const uint32_t b = __float_as_uint(x + 0.0f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ bool choice_better(uint32_t ka, int ia, uint32_t kb, int ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+template <int N>
+__device__ __forceinline__ void cswap(uint32_t (&k)[N], int (&id)[N], float (&sc)[N], int i,
+                                      int j) {
+  if (choice_better(k[j], id[j], k[i], id[i])) {
+    const uint32_t tk = k[i];
+    k[i] = k[j];
+    k[j] = tk;
+    const int ti = id[i];
+    id[i] = id[j];
+    id[j] = ti;
+    const float ts = sc[i];
+    sc[i] = sc[j];
+    sc[j] = ts;
+  }
 }
 
 __global__ void __launch_bounds__(RT_WARPS * 32)
     router_kernel(const uint16_t* __restrict__ hidden, int64_t hs, int T, int K,
                   const uint16_t* __restrict__ weight, const float* __restrict__ bias, int E,
                   int top_k, int renorm, float scaling, int64_t* __restrict__ idx_out,
-                  float* __restrict__ w_out, float* __restrict__ logits,
+                  int64_t append_id, float* __restrict__ w_out, float* __restrict__ logits,
                   int* __restrict__ counters) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t* hsm = reinterpret_cast<uint16_t*>(smem);  // [RT_TOK][K]
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * RT_TOK;
@@ -47,35 +67,41 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
   pdl_wait();
   pdl_launch_dependents();
 
-  for (int e = threadIdx.x; e < nt * words; e += RT_WARPS * 32) {
-    const int m = e / words, w = e - m * words;
-    reinterpret_cast<uint4*>(hsm + (size_t)m * K)[w] =
-        *reinterpret_cast<const uint4*>(hidden + (size_t)(t0 + m) * hs + (size_t)w * 8);
-  }
-  __syncthreads();
-
   const int expert = blockIdx.x * RT_WARPS + warp;
   if (expert < E) {
     float acc[RT_TOK];
 #pragma unroll
     for (int m = 0; m < RT_TOK; ++m) acc[m] = 0.f;
     const uint16_t* wrow = weight + (size_t)expert * K;
-    for (int w = lane; w < words; w += 32) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)w * 8);
-      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+    // Eight 16-byte pieces per lane in flight at a time.
+    for (int w0 = 0; w0 < words; w0 += 32 * 8) {
+      uint4 wv[8];
 #pragma unroll
-      for (int m = 0; m < RT_TOK; ++m) {
-        if (m < nt) {
-          const uint4 hv = reinterpret_cast<const uint4*>(hsm + (size_t)m * K)[w];
-          const uint32_t hr[4] = {hv.x, hv.y, hv.z, hv.w};
+      for (int u = 0; u < 8; ++u) {
+        const int w = w0 + u * 32 + lane;
+        wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float w_lo = __uint_as_float(wr[j] << 16);
-            const float w_hi = __uint_as_float(wr[j] & 0xFFFF0000u);
-            const float h_lo = __uint_as_float(hr[j] << 16);
-            const float h_hi = __uint_as_float(hr[j] & 0xFFFF0000u);
-            acc[m] = __fmaf_rn(h_lo, w_lo, acc[m]);
-            acc[m] = __fmaf_rn(h_hi, w_hi, acc[m]);
+      for (int u = 0; u < 8; ++u) {
+        const int w = w0 + u * 32 + lane;
+        if (w < words) {
+          const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+          for (int m = 0; m < RT_TOK; ++m) {
+            if (m < nt) {
+              const uint4 hv =
+                  __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)(t0 + m) * hs) + w);
+              const uint32_t hr[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float w_lo = __uint_as_float(wr[j] << 16);
+                const float w_hi = __uint_as_float(wr[j] & 0xFFFF0000u);
+                const float h_lo = __uint_as_float(hr[j] << 16);
+                const float h_hi = __uint_as_float(hr[j] & 0xFFFF0000u);
+                acc[m] = __fmaf_rn(h_lo, w_lo, acc[m]);
+                acc[m] = __fmaf_rn(h_hi, w_hi, acc[m]);
+              }
+            }
           }
         }
       }
@@ -89,67 +115,139 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
   }
 
   // Arrival: the last expert block of this token block runs the selection.
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const int old = atomicAdd(&counters[blockIdx.y], 1);
     s_last = (old == (int)gridDim.x - 1);
+    if (s_last) __threadfence();
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
 
   for (int m = warp; m < nt; m += RT_WARPS) {
     const int tok = t0 + m;
     const float* lrow = logits + (size_t)tok * E;
-    // Selection by repeated warp argmax over (choice desc, index asc).
-    unsigned taken_mask_local = 0;  // bit j: expert lane + 32*j already taken
-    float wsum = 0.f;
-    float picked_score[32];
-    int picked_idx[32];
-    for (int sel = 0; sel < top_k; ++sel) {
-      float best = 0.f;
-      int bidx = 0x7fffffff;
-      bool have = false;
-      for (int j = 0; lane + 32 * j < E; ++j) {
-        const int e = lane + 32 * j;
-        if (taken_mask_local & (1u << j)) continue;
-        const float lg = __ldcg(&lrow[e]);
-        const float sc = 1.0f / (1.0f + expf(-lg));
-        const float ch = sc + (bias ? bias[e] : 0.f);
-        if (!have || choice_better(ch, e, best, bidx)) {
-          best = ch;
-          bidx = e;
-          have = true;
-        }
-      }
+    float my_score = 0.f, wsum = 0.f;
+    int my_idx = 0;
+    if (E <= 256) {
+      uint32_t key[8];
+      int id[8];
+      float sc[8];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-        const int oh = __shfl_xor_sync(0xffffffffu, (int)have, o);
-        if (oh && (!have || choice_better(ob, oi, best, bidx))) {
-          best = ob;
-          bidx = oi;
-          have = true;
+      for (int j = 0; j < 8; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) {
+          const float lg = __ldcg(&lrow[e]);
+          sc[j] = 1.0f / (1.0f + expf(-lg));
+          key[j] = choice_key(sc[j] + (bias ? bias[e] : 0.f));
+          id[j] = e;
+        } else {
+          sc[j] = 0.f;
+          key[j] = 0u;
+          id[j] = 0x7fffffff;
         }
       }
-      if ((bidx & 31) == lane) taken_mask_local |= 1u << (bidx >> 5);
-      const float lg = __ldcg(&lrow[bidx]);
-      const float sc = 1.0f / (1.0f + expf(-lg));
-      picked_score[sel] = sc;
-      picked_idx[sel] = bidx;
-    }
-    for (int sel = 0; sel < top_k; ++sel) wsum += picked_score[sel];
-    const float denom = wsum + 1e-20f;
-    if (lane == 0) {
+      // Sort descending by (key, -index): optimal 19-comparator network.
+      cswap(key, id, sc, 0, 2);
+      cswap(key, id, sc, 1, 3);
+      cswap(key, id, sc, 4, 6);
+      cswap(key, id, sc, 5, 7);
+      cswap(key, id, sc, 0, 4);
+      cswap(key, id, sc, 1, 5);
+      cswap(key, id, sc, 2, 6);
+      cswap(key, id, sc, 3, 7);
+      cswap(key, id, sc, 0, 1);
+      cswap(key, id, sc, 2, 3);
+      cswap(key, id, sc, 4, 5);
+      cswap(key, id, sc, 6, 7);
+      cswap(key, id, sc, 2, 4);
+      cswap(key, id, sc, 3, 5);
+      cswap(key, id, sc, 1, 4);
+      cswap(key, id, sc, 3, 6);
+      cswap(key, id, sc, 1, 2);
+      cswap(key, id, sc, 3, 4);
+      cswap(key, id, sc, 5, 6);
       for (int sel = 0; sel < top_k; ++sel) {
-        float wv = picked_score[sel];
-        if (renorm && top_k > 1) wv = wv / denom;
-        idx_out[(size_t)tok * top_k + sel] = picked_idx[sel];
-        w_out[(size_t)tok * top_k + sel] = wv * scaling;
+        const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+        const uint32_t cand = (key[0] == best) ? (uint32_t)id[0] : 0xffffffffu;
+        const int win = (int)__reduce_min_sync(0xffffffffu, cand);
+        float s = 0.f;
+        if (id[0] == win) {
+          s = sc[0];
+#pragma unroll
+          for (int j = 0; j < 7; ++j) {
+            key[j] = key[j + 1];
+            id[j] = id[j + 1];
+            sc[j] = sc[j + 1];
+          }
+          key[7] = 0u;
+          id[7] = 0x7fffffff;
+          sc[7] = 0.f;
+        }
+        s = __shfl_sync(0xffffffffu, s, win & 31);
+        wsum += s;
+        if (lane == sel) {
+          my_score = s;
+          my_idx = win;
+        }
+      }
+    } else {
+      // General E <= 1024: repeated warp argmax over register-held scores.
+      float score[32];
+      uint32_t key[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) {
+          const float lg = __ldcg(&lrow[e]);
+          score[j] = 1.0f / (1.0f + expf(-lg));
+          key[j] = choice_key(score[j] + (bias ? bias[e] : 0.f));
+        } else {
+          score[j] = 0.f;
+          key[j] = 0u;
+        }
+      }
+      unsigned taken = 0;
+      for (int sel = 0; sel < top_k; ++sel) {
+        uint32_t bk = 0u;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int e = lane + 32 * j;
+          if (e < E && !(taken & (1u << j)) && choice_better(key[j], e, bk, bi)) {
+            bk = key[j];
+            bi = e;
+          }
+        }
+        const uint32_t best = __reduce_max_sync(0xffffffffu, bk);
+        const int win =
+            (int)__reduce_min_sync(0xffffffffu, (bk == best) ? (uint32_t)bi : 0xffffffffu);
+        float s = 0.f;
+        if ((win & 31) == lane) {
+          const int jw = win >> 5;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j == jw) s = score[j];
+          taken |= 1u << jw;
+        }
+        s = __shfl_sync(0xffffffffu, s, win & 31);
+        wsum += s;
+        if (lane == sel) {
+          my_score = s;
+          my_idx = win;
+        }
       }
     }
+    const float denom = wsum + 1e-20f;
+    const int istride = top_k + (append_id >= 0 ? 1 : 0);
+    if (lane < top_k) {
+      float wv = my_score;
+      if (renorm && top_k > 1) wv = wv / denom;
+      idx_out[(size_t)tok * istride + lane] = my_idx;
+      w_out[(size_t)tok * top_k + lane] = wv * scaling;
+    }
+    if (append_id >= 0 && lane == 0) idx_out[(size_t)tok * istride + top_k] = append_id;
   }
   __syncthreads();
   if (threadIdx.x == 0) counters[blockIdx.y] = 0;
@@ -167,15 +265,15 @@ extern "C" size_t kb_router_workspace_size(int64_t T, int64_t E) {
 extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t K,
                               const uint16_t* weight, const float* bias, int64_t E,
                               int64_t top_k, int renormalize, float scaling, int64_t* idx_out,
-                              float* w_out, void* workspace, size_t workspace_bytes,
-                              void* stream) {
+                              int64_t append_id, float* w_out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
   kb::clear_error();
   KB_REQUIRE(T >= 0 && K > 0 && E > 0 && top_k > 0, KB_ERR_BAD_SHAPE,
              "router needs T >= 0 and K, E, top_k > 0");
   KB_REQUIRE(top_k <= E, KB_ERR_BAD_SHAPE, "top_k %lld exceeds E %lld", (long long)top_k,
              (long long)E);
-  KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 8192 && K % 8 == 0, KB_ERR_UNSUPPORTED,
-             "router supports E <= 1024, top_k <= 32, K <= 8192 with K %% 8 == 0");
+  KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 65536 && K % 8 == 0, KB_ERR_UNSUPPORTED,
+             "router supports E <= 1024, top_k <= 32, K <= 65536 with K %% 8 == 0");
   if (T == 0) return KB_OK;
   KB_REQUIRE(hidden && weight && idx_out && w_out, KB_ERR_NULL_POINTER, "NULL router pointer");
   KB_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0 && h_stride % 8 == 0 &&
@@ -188,16 +286,9 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
   float* logits = reinterpret_cast<float*>(workspace);
   const size_t lbytes = ((size_t)T * E * sizeof(float) + 255) / 256 * 256;
   int* counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + lbytes);
-  const size_t smem = (size_t)kb::RT_TOK * K * sizeof(uint16_t);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(kb::router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)(kb::RT_TOK * 8192 * sizeof(uint16_t)));
-    attr_done = true;
-  }
   const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
                   (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
-  return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,
+  return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), 0, stream, hidden,
                     h_stride, (int)T, (int)K, weight, bias, (int)E, (int)top_k, renormalize,
-                    scaling, idx_out, w_out, logits, counters);
+                    scaling, idx_out, append_id, w_out, logits, counters);
 }

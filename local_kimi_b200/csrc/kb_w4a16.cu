@@ -3,19 +3,29 @@
 // One persistent kernel serves every INT4-weight projection of the decode hot
 // path: dense (w4a16_dense, fused QKV), expert-grouped (w4a16_grouped), fused
 // gate/up + SwiGLU (w4a16_swiglu) and down projection + weighted combine
-// (fused_w2_combine).  Work is split into items; an item is a group of 16-row
-// blocks of one weight matrix (or of the w1/w3 pair) over the full reduction
-// axis, for up to 8*NSUB tokens that use that matrix.
+// (fused_w2_combine).  Work is split into items: an item is RBc 16-row blocks
+// of one weight matrix (or of the w1/w3 pair) over the full reduction axis,
+// for all tokens that use that matrix.
 //
-// Inside an item each warp owns one 16-row block and one slice of the
-// reduction axis.  A lane streams 16-byte pieces of packed codes for two rows
-// straight from HBM (ld.global.nc, L1 bypass), decodes them in registers to
-// bf16(code * scale) with bf16x2 arithmetic (decode_word), and feeds the
-// tensor core through mma.m16n8k16 with the weights as the 16x16 A operand
-// and up to 8 tokens of activations (staged once per item in shared memory in
-// decode pair order) as the B operand, accumulating in fp32.  Slices of the
-// reduction axis are summed in a fixed order through shared memory, so every
-// output is deterministic run to run.
+// Data movement.  A producer warp streams each item's packed codes (one
+// cp.async.bulk per weight row, L2 evict-first) and its bf16 scales (one bulk
+// copy per matrix and item) from HBM into a ring of shared-memory stages
+// guarded by mbarriers (full: transaction bytes; empty: one arrival per
+// consumer warp).  Rows land with a padded stride (K/2 + pad, the pad making
+// the stride 64 mod 128 bytes) so the consumers' 16-byte fragment loads are
+// bank-conflict free.  For dense problems the producer starts streaming before
+// the programmatic-dependent-launch wait: no kernel of this library that lets
+// its successor start early writes packed weights or scales, so their fetch
+// overlaps the tail of the kernel in front.
+//
+// Compute.  Eight consumer warps each own one 16-row block and one slice of
+// the reduction axis of the item.  A lane decodes 16-byte pieces of two rows
+// to bf16(code * scale) with bf16x2 arithmetic (decode_word) and feeds the
+// tensor core through mma.m16n8k16: weights are the 16x16 A operand, eight
+// tokens of activations (staged in shared memory in decode pair order) are the
+// B operand, fp32 accumulation in two independent accumulator sets.
+// Reduction-axis slices are summed in a fixed order through shared memory, so
+// every output is deterministic run to run.
 //
 // Reference semantics (engine/kernels/w4a16_gemv.py:56-174, :224-392,
 // engine/kernels/moe_combine.py:209-261): decoded weight bf16(code*scale),
@@ -29,12 +39,17 @@
 
 namespace kb {
 
-constexpr int NW = 8;               // warps per CTA
-constexpr int NTHREADS = NW * 32;
-constexpr int KCH = 4;              // 128-wide reduction blocks loaded per batch
-constexpr int MAX_SMEM = 200 * 1024;
+constexpr int NCW = 16;                 // consumer warps
+constexpr int NCT = NCW * 32;           // consumer threads
+constexpr int NTHREADS = NCT + 32;      // + one producer warp
+constexpr int MAX_SMEM = 225 * 1024;
+constexpr int MAX_STAGES = 6;
+constexpr int X_RESIDENT_BUDGET = 64 * 1024;  // bytes of activations kept resident
+constexpr int CBAR = 1;                 // named barrier id of the consumer warps
+constexpr int SMEM_RESERVE = 2048;      // static shared memory and barriers
 
 enum : int { MODE_DENSE = 0, MODE_GROUPED = 1, MODE_SWIGLU = 2, MODE_W2C = 3 };
+enum : uint32_t { ERR_INDEX = 1u, ERR_TIMEOUT = 2u };
 
 struct DenseProb {
   const uint16_t* x;
@@ -44,8 +59,9 @@ struct DenseProb {
   uint16_t* y;
   int64_t ys;
   int M, K, N, gshift;
-  int KS, RBc, items_rb, tok_groups;
+  int KS, RBc, items;
   int item_begin;
+  int x_off;  // resident activations: byte offset of token 0 (-1: streamed per group)
 };
 
 struct GroupedArgs {
@@ -65,30 +81,246 @@ struct GroupedArgs {
   int* counters;
   int T, R, K, N, E, gshift;
   int KS, RBc, items_rb;
+  int x_rows;  // resident activation rows (T, or T*R for W2C); 0: streamed per group
 };
 
 struct EngineParams {
   int mode;
-  int tok_cap;
-  int tstride;
-  int red_off;
-  int plan_off;
-  int total_items;
+  int tok_cap;      // tokens per compute group (8 * NSUB)
+  int tstride;      // bytes per staged token row
+  int x_bytes;      // bytes of the activation region
+  int stage_bytes;  // bytes per ring stage
+  int stages;
+  int ring_off, red_off, plan_off, bar_off;
+  int total_items;  // dense
   int nprob;
   uint32_t* err;
   DenseProb prob[KB_MAX_DENSE_PROBLEMS];
   GroupedArgs g;
 };
 
-// ---------------------------------------------------------------------------
-// Device side.
-// ---------------------------------------------------------------------------
+// Description of one item, computed identically by producer and consumers.
+struct Item {
+  const uint8_t* w[2];
+  const uint16_t* s[2];
+  int mats;
+  int K, N, gshift, KS, RBc;
+  int r0;           // first row of the item
+  int rows;         // valid rows (<= RBc*16)
+  int RS;           // padded shared-memory row stride in bytes
+  int ng;           // scale groups per row
+  bool scale_bulk;  // scales copied into the stage (else read from global memory)
+  int p;            // dense problem index or grouped slot
+  int abase, count; // grouped: assignment range; dense: 0, M
+};
 
-// Stage one activation row (K bf16, 16-byte aligned) into shared memory in the
-// layout the B fragments read: token row m, word j of chunk c at byte offset
-// m*tstride + (j*NC + c)*16, each word in pair order (x0,x4),(x1,x5),...
-__device__ __forceinline__ void stage_row(uint8_t* xs_row, const uint16_t* src, int K,
-                                          int first, int step) {
+__host__ __device__ __forceinline__ int row_stride_bytes(int K) {
+  const int b = K / 2;
+  return b + ((64 - (b % 128)) + 128) % 128;
+}
+
+__device__ __forceinline__ bool scale_bulk_ok(const uint16_t* s, int r0, int rows, int ng) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(s + (size_t)r0 * ng);
+  const uint32_t bytes = (uint32_t)rows * ng * 2;
+  return (a % 16 == 0) && (bytes % 16 == 0);
+}
+
+__device__ __forceinline__ void describe_dense(const EngineParams& P, int item, Item& it) {
+  int p = 0;
+  while (p + 1 < P.nprob && item >= P.prob[p + 1].item_begin) ++p;
+  const DenseProb& D = P.prob[p];
+  const int rbg = item - D.item_begin;
+  it.mats = 1;
+  it.w[0] = D.w;
+  it.s[0] = D.s;
+  it.w[1] = nullptr;
+  it.s[1] = nullptr;
+  it.K = D.K;
+  it.N = D.N;
+  it.gshift = D.gshift;
+  it.KS = D.KS;
+  it.RBc = D.RBc;
+  it.r0 = rbg * D.RBc * 16;
+  it.rows = min(D.RBc * 16, D.N - it.r0);
+  it.RS = row_stride_bytes(D.K);
+  it.ng = D.K >> (5 + D.gshift);
+  it.scale_bulk = scale_bulk_ok(D.s, it.r0, it.rows, it.ng);
+  it.p = p;
+  it.abase = 0;
+  it.count = D.M;
+}
+
+__device__ __forceinline__ void describe_grouped(const EngineParams& P, int item,
+                                                 const int* slot_expert, const int* slot_start,
+                                                 Item& it) {
+  const GroupedArgs& G = P.g;
+  const int slot = item / G.items_rb;
+  const int rbg = item - slot * G.items_rb;
+  const int e = slot_expert[slot];
+  it.mats = (P.mode == MODE_SWIGLU) ? 2 : 1;
+  it.w[0] = G.w0 + (size_t)e * (size_t)G.wse;
+  it.s[0] = G.s0 + (size_t)e * (size_t)G.sse;
+  it.w[1] = (it.mats == 2) ? G.w1 + (size_t)e * (size_t)G.wse : nullptr;
+  it.s[1] = (it.mats == 2) ? G.s1 + (size_t)e * (size_t)G.sse : nullptr;
+  it.K = G.K;
+  it.N = G.N;
+  it.gshift = G.gshift;
+  it.KS = G.KS;
+  it.RBc = G.RBc;
+  it.r0 = rbg * G.RBc * 16;
+  it.rows = min(G.RBc * 16, G.N - it.r0);
+  it.RS = row_stride_bytes(G.K);
+  it.ng = G.K >> (5 + G.gshift);
+  it.scale_bulk = scale_bulk_ok(it.s[0], it.r0, it.rows, it.ng) &&
+                  (it.mats == 1 || scale_bulk_ok(it.s[1], it.r0, it.rows, it.ng));
+  it.p = slot;
+  it.abase = slot_start[slot];
+  it.count = slot_start[slot + 1] - it.abase;
+}
+
+// Stage layout of an item: mats x RBc*16 weight rows of RS bytes, then one
+// 16-byte-padded block of scale rows per matrix.
+__device__ __forceinline__ int stage_scale_offset(const Item& it) {
+  return it.mats * it.RBc * 16 * it.RS;
+}
+__device__ __forceinline__ int stage_scale_stride(const Item& it) {
+  return (it.RBc * 16 * it.ng * 2 + 15) / 16 * 16;
+}
+
+// ---------------------------------------------------------------------------
+// Producer: stream one item into a ring stage.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void produce_item(const Item& it, uint8_t* stage, uint64_t* full,
+                                             uint64_t policy) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t wbytes = (uint32_t)(it.K / 2);
+  const uint32_t sbytes = (uint32_t)it.rows * it.ng * 2;
+  uint32_t total = (uint32_t)it.mats * it.rows * wbytes;
+  if (it.scale_bulk) total += (uint32_t)it.mats * sbytes;
+  if (lane == 0) mbar_arrive_expect_tx(full, total);
+  __syncwarp();
+  const int nrows = it.mats * it.rows;
+  for (int i = lane; i < nrows; i += 32) {
+    const int m = i / it.rows, r = i - m * it.rows;
+    const uint8_t* wm = m ? it.w[1] : it.w[0];
+    bulk_g2s(stage + (m * it.RBc * 16 + r) * it.RS, wm + (size_t)(it.r0 + r) * wbytes, wbytes,
+             full, policy);
+  }
+  if (it.scale_bulk && lane < it.mats) {
+    const uint16_t* sm = lane ? it.s[1] : it.s[0];
+    bulk_g2s(stage + stage_scale_offset(it) + lane * stage_scale_stride(it),
+             sm + (size_t)it.r0 * it.ng, sbytes, full, policy);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumer: one 16-row block x one reduction slice of a staged item.
+// ---------------------------------------------------------------------------
+// One 128-wide reduction block for this lane: 16-byte pieces of rows g (WA)
+// and g+8 (WB), their replicated scales, and the activation words at px[p]
+// (token slot 8p+g; word j of the chunk at px[p] + j*NC16).
+template <int NSUB>
+__device__ __forceinline__ void kblock_mma(uint4 WA, uint4 WB, uint32_t sa2, uint32_t sb2,
+                                           const uint8_t* const (&px)[NSUB], int NC16, int nact,
+                                           float (&acc)[NSUB][4], float (&acc2)[NSUB][4]) {
+  const uint32_t wa[4] = {WA.x, WA.y, WA.z, WA.w};
+  const uint32_t wb[4] = {WB.x, WB.y, WB.z, WB.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+    decode_word(wa[j], sa2, a0, a1, a2, a3);
+    decode_word(wb[j], sb2, b0, b1, b2, b3);
+#pragma unroll
+    for (int p = 0; p < NSUB; ++p) {
+      if (NSUB == 1 || p < nact) {
+        const uint4 xv = lds_v4(px[p] + j * NC16);
+        if (j & 1) {
+          mma_bf16_16816(acc2[p], a0, b0, a1, b1, xv.x, xv.y);
+          mma_bf16_16816(acc2[p], a2, b2, a3, b3, xv.z, xv.w);
+        } else {
+          mma_bf16_16816(acc[p], a0, b0, a1, b1, xv.x, xv.y);
+          mma_bf16_16816(acc[p], a2, b2, a3, b3, xv.z, xv.w);
+        }
+      }
+    }
+  }
+}
+
+// xrow[p]: this lane's activation row for token slot 8p + g (shared memory).
+// srow: scale rows of this row block (shared or global memory, generic loads).
+// D fragment: acc[p][0] = (row g, token 2t), [1] = (row g, token 2t+1),
+// [2] = (row g+8, token 2t), [3] = (row g+8, token 2t+1).
+template <int NSUB>
+__device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
+                                                 const uint16_t* srow, int ng, int rows_valid,
+                                                 int K, int gshift, int kb0, int kb1,
+                                                 const uint8_t* (&xrow)[NSUB], int nact,
+                                                 float (&acc)[NSUB][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int NC = K >> 5;
+  const int NC16 = NC * 16;
+  const int rowA = min(g, rows_valid - 1);
+  const int rowB = min(g + 8, rows_valid - 1);
+  const uint16_t* sA = srow + rowA * ng;
+  const uint16_t* sB = srow + rowB * ng;
+  float acc2[NSUB][4];
+#pragma unroll
+  for (int p = 0; p < NSUB; ++p)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc2[p][i] = 0.f;
+  // Full 128-wide blocks first (every chunk of the block exists), then the
+  // partial block at the end of the reduction axis when K % 128 != 0.
+  const int kbf = min(kb1, NC >> 2);
+  int c = kb0 * 4 + t;
+  const uint8_t* pa = wtile + rowA * RS + c * 16;
+  const uint8_t* pb = wtile + rowB * RS + c * 16;
+  const uint8_t* px[NSUB];
+#pragma unroll
+  for (int p = 0; p < NSUB; ++p) px[p] = xrow[p] + c * 16;
+#pragma unroll 1
+  for (int kb = kb0; kb < kbf; ++kb) {
+    const uint4 WA = lds_v4(pa);
+    const uint4 WB = lds_v4(pb);
+    const uint32_t sa = sA[c >> gshift];
+    const uint32_t sb = sB[c >> gshift];
+    kblock_mma<NSUB>(WA, WB, prmt(sa, 0, 0x1010), prmt(sb, 0, 0x1010), px, NC16, nact, acc,
+                     acc2);
+    pa += 64;
+    pb += 64;
+    c += 4;
+#pragma unroll
+    for (int p = 0; p < NSUB; ++p) px[p] += 64;
+  }
+  if (kbf < kb1) {
+    // Partial block: chunks at or past NC contribute zero weights.
+    const bool valid = c < NC;
+    const int cc = valid ? c : NC - 1;
+    const int back = (c - cc) * 16;
+    uint4 WA = lds_v4(pa - back);
+    uint4 WB = lds_v4(pb - back);
+    if (!valid) {
+      WA = make_uint4(0, 0, 0, 0);
+      WB = make_uint4(0, 0, 0, 0);
+    }
+    const uint32_t sa = sA[cc >> gshift];
+    const uint32_t sb = sB[cc >> gshift];
+    const uint8_t* pxc[NSUB];
+#pragma unroll
+    for (int p = 0; p < NSUB; ++p) pxc[p] = px[p] - back;
+    kblock_mma<NSUB>(WA, WB, prmt(sa, 0, 0x1010), prmt(sb, 0, 0x1010), pxc, NC16, nact, acc,
+                     acc2);
+  }
+#pragma unroll
+  for (int p = 0; p < NSUB; ++p)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[p][i] += acc2[p][i];
+}
+
+// Stage one activation row (K bf16, 16-byte aligned) into shared memory in
+// the layout the B fragments read: word j of chunk c at (j*NC + c)*16, each
+// word in pair order (x0,x4),(x1,x5),(x2,x6),(x3,x7).
+__device__ __forceinline__ void stage_row(uint8_t* xs_row, const uint16_t* src, int K, int first,
+                                          int step) {
   const int NC = K >> 5;
   const int words = K >> 3;
   for (int w = first; w < words; w += step) {
@@ -98,78 +330,9 @@ __device__ __forceinline__ void stage_row(uint8_t* xs_row, const uint16_t* src, 
   }
 }
 
-// Accumulate the 16-row block [r0, r0+16) of matrix (w, s) over reduction
-// blocks [kb0, kb1) into acc[p] for token sub-pass p (tokens 8p..8p+7).
-// D fragment: acc[p][0] = (row g, token 2t), [1] = (row g, token 2t+1),
-// [2] = (row g+8, token 2t), [3] = (row g+8, token 2t+1).
-template <int NSUB>
-__device__ __forceinline__ void rowblock_mma(const uint8_t* __restrict__ w,
-                                             const uint16_t* __restrict__ s, int N, int K,
-                                             int gshift, int r0, int kb0, int kb1,
-                                             const uint8_t* xs, int tstride, int ntok,
-                                             float (&acc)[NSUB][4]) {
-  const int nact = (ntok + 7) >> 3;  // sub-passes holding at least one token
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int NC = K >> 5;
-  const int rowA = min(r0 + g, N - 1);
-  const int rowB = min(r0 + g + 8, N - 1);
-  const uint8_t* wA = w + (size_t)rowA * (size_t)(K >> 1);
-  const uint8_t* wB = w + (size_t)rowB * (size_t)(K >> 1);
-  const int ng = K >> (5 + gshift);
-  const uint16_t* sA = s + (size_t)rowA * ng;
-  const uint16_t* sB = s + (size_t)rowB * ng;
-  const uint8_t* xrow[NSUB];
-#pragma unroll
-  for (int p = 0; p < NSUB; ++p) xrow[p] = xs + min(p * 8 + g, ntok - 1) * tstride;
-
-  for (int kb = kb0; kb < kb1; kb += KCH) {
-    uint4 WA[KCH], WB[KCH];
-    uint32_t SA[KCH], SB[KCH];
-#pragma unroll
-    for (int i = 0; i < KCH; ++i) {
-      const int c = (kb + i) * 4 + t;
-      if (kb + i < kb1 && c < NC) {
-        WA[i] = ldg_stream_v4(wA + (size_t)c * 16);
-        WB[i] = ldg_stream_v4(wB + (size_t)c * 16);
-        SA[i] = ldg_u16(sA + (c >> gshift));
-        SB[i] = ldg_u16(sB + (c >> gshift));
-      } else {
-        WA[i] = make_uint4(0, 0, 0, 0);
-        WB[i] = make_uint4(0, 0, 0, 0);
-        SA[i] = 0;
-        SB[i] = 0;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < KCH; ++i) {
-      if (kb + i < kb1) {
-        const int c = min((kb + i) * 4 + t, NC - 1);
-        const uint32_t sa2 = SA[i] | (SA[i] << 16);
-        const uint32_t sb2 = SB[i] | (SB[i] << 16);
-        const uint32_t wa[4] = {WA[i].x, WA[i].y, WA[i].z, WA[i].w};
-        const uint32_t wb[4] = {WB[i].x, WB[i].y, WB[i].z, WB[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          decode_word(wa[j], sa2, a0, a1, a2, a3);
-          decode_word(wb[j], sb2, b0, b1, b2, b3);
-#pragma unroll
-          for (int p = 0; p < NSUB; ++p) {
-            if (p < nact) {
-              const uint4 xv = lds_v4(xrow[p] + (j * NC + c) * 16);
-              mma_bf16_16816(acc[p], a0, b0, a1, b1, xv.x, xv.y);
-              mma_bf16_16816(acc[p], a2, b2, a3, b3, xv.z, xv.w);
-            }
-          }
-        }
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ int clamp_expert(int64_t v, int E, uint32_t* err) {
   if (v < 0 || v >= E) {
-    atomicOr(err, 1u);
+    atomicOr(err, ERR_INDEX);
     return 0;
   }
   return static_cast<int>(v);
@@ -183,74 +346,10 @@ __device__ __forceinline__ float swiglu_contract(float gate, float up) {
   return sl * u;
 }
 
-template <int NSUB>
-__device__ void dense_loop(const EngineParams& P, uint8_t* xs, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  int staged_p = -1, staged_gb = -1;
-  for (int item = blockIdx.x; item < P.total_items; item += gridDim.x) {
-    int p = 0;
-    while (p + 1 < P.nprob && item >= P.prob[p + 1].item_begin) ++p;
-    const DenseProb& D = P.prob[p];
-    const int local = item - D.item_begin;
-    const int gb = local / D.items_rb;
-    const int rbg = local - gb * D.items_rb;
-    const int tok0 = gb * P.tok_cap;
-    const int ntok = min(P.tok_cap, D.M - tok0);
-    if (p != staged_p || gb != staged_gb) {
-      __syncthreads();
-      for (int m = 0; m < ntok; ++m)
-        stage_row(xs + m * P.tstride, D.x + (size_t)(tok0 + m) * D.xs, D.K, threadIdx.x,
-                  NTHREADS);
-      __syncthreads();
-      staged_p = p;
-      staged_gb = gb;
-    }
-    const int ks = warp % D.KS;
-    const int rb = warp / D.KS;
-    const int KB = (D.K + 127) >> 7;
-    const int kb0 = KB * ks / D.KS, kb1 = KB * (ks + 1) / D.KS;
-    const int r0 = (rbg * D.RBc + rb) * 16;
-    float acc[NSUB][4];
-#pragma unroll
-    for (int q = 0; q < NSUB; ++q)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[q][i] = 0.f;
-    if (r0 < D.N)
-      rowblock_mma<NSUB>(D.w, D.s, D.N, D.K, D.gshift, r0, kb0, kb1, xs, P.tstride, ntok, acc);
-#pragma unroll
-    for (int q = 0; q < NSUB; ++q)
-      *reinterpret_cast<float4*>(red + ((warp * NSUB + q) * 32 + lane) * 4) =
-          make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
-    __syncthreads();
-    if (ks == 0 && r0 < D.N) {
-#pragma unroll
-      for (int q = 0; q < NSUB; ++q) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k2 = 0; k2 < D.KS; ++k2) {
-          const float4 pv =
-              *reinterpret_cast<const float4*>(red + (((warp + k2) * NSUB + q) * 32 + lane) * 4);
-          v[0] += pv.x;
-          v[1] += pv.y;
-          v[2] += pv.z;
-          v[3] += pv.w;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = r0 + g + ((i >> 1) << 3);
-          const int tok = q * 8 + 2 * t + (i & 1);
-          if (row < D.N && tok < ntok)
-            D.y[(size_t)(tok0 + tok) * D.ys + row] = float_to_bf16_bits(v[i]);
-        }
-      }
-    }
-    __syncthreads();
-  }
-}
-
-// Build the expert-major assignment plan in shared memory: the used experts in
+// Build the expert-major assignment plan in shared memory: used experts in
 // ascending order (slot_expert), the start of each slot's assignments
-// (slot_start) and the assignment ids ordered by (expert, id) (assign).
+// (slot_start) and assignment ids ordered by (expert, id) (assign).  All
+// NTHREADS threads take part.
 __device__ int build_plan(const GroupedArgs& G, uint32_t* err, int* cnt, int* slot_expert,
                           int* slot_start, int* assign) {
   __shared__ int s_nslots;
@@ -265,27 +364,39 @@ __device__ int build_plan(const GroupedArgs& G, uint32_t* err, int* cnt, int* sl
   }
   __syncthreads();
   if (warp == 0) {
-    int running = 0, nslots = 0;
-    for (int base = 0; base < E; base += 32) {
-      const int e = base + lane;
-      const int c = (e < E) ? cnt[e] : 0;
-      int incl = c;
+    // Each lane scans a contiguous run of experts; one warp-wide scan joins
+    // the runs, so the pass over E experts takes ceil(E/32) steps per lane.
+    const int per = (E + 31) / 32;
+    const int e0 = lane * per, e1 = min(E, e0 + per);
+    int tot = 0, used_cnt = 0;
+    for (int e = e0; e < e1; ++e) {
+      const int c = cnt[e];
+      tot += c;
+      used_cnt += (c > 0);
+    }
+    int incl = tot, uincl = used_cnt;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      const int un = __shfl_up_sync(0xffffffffu, uincl, o);
+      if (lane >= o) {
+        incl += n;
+        uincl += un;
       }
-      const int excl = running + incl - c;
-      const unsigned used = __ballot_sync(0xffffffffu, c > 0);
-      const int rank = nslots + __popc(used & ((1u << lane) - 1u));
+    }
+    int running = incl - tot, rank = uincl - used_cnt;
+    for (int e = e0; e < e1; ++e) {
+      const int c = cnt[e];
       if (c > 0) {
         slot_expert[rank] = e;
-        slot_start[rank] = excl;
+        slot_start[rank] = running;
+        ++rank;
       }
-      if (e < E) cnt[e] = excl;
-      running += __shfl_sync(0xffffffffu, incl, 31);
-      nslots += __popc(used);
+      cnt[e] = running;
+      running += c;
     }
+    const int nslots = __shfl_sync(0xffffffffu, uincl, 31);
+    running = __shfl_sync(0xffffffffu, incl, 31);
     if (lane == 0) {
       slot_start[nslots] = running;
       s_nslots = nslots;
@@ -315,77 +426,206 @@ __device__ int build_plan(const GroupedArgs& G, uint32_t* err, int* cnt, int* sl
   return s_nslots;
 }
 
+// Global source row of the activations of token slot m of an item.
+__device__ __forceinline__ const uint16_t* token_src(const EngineParams& P, const Item& it,
+                                                     const int* assign, int m) {
+  if (P.mode == MODE_DENSE) {
+    const DenseProb& D = P.prob[it.p];
+    return D.x + (size_t)m * D.xs;
+  }
+  const int a = assign[it.abase + m];
+  return (P.mode == MODE_W2C) ? P.g.x + (size_t)a * P.g.xs
+                              : P.g.x + (size_t)(a / P.g.R) * P.g.xs;
+}
+
+// Byte offset of token slot m's row inside the resident activation region.
+__device__ __forceinline__ int resident_off(const EngineParams& P, const Item& it,
+                                            const int* assign, int m) {
+  if (P.mode == MODE_DENSE) return P.prob[it.p].x_off + m * P.tstride;
+  const int a = assign[it.abase + m];
+  return ((P.mode == MODE_W2C) ? a : a / P.g.R) * P.tstride;
+}
+
 template <int NSUB>
-__device__ void grouped_loop(const EngineParams& P, uint8_t* xs, float* red, uint8_t* plan) {
-  const GroupedArgs& G = P.g;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  int* cnt = reinterpret_cast<int*>(plan);
-  int* slot_expert = cnt + (G.E + 1);
-  int* slot_start = slot_expert + G.E;
-  int* assign = slot_start + (G.E + 1);
+__global__ void __launch_bounds__(NTHREADS, 1)
+    w4a16_engine(const __grid_constant__ EngineParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_done[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool producer = warp == NCW;
+  uint8_t* xs = smem;
+  uint8_t* ring = smem + P.ring_off;
+  float* red = reinterpret_cast<float*>(smem + P.red_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bar_off);
+  uint64_t* empty = full + P.stages;
+  int* cnt = reinterpret_cast<int*>(smem + P.plan_off);
 
-  const int nslots = build_plan(G, P.err, cnt, slot_expert, slot_start, assign);
-  const int mats = (P.mode == MODE_SWIGLU) ? 2 : 1;
-  const int per_mat = G.RBc * G.KS;
-  const int mat = warp / per_mat;
-  const int rem = warp - mat * per_mat;
-  const int rb = rem / G.KS;
-  const int ks = rem - rb * G.KS;
-  const int KB = (G.K + 127) >> 7;
-  const int kb0 = KB * ks / G.KS, kb1 = KB * (ks + 1) / G.KS;
-  const int nitems = nslots * G.items_rb;
-  (void)mats;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
 
-  for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-    const int slot = item / G.items_rb;
-    const int rbg = item - slot * G.items_rb;
-    const int e = slot_expert[slot];
-    const int abase = slot_start[slot];
-    const int count = slot_start[slot + 1] - abase;
-    const int r0 = (rbg * G.RBc + rb) * 16;
-    for (int gb = 0; gb < count; gb += P.tok_cap) {
-      const int ntok = min(P.tok_cap, count - gb);
-      __syncthreads();
-      for (int m = 0; m < ntok; ++m) {
-        const int a = assign[abase + gb + m];
-        const uint16_t* src = (P.mode == MODE_W2C) ? G.x + (size_t)a * G.xs
-                                                   : G.x + (size_t)(a / G.R) * G.xs;
-        stage_row(xs + m * P.tstride, src, G.K, threadIdx.x, NTHREADS);
+  const bool dense = P.mode == MODE_DENSE;
+  int nitems = 0;
+  int* slot_expert = nullptr;
+  int* slot_start = nullptr;
+  int* assign = nullptr;
+  bool x_resident = false;
+
+  if (dense) {
+    nitems = P.total_items;
+    x_resident = P.prob[0].x_off >= 0;
+    if (producer) {
+      // Weights never depend on the previous kernel: start streaming at once
+      // and wait for that kernel only when the ring is full.
+      const uint64_t pol = l2_evict_first_policy();
+      int use = 0;
+      bool waited = false;
+      for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++use) {
+        if (!waited && use >= P.stages) {
+          pdl_wait();
+          waited = true;
+        }
+        const int s = use % P.stages;
+        const uint32_t ph = (use / P.stages) & 1;
+        if (!mbar_wait_bounded(&empty[s], ph ^ 1)) {
+          if (lane == 0) atomicOr(P.err, ERR_TIMEOUT);
+          break;
+        }
+        Item it;
+        describe_dense(P, item, it);
+        produce_item(it, ring + (size_t)s * P.stage_bytes, &full[s], pol);
       }
-      __syncthreads();
+      if (!waited) pdl_wait();
+      return;
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    if (x_resident) {
+      for (int p = 0; p < P.nprob; ++p) {
+        const DenseProb& D = P.prob[p];
+        bool dup = false;
+        for (int q = 0; q < p; ++q) dup |= (P.prob[q].x_off == D.x_off);
+        if (dup) continue;
+        for (int m = 0; m < D.M; ++m)
+          stage_row(xs + D.x_off + m * P.tstride, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+      }
+    }
+    named_barrier(CBAR, NCT);
+  } else {
+    pdl_wait();
+    pdl_launch_dependents();
+    const GroupedArgs& G = P.g;
+    slot_expert = cnt + (G.E + 1);
+    slot_start = slot_expert + G.E;
+    assign = slot_start + (G.E + 1);
+    const int nslots = build_plan(G, P.err, cnt, slot_expert, slot_start, assign);
+    nitems = nslots * G.items_rb;
+    x_resident = G.x_rows > 0;
+    if (x_resident) {
+      for (int r = 0; r < G.x_rows; ++r)
+        stage_row(xs + r * P.tstride, G.x + (size_t)r * G.xs, G.K, threadIdx.x, NTHREADS);
+    }
+    __syncthreads();
+    if (producer) {
+      const uint64_t pol = l2_evict_first_policy();
+      int use = 0;
+      for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++use) {
+        const int s = use % P.stages;
+        const uint32_t ph = (use / P.stages) & 1;
+        if (!mbar_wait_bounded(&empty[s], ph ^ 1)) {
+          if (lane == 0) atomicOr(P.err, ERR_TIMEOUT);
+          break;
+        }
+        Item it;
+        describe_grouped(P, item, slot_expert, slot_start, it);
+        produce_item(it, ring + (size_t)s * P.stage_bytes, &full[s], pol);
+      }
+      return;
+    }
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  int rslot = 0;
+  int use = 0;
+  for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++use) {
+    Item it;
+    if (dense)
+      describe_dense(P, item, it);
+    else
+      describe_grouped(P, item, slot_expert, slot_start, it);
+    const int s = use % P.stages;
+    const uint32_t ph = (use / P.stages) & 1;
+    if (!mbar_wait_bounded(&full[s], ph)) {
+      if (lane == 0) atomicOr(P.err, ERR_TIMEOUT);
+      break;
+    }
+    uint8_t* stage = ring + (size_t)s * P.stage_bytes;
+    const int per_mat = it.RBc * it.KS;
+    const int mat = warp / per_mat;
+    const int rem = warp - mat * per_mat;
+    const int rb = rem / it.KS;
+    const int ks = rem - rb * it.KS;
+    const int KB = (it.K + 127) >> 7;
+    const int kb0 = KB * ks / it.KS, kb1 = KB * (ks + 1) / it.KS;
+    const int rb_rows = min(16, it.rows - rb * 16);
+    const uint8_t* wtile = stage + (mat * it.RBc * 16 + rb * 16) * it.RS;
+    const uint16_t* srow =
+        it.scale_bulk ? reinterpret_cast<const uint16_t*>(stage + stage_scale_offset(it) +
+                                                          mat * stage_scale_stride(it)) +
+                            rb * 16 * it.ng
+                      : (mat ? it.s[1] : it.s[0]) + (size_t)(it.r0 + rb * 16) * it.ng;
+
+    for (int gb = 0; gb < it.count; gb += P.tok_cap) {
+      const int ntok = min(P.tok_cap, it.count - gb);
+      const uint8_t* xrow[NSUB];
+      if (x_resident) {
+#pragma unroll
+        for (int q = 0; q < NSUB; ++q)
+          xrow[q] = xs + resident_off(P, it, assign, gb + min(q * 8 + g, ntok - 1));
+      } else {
+        named_barrier(CBAR, NCT);
+        for (int m = 0; m < ntok; ++m)
+          stage_row(xs + m * P.tstride, token_src(P, it, assign, gb + m), it.K, threadIdx.x,
+                    NCT);
+        named_barrier(CBAR, NCT);
+#pragma unroll
+        for (int q = 0; q < NSUB; ++q) xrow[q] = xs + min(q * 8 + g, ntok - 1) * P.tstride;
+      }
       float acc[NSUB][4];
 #pragma unroll
       for (int q = 0; q < NSUB; ++q)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[q][i] = 0.f;
-      if (r0 < G.N) {
-        const uint8_t* wbase = (mat ? G.w1 : G.w0) + (size_t)e * (size_t)G.wse;
-        const uint16_t* sbase = (mat ? G.s1 : G.s0) + (size_t)e * (size_t)G.sse;
-        rowblock_mma<NSUB>(wbase, sbase, G.N, G.K, G.gshift, r0, kb0, kb1, xs, P.tstride, ntok,
-                           acc);
-      }
+      if (rb_rows > 0)
+        rowblock_compute<NSUB>(wtile, it.RS, srow, it.ng, rb_rows, it.K, it.gshift, kb0, kb1,
+                               xrow, (ntok + 7) >> 3, acc);
+      float* rbuf = red + rslot * (NCW * NSUB * 128);
 #pragma unroll
       for (int q = 0; q < NSUB; ++q)
-        *reinterpret_cast<float4*>(red + ((warp * NSUB + q) * 32 + lane) * 4) =
+        *reinterpret_cast<float4*>(rbuf + ((warp * NSUB + q) * 32 + lane) * 4) =
             make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
-      __syncthreads();
-      if (mat == 0 && ks == 0 && r0 < G.N) {
+      named_barrier(CBAR, NCT);
+      if (mat == 0 && ks == 0 && rb_rows > 0) {
 #pragma unroll
         for (int q = 0; q < NSUB; ++q) {
           float v0[4] = {0.f, 0.f, 0.f, 0.f};
           float v1[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int k2 = 0; k2 < G.KS; ++k2) {
+          for (int k2 = 0; k2 < it.KS; ++k2) {
             const float4 pv = *reinterpret_cast<const float4*>(
-                red + (((warp + k2) * NSUB + q) * 32 + lane) * 4);
+                rbuf + (((warp + k2) * NSUB + q) * 32 + lane) * 4);
             v0[0] += pv.x;
             v0[1] += pv.y;
             v0[2] += pv.z;
             v0[3] += pv.w;
             if (P.mode == MODE_SWIGLU) {
               const float4 uv = *reinterpret_cast<const float4*>(
-                  red + (((warp + per_mat + k2) * NSUB + q) * 32 + lane) * 4);
+                  rbuf + (((warp + per_mat + k2) * NSUB + q) * 32 + lane) * 4);
               v1[0] += uv.x;
               v1[1] += uv.y;
               v1[2] += uv.z;
@@ -394,41 +634,52 @@ __device__ void grouped_loop(const EngineParams& P, uint8_t* xs, float* red, uin
           }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int row = r0 + g + ((i >> 1) << 3);
+            const int rloc = rb * 16 + g + ((i >> 1) << 3);
             const int tok = q * 8 + 2 * t + (i & 1);
-            if (row < G.N && tok < ntok) {
-              const int a = assign[abase + gb + tok];
-              const size_t o = (size_t)a * G.N + row;
-              if (P.mode == MODE_GROUPED) {
-                G.y[o] = float_to_bf16_bits(v0[i]);
-              } else if (P.mode == MODE_SWIGLU) {
-                G.y[o] = float_to_bf16_bits(swiglu_contract(v0[i], v1[i]));
+            if (rloc < it.rows && tok < ntok) {
+              const int row = it.r0 + rloc;
+              if (dense) {
+                const DenseProb& D = P.prob[it.p];
+                D.y[(size_t)(gb + tok) * D.ys + row] = float_to_bf16_bits(v0[i]);
               } else {
-                G.wsy[o] = float_to_bf16_bits(v0[i]);
+                const int a = assign[it.abase + gb + tok];
+                const size_t o = (size_t)a * P.g.N + row;
+                if (P.mode == MODE_GROUPED)
+                  P.g.y[o] = float_to_bf16_bits(v0[i]);
+                else if (P.mode == MODE_SWIGLU)
+                  P.g.y[o] = float_to_bf16_bits(swiglu_contract(v0[i], v1[i]));
+                else
+                  P.g.wsy[o] = float_to_bf16_bits(v0[i]);
               }
             }
           }
         }
       }
+      rslot ^= 1;
       if (P.mode == MODE_W2C) {
         // Arrival: once all R routes of a token have written this row group,
-        // the CTA that arrives last combines them (fixed route order).
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x < ntok) {
-          const int a = assign[abase + gb + threadIdx.x];
-          const int tok = a / G.R;
-          const int old = atomicAdd(&G.counters[tok * G.items_rb + rbg], 1);
-          s_done[threadIdx.x] = (old == G.R - 1) ? tok : -1;
+        // the CTA that arrives last combines them in fixed route order.
+        const GroupedArgs& G = P.g;
+        const int rbg = it.r0 / (G.RBc * 16);
+        // One thread publishes the group: the barrier orders every consumer's
+        // stores before its release fence, and the fence before the counters.
+        named_barrier(CBAR, NCT);
+        if (threadIdx.x == 0) {
+          __threadfence();
+          for (int m = 0; m < ntok; ++m) {
+            const int a = assign[it.abase + gb + m];
+            const int tok = a / G.R;
+            const int old = atomicAdd(&G.counters[tok * G.items_rb + rbg], 1);
+            s_done[m] = (old == G.R - 1) ? tok : -1;
+          }
+          __threadfence();  // acquire side for the combine below
         }
-        __syncthreads();
-        const int rstart = rbg * G.RBc * 16;
-        const int rend = min(G.N, rstart + G.RBc * 16);
+        named_barrier(CBAR, NCT);
         for (int m = 0; m < ntok; ++m) {
           const int tok = s_done[m];
           if (tok < 0) continue;
-          __threadfence();
-          for (int row = rstart + threadIdx.x; row < rend; row += NTHREADS) {
+          for (int rl = threadIdx.x; rl < it.rows; rl += NCT) {
+            const int row = it.r0 + rl;
             float accum = 0.f;
             for (int r = 0; r + 1 < G.R; ++r) {
               const uint16_t ov = __ldcg(&G.wsy[((size_t)tok * G.R + r) * G.N + row]);
@@ -440,22 +691,13 @@ __device__ void grouped_loop(const EngineParams& P, uint8_t* xs, float* red, uin
           }
           if (threadIdx.x == 0) G.counters[tok * G.items_rb + rbg] = 0;
         }
+        // s_done is rewritten by the next group only after its barriers.
       }
-      __syncthreads();
     }
+    // This warp has finished reading stage s.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
-}
-
-template <int NSUB>
-__global__ void __launch_bounds__(NTHREADS, 1) w4a16_engine(const __grid_constant__ EngineParams P) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  pdl_wait();
-  pdl_launch_dependents();
-  float* red = reinterpret_cast<float*>(smem + P.red_off);
-  if (P.mode == MODE_DENSE)
-    dense_loop<NSUB>(P, smem, red);
-  else
-    grouped_loop<NSUB>(P, smem, red, smem + P.plan_off);
 }
 
 // ---------------------------------------------------------------------------
@@ -483,10 +725,10 @@ static int check_group(int64_t K, int64_t group, int* gshift) {
 
 // Warp split for a reduction width: KS warps share a 16-row block, each
 // covering at least four 128-wide blocks when possible; RBc row blocks per
-// item so that mats * RBc * KS == NW.
+// item so that mats * RBc * KS == NCW.
 static void choose_split(int K, int mats, int* KS, int* RBc) {
   const int KB = (K + 127) / 128;
-  const int maxks = NW / mats;
+  const int maxks = NCW / mats;
   int ks = 1;
   while (ks * 2 <= maxks && KB / (ks * 2) >= 4) ks *= 2;
   *KS = ks;
@@ -503,8 +745,15 @@ static int token_stride(int K) {
   return bytes + pad;
 }
 
+static int item_stage_bytes(int K, int mats, int RBc, int ng) {
+  const int rows = RBc * 16;
+  const int wb = mats * rows * row_stride_bytes(K);
+  const int sb = mats * ((rows * ng * 2 + 15) / 16 * 16);
+  return (wb + sb + 127) / 128 * 128;
+}
+
 template <int NSUB>
-static int engine_launch(EngineParams& P, int grid_items, size_t smem, void* stream) {
+static int engine_launch(EngineParams& P, int grid_items, size_t fixed_smem, void* stream) {
   static std::once_flag once[2];
   static cudaError_t attr_err[2] = {cudaSuccess, cudaSuccess};
   std::call_once(once[NSUB - 1], [] {
@@ -513,14 +762,22 @@ static int engine_launch(EngineParams& P, int grid_items, size_t smem, void* str
   });
   KB_REQUIRE(attr_err[NSUB - 1] == cudaSuccess, KB_ERR_LAUNCH,
              "cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err[NSUB - 1]));
-  KB_REQUIRE(smem <= (size_t)MAX_SMEM, KB_ERR_UNSUPPORTED,
-             "shared memory need %zu bytes exceeds %d (reduce K or tokens)", smem, MAX_SMEM);
+  // The ring takes what the fixed regions (activations, reduction, plan) leave.
+  const size_t reserve = SMEM_RESERVE;
+  KB_REQUIRE(fixed_smem + reserve + 2 * (size_t)P.stage_bytes <= (size_t)MAX_SMEM,
+             KB_ERR_UNSUPPORTED,
+             "shared memory: %zu bytes of fixed regions leave no room for two %d-byte stages",
+             fixed_smem, P.stage_bytes);
+  const size_t avail = (size_t)MAX_SMEM - reserve - fixed_smem;
+  P.stages = (int)std::min<size_t>(MAX_STAGES, avail / P.stage_bytes);
+  P.ring_off = (int)((fixed_smem + 127) / 128 * 128);
+  P.bar_off = P.ring_off + P.stages * P.stage_bytes;
+  const size_t smem = (size_t)P.bar_off + 2 * P.stages * sizeof(uint64_t);
+  KB_REQUIRE(smem + 256 <= (size_t)MAX_SMEM, KB_ERR_UNSUPPORTED, "shared memory plan overflow");
   const int dev = bind_stream_device(stream);
-  int occ = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w4a16_engine<NSUB>, NTHREADS, smem);
-  if (occ < 1) occ = 1;
-  const int grid = std::max(1, std::min(grid_items, num_sms(dev) * occ));
   P.err = device_error_word(dev);
+  KB_REQUIRE(P.err != nullptr, KB_ERR_LAUNCH, "device error word unavailable");
+  const int grid = std::max(1, std::min(grid_items, num_sms(dev)));
   return launch(w4a16_engine<NSUB>, dim3(grid), dim3(NTHREADS), smem, stream, P);
 }
 
@@ -538,8 +795,9 @@ static int dense_multi_impl(const kb_dense_problem* probs, int count, void* stre
                (long long)q.M, (long long)q.K, (long long)q.N);
     KB_REQUIRE(q.K % 32 == 0, KB_ERR_BAD_SHAPE,
                "problem %d: reduction width %lld is not divisible by 32", i, (long long)q.K);
-    KB_REQUIRE(q.K <= 65536 && q.N <= (int64_t(1) << 30) && q.M <= (int64_t(1) << 30),
-               KB_ERR_UNSUPPORTED, "problem %d: size above the supported range", i);
+    KB_REQUIRE(q.K <= 16384 && q.N <= (int64_t(1) << 30) && q.M <= (int64_t(1) << 30),
+               KB_ERR_UNSUPPORTED, "problem %d: size above the supported range (K <= 16384)",
+               i);
     int gs = 0;
     int rc = check_group(q.K, q.group, &gs);
     if (rc) return rc;
@@ -573,22 +831,47 @@ static int dense_multi_impl(const kb_dense_problem* probs, int count, void* stre
   if (P.nprob == 0) return KB_OK;
   const int nsub = (maxM > 8) ? 2 : 1;
   P.tok_cap = 8 * nsub;
-  int items = 0;
+  P.tstride = token_stride(maxK);
+  int items = 0, stage = 0;
   for (int i = 0; i < P.nprob; ++i) {
     DenseProb& D = P.prob[i];
-    D.items_rb = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
-    D.tok_groups = (D.M + P.tok_cap - 1) / P.tok_cap;
+    D.items = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
     D.item_begin = items;
-    items += D.items_rb * D.tok_groups;
+    items += D.items;
+    stage = std::max(stage, item_stage_bytes(D.K, 1, D.RBc, D.K >> (5 + D.gshift)));
+  }
+  const int red_bytes = 2 * NCW * nsub * 128 * (int)sizeof(float);
+  const int x_budget =
+      std::min(X_RESIDENT_BUDGET, MAX_SMEM - SMEM_RESERVE - red_bytes - 2 * stage - 128);
+  KB_REQUIRE(x_budget >= P.tstride, KB_ERR_UNSUPPORTED,
+             "shared memory cannot hold one activation row of K=%d next to two stages", maxK);
+  // Resident activations: every distinct x, all of its tokens, if they fit.
+  int xbytes = 0;
+  for (int i = 0; i < P.nprob; ++i) {
+    DenseProb& D = P.prob[i];
+    D.x_off = -1;
+    for (int j = 0; j < i; ++j)
+      if (P.prob[j].x == D.x && P.prob[j].xs == D.xs && P.prob[j].K == D.K &&
+          P.prob[j].M == D.M)
+        D.x_off = P.prob[j].x_off;
+    if (D.x_off < 0) {
+      D.x_off = xbytes;
+      xbytes += D.M * P.tstride;
+    }
+  }
+  if (xbytes > x_budget) {
+    for (int i = 0; i < P.nprob; ++i) P.prob[i].x_off = -1;
+    P.tok_cap = std::min(P.tok_cap, x_budget / P.tstride);
+    xbytes = P.tok_cap * P.tstride;
   }
   P.total_items = items;
-  P.tstride = token_stride(maxK);
-  const int staged = std::min(P.tok_cap, maxM);
-  P.red_off = ((staged * P.tstride) + 127) / 128 * 128;
-  const size_t smem = (size_t)P.red_off + (size_t)NW * nsub * 32 * 4 * sizeof(float);
-  P.plan_off = 0;
-  return nsub == 2 ? engine_launch<2>(P, items, smem, stream)
-                   : engine_launch<1>(P, items, smem, stream);
+  P.x_bytes = (xbytes + 127) / 128 * 128;
+  P.red_off = P.x_bytes;
+  P.plan_off = P.red_off + red_bytes;
+  P.stage_bytes = stage;
+  const size_t fixed = (size_t)P.plan_off;
+  return nsub == 2 ? engine_launch<2>(P, items, fixed, stream)
+                   : engine_launch<1>(P, items, fixed, stream);
 }
 
 static int grouped_impl(int mode, const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
@@ -608,8 +891,8 @@ static int grouped_impl(int mode, const uint16_t* x, int64_t x_stride, int64_t T
   KB_REQUIRE(T * R <= KB_MAX_ASSIGNMENTS, KB_ERR_UNSUPPORTED,
              "T*R = %lld exceeds the limit of %d assignments per call", (long long)(T * R),
              KB_MAX_ASSIGNMENTS);
-  KB_REQUIRE(E <= 4096 && K <= 65536 && N <= (int64_t(1) << 24), KB_ERR_UNSUPPORTED,
-             "E, K or N above the supported range");
+  KB_REQUIRE(E <= 4096 && K <= 16384 && N <= (int64_t(1) << 24), KB_ERR_UNSUPPORTED,
+             "E, K or N above the supported range (E <= 4096, K <= 16384)");
   KB_REQUIRE(x && idx && w0 && s0, KB_ERR_NULL_POINTER, "NULL input pointer");
   KB_REQUIRE(mode != MODE_SWIGLU || (w1 && s1), KB_ERR_NULL_POINTER, "NULL w3 pointer");
   KB_REQUIRE(aligned(x, 16) && x_stride % 8 == 0 && x_stride >= K, KB_ERR_ALIGNMENT,
@@ -617,6 +900,8 @@ static int grouped_impl(int mode, const uint16_t* x, int64_t x_stride, int64_t T
              "elements and >= K");
   KB_REQUIRE(aligned(w0, 16) && (!w1 || aligned(w1, 16)), KB_ERR_ALIGNMENT,
              "packed weights must be 16-byte aligned");
+  KB_REQUIRE(aligned(s0, 2) && (!s1 || aligned(s1, 2)), KB_ERR_ALIGNMENT,
+             "scales must be 2-byte aligned");
   KB_REQUIRE(aligned(idx, 8), KB_ERR_ALIGNMENT, "expert indices must be 8-byte aligned");
   EngineParams P = {};
   P.mode = mode;
@@ -656,18 +941,37 @@ static int grouped_impl(int mode, const uint16_t* x, int64_t x_stride, int64_t T
     KB_REQUIRE(y, KB_ERR_NULL_POINTER, "NULL output pointer");
   }
   const int64_t TR = T * R;
-  const int maxtok = (int)std::min<int64_t>(TR, 16);
-  const int nsub = (maxtok > 8) ? 2 : 1;
+  // An expert serves at most T assignments when each token routes to distinct
+  // experts; more (repeated experts within a token) still works through
+  // several token groups.
+  const int nsub = (T > 8) ? 2 : 1;
   P.tok_cap = 8 * nsub;
   P.tstride = token_stride(G.K);
-  const int staged = std::min(P.tok_cap, maxtok);
-  P.red_off = ((staged * P.tstride) + 127) / 128 * 128;
-  P.plan_off = P.red_off + NW * nsub * 32 * 4 * (int)sizeof(float);
-  const size_t smem = (size_t)P.plan_off + (size_t)(3 * E + 2 + TR) * sizeof(int);
+  P.stage_bytes = item_stage_bytes(G.K, mats, G.RBc, G.K >> (5 + gs));
+  const int red_bytes = 2 * NCW * nsub * 128 * (int)sizeof(float);
+  const size_t plan_bytes = ((size_t)(3 * E + 2 + TR) * sizeof(int) + 127) / 128 * 128;
+  const int x_budget = std::min<int>(
+      X_RESIDENT_BUDGET,
+      MAX_SMEM - SMEM_RESERVE - red_bytes - (int)plan_bytes - 2 * P.stage_bytes - 128);
+  KB_REQUIRE(x_budget >= P.tstride, KB_ERR_UNSUPPORTED,
+             "shared memory cannot hold one activation row of K=%d next to two stages", G.K);
+  const int64_t xrows = (mode == MODE_W2C) ? TR : T;
+  if (xrows * P.tstride <= x_budget) {
+    G.x_rows = (int)xrows;
+    P.x_bytes = (int)xrows * P.tstride;
+  } else {
+    G.x_rows = 0;
+    P.tok_cap = std::min(P.tok_cap, x_budget / P.tstride);
+    P.x_bytes = P.tok_cap * P.tstride;
+  }
+  P.x_bytes = (P.x_bytes + 127) / 128 * 128;
+  P.red_off = P.x_bytes;
+  P.plan_off = P.red_off + red_bytes;
+  const size_t fixed = (size_t)P.plan_off + plan_bytes;
   const int64_t max_slots = std::min<int64_t>(E, TR);
   const int grid_items = (int)std::min<int64_t>(max_slots * G.items_rb, 1 << 20);
-  return nsub == 2 ? engine_launch<2>(P, grid_items, smem, stream)
-                   : engine_launch<1>(P, grid_items, smem, stream);
+  return nsub == 2 ? engine_launch<2>(P, grid_items, fixed, stream)
+                   : engine_launch<1>(P, grid_items, fixed, stream);
 }
 
 }  // namespace kb

@@ -1,0 +1,272 @@
+"""Kimi-Linear-48B-A3B W4A16 decode step on the B200 kernels (the hot path).
+
+One decode step runs, for each of the 27 layers, every INT4 projection of the
+layer, the KDA recurrent-state step of the KDA layers, and the MoE block
+(router top-8 with the shared route appended, gate/up + SwiGLU over the
+touched experts, down projection + routing-weighted combine), then the INT4
+lm_head.  Shapes follow engine/klinear/config.py:38-80 (hidden 2304, 27 layers
+with MLA at layers 4, 8, ..., 24, 27 one-based and KDA elsewhere, KDA 32 heads
+x 128, MLA 32 heads with q 32 x 192 and kv_b 512 -> 32 x 256, 256 experts +
+1 shared, intermediate 1024, layer 0 a dense 9216-wide MLP, vocab 163840) and
+the INT4 classes of engine/quant/klinear_plan.py:320-419 (attention
+projections, experts, shared expert, layer-0 MLP; plus the INT4 lm_head of
+KLinearModel.quantize_lm_head, engine/klinear/model.py:134-160).
+
+The parts of a layer that are not on this path -- RMS norms, the short
+convolutions and gates that prepare the KDA inputs, MLA softmax attention, the
+BF16-retained projections -- are not computed.  Their outputs enter as fixed
+synthetic tensors: the KDA step reads fixed normalised q/k, v, decay and beta;
+the MLA kv_b and o_proj projections read a fixed latent and attention output.
+The data dependencies kept are the ones along the path: the KDA step output
+(bf16) feeds o_proj, o_proj feeds the MoE block, the MoE output feeds the next
+layer's projections, the last layer's output feeds the lm_head.
+
+Weights are random-init (N(0, 0.02) bf16, quantised on the device by the
+codec kernel), generated from seeded CUDA generators.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .moe import MoELayerWeights, moe_forward
+
+
+@dataclass(frozen=True)
+class KimiLinearShape:
+    vocab_size: int = 163_840
+    hidden: int = 2_304
+    layers: int = 27
+    kda_heads: int = 32
+    kda_head_dim: int = 128
+    mla_heads: int = 32
+    mla_q_head_dim: int = 192      # qk_nope 128 + qk_rope 64
+    kv_lora_rank: int = 512
+    mla_kv_head_dim: int = 256     # qk_nope 128 + v 128
+    mla_v_head_dim: int = 128
+    experts: int = 256
+    top_k: int = 8
+    moe_intermediate: int = 1_024
+    dense_intermediate: int = 9_216
+    routed_scaling_factor: float = 2.446
+    first_k_dense: int = 1
+    # one-based full-attention (MLA) layers, engine/klinear/config.py:10
+    mla_layers: tuple[int, ...] = field(default_factory=lambda: (4, 8, 12, 16, 20, 24, 27))
+
+    def is_mla(self, layer: int) -> bool:
+        return (layer + 1) in self.mla_layers
+
+
+@dataclass
+class LayerWeights:
+    kind: str                       # "kda" or "mla"
+    qkv: list[tuple[torch.Tensor, torch.Tensor]] | None = None   # KDA q, k, v
+    q_proj: tuple[torch.Tensor, torch.Tensor] | None = None      # MLA
+    kv_b: tuple[torch.Tensor, torch.Tensor] | None = None        # MLA
+    o_proj: tuple[torch.Tensor, torch.Tensor] | None = None
+    kda_state: torch.Tensor | None = None                        # fp32 [B, H, 128, 128]
+    moe: MoELayerWeights | None = None
+    dense_mlp: tuple | None = None  # (w1p, w1s, w3p, w3s) banks [1, I, H/2], (w2p, w2s)
+
+
+def _bytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
+
+
+class HotPathDecoder:
+    """Synthetic-weight Kimi-Linear-48B-A3B decode hot path for a batch of B tokens."""
+
+    def __init__(self, batch: int, *, group: int = 128, device: str | torch.device = "cuda",
+                 shape: KimiLinearShape | None = None, seed: int = 0,
+                 layers: int | None = None) -> None:
+        self.shape = shape or KimiLinearShape()
+        self.batch = batch
+        self.group = group
+        self.device = torch.device(device)
+        self.nlayers = self.shape.layers if layers is None else layers
+        self._gen = torch.Generator(device=self.device)
+        self._gen.manual_seed(seed)
+        s = self.shape
+        self.layers: list[LayerWeights] = []
+        for layer in range(self.nlayers):
+            self.layers.append(self._make_layer(layer))
+        self.lm_head = self._quant(s.vocab_size, s.hidden)
+        self._make_inputs(seed + 1)
+        self.launches_per_step = self._count_launches()
+
+    # -- weights ---------------------------------------------------------------
+    def _randn(self, shape) -> torch.Tensor:
+        return (torch.randn(shape, generator=self._gen, device=self.device) * 0.02).to(
+            torch.bfloat16)
+
+    def _quant(self, n: int, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return ops.quantise(self._randn((n, k)), self.group)
+
+    def _bank(self, experts: int, n: int, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+        packed = torch.empty((experts, n, k // 2), dtype=torch.uint8, device=self.device)
+        scales = torch.empty((experts, n, k // self.group), dtype=torch.bfloat16,
+                             device=self.device)
+        chunk = 64
+        for e0 in range(0, experts, chunk):
+            e1 = min(experts, e0 + chunk)
+            p, sc = ops.quantise(self._randn(((e1 - e0) * n, k)), self.group)
+            packed[e0:e1] = p.view(e1 - e0, n, k // 2)
+            scales[e0:e1] = sc.view(e1 - e0, n, k // self.group)
+        return packed, scales
+
+    def _make_layer(self, layer: int) -> LayerWeights:
+        s = self.shape
+        B = self.batch
+        if s.is_mla(layer):
+            lw = LayerWeights(
+                kind="mla",
+                q_proj=self._quant(s.mla_heads * s.mla_q_head_dim, s.hidden),
+                kv_b=self._quant(s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank),
+                o_proj=self._quant(s.hidden, s.mla_heads * s.mla_v_head_dim),
+            )
+        else:
+            proj = s.kda_heads * s.kda_head_dim
+            lw = LayerWeights(
+                kind="kda",
+                qkv=[self._quant(proj, s.hidden) for _ in range(3)],
+                o_proj=self._quant(s.hidden, proj),
+                kda_state=0.05 * torch.randn((B, s.kda_heads, s.kda_head_dim, s.kda_head_dim),
+                                             generator=self._gen, device=self.device),
+            )
+        if layer < s.first_k_dense:
+            w1 = self._bank(1, s.dense_intermediate, s.hidden)
+            w3 = self._bank(1, s.dense_intermediate, s.hidden)
+            w2 = self._quant(s.hidden, s.dense_intermediate)
+            lw.dense_mlp = (w1, w3, w2)
+        else:
+            router = self._randn((s.experts, s.hidden))
+            w1 = self._bank(s.experts + 1, s.moe_intermediate, s.hidden)
+            w2 = self._bank(s.experts + 1, s.hidden, s.moe_intermediate)
+            w3 = self._bank(s.experts + 1, s.moe_intermediate, s.hidden)
+            lw.moe = MoELayerWeights(router, torch.zeros(s.experts, device=self.device), *w1,
+                                     *w2, *w3, top_k=s.top_k, scaling=s.routed_scaling_factor)
+        return lw
+
+    def _make_inputs(self, seed: int) -> None:
+        s = self.shape
+        B = self.batch
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        self.x0 = torch.randn((B, s.hidden), generator=g, device=self.device).to(torch.bfloat16)
+        H, D = s.kda_heads, s.kda_head_dim
+        self.kda_q = F.normalize(torch.randn((B, H, D), generator=g, device=self.device), dim=-1)
+        self.kda_k = F.normalize(torch.randn((B, H, D), generator=g, device=self.device), dim=-1)
+        self.kda_v = 0.2 * torch.randn((B, H, D), generator=g, device=self.device)
+        self.kda_decay = -(0.005 + 0.075 * torch.rand((B, H, D), generator=g,
+                                                      device=self.device))
+        self.kda_beta = torch.sigmoid(torch.randn((B, H), generator=g, device=self.device))
+        self.kda_out = torch.empty((B, H * D), dtype=torch.bfloat16, device=self.device)
+        self.mla_latent = torch.randn((B, s.kv_lora_rank), generator=g,
+                                      device=self.device).to(torch.bfloat16)
+        self.mla_attn = torch.randn((B, s.mla_heads * s.mla_v_head_dim), generator=g,
+                                    device=self.device).to(torch.bfloat16)
+        self.dense_idx = torch.zeros((B, 1), dtype=torch.long, device=self.device)
+
+    # -- one step --------------------------------------------------------------------
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        """x bf16 [B, hidden] -> logits bf16 [B, vocab]."""
+        s = self.shape
+        for lw in self.layers:
+            if lw.kind == "kda":
+                ops.w4a16_dense_multi([(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
+                ops.kda_decode_step(lw.kda_state, self.kda_q, self.kda_k, self.kda_v,
+                                    self.kda_decay, self.kda_beta, scale=s.kda_head_dim ** -0.5,
+                                    out_bf16=self.kda_out)
+                h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
+            else:
+                _, _, h = ops.w4a16_dense_multi(
+                    [(x, *lw.q_proj), (self.mla_latent, *lw.kv_b), (self.mla_attn, *lw.o_proj)])
+            if lw.dense_mlp is not None:
+                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+                act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
+                x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
+            else:
+                x, _, _ = moe_forward(h, lw.moe)
+        return ops.w4a16_dense(x, *self.lm_head)
+
+    def _count_launches(self) -> int:
+        n = 1  # lm_head
+        for lw in self.layers:
+            n += 3 if lw.kind == "kda" else 1
+            n += 2 if lw.dense_mlp is not None else 3
+        return n
+
+    # -- byte accounting ----------------------------------------------------------------
+    def weight_bytes(self) -> int:
+        """Resident bytes of every quantised weight and bf16 router of the model."""
+        total = _bytes(self.lm_head[0]) + _bytes(self.lm_head[1])
+        for lw in self.layers:
+            for pair in (lw.qkv or []) + [m for m in (lw.q_proj, lw.kv_b, lw.o_proj) if m]:
+                total += _bytes(pair[0]) + _bytes(pair[1])
+            if lw.dense_mlp is not None:
+                total += sum(_bytes(t) for pair in lw.dense_mlp for t in pair)
+            if lw.moe is not None:
+                m = lw.moe
+                total += sum(_bytes(t) for t in (m.router_weight, m.w1_packed, m.w1_scales,
+                                                 m.w2_packed, m.w2_scales, m.w3_packed,
+                                                 m.w3_scales))
+        return total
+
+    def step_bytes(self, expert_counts: list[int] | None = None) -> dict[str, int]:
+        """Algorithmic bytes of one step by component.
+
+        expert_counts[l]: distinct experts (routed + shared) touched in MoE
+        layer l; defaults to top_k + 1 per token capped at E + 1 (batch 1).
+        """
+        s = self.shape
+        B = self.batch
+        out = {"dense_proj": 0, "experts": 0, "router": 0, "kda_state": 0, "lm_head": 0,
+               "activations": 0}
+        moe_i = 0
+        for lw in self.layers:
+            mats = (lw.qkv or []) + [m for m in (lw.q_proj, lw.kv_b, lw.o_proj) if m is not None]
+            for p, sc in mats:
+                out["dense_proj"] += _bytes(p) + _bytes(sc)
+            if lw.kda_state is not None:
+                out["kda_state"] += 2 * _bytes(lw.kda_state)
+            if lw.dense_mlp is not None:
+                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+                out["dense_proj"] += sum(_bytes(t) for t in (w1p, w1s, w3p, w3s, w2p, w2s))
+            if lw.moe is not None:
+                m = lw.moe
+                per_expert = sum(_bytes(t[0]) for t in (m.w1_packed, m.w1_scales, m.w2_packed,
+                                                        m.w2_scales, m.w3_packed, m.w3_scales))
+                touched = (expert_counts[moe_i] if expert_counts is not None
+                           else min(s.experts + 1, B * s.top_k + 1))
+                out["experts"] += per_expert * touched
+                out["router"] += _bytes(m.router_weight)
+                moe_i += 1
+        out["lm_head"] = _bytes(self.lm_head[0]) + _bytes(self.lm_head[1])
+        out["activations"] = B * s.hidden * 2 * (2 * self.nlayers) + B * s.vocab_size * 2
+        out["total"] = sum(out.values())
+        return out
+
+    def touched_experts(self, x: torch.Tensor) -> list[int]:
+        """Distinct experts per MoE layer for input x (runs one step eagerly)."""
+        counts = []
+        s = self.shape
+        for lw in self.layers:
+            if lw.kind == "kda":
+                ops.kda_decode_step(lw.kda_state.clone(), self.kda_q, self.kda_k, self.kda_v,
+                                    self.kda_decay, self.kda_beta, scale=s.kda_head_dim ** -0.5,
+                                    out_bf16=self.kda_out)
+                h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
+            else:
+                h = ops.w4a16_dense(self.mla_attn, *lw.o_proj)
+            if lw.dense_mlp is not None:
+                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+                act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
+                x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
+            else:
+                x, idx, _ = moe_forward(h, lw.moe)
+                counts.append(int(torch.unique(idx).numel()) + 1)
+        return counts

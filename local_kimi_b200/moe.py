@@ -4,10 +4,10 @@ The composition of KLinearMoE.forward with grouped W4A16 banks
 (engine/klinear/moe.py:278-334, :375-398) in three launches:
 
   1. moe_router          fp32 logits, sigmoid, biased top-k, renormalised and
-                         scaled weights (engine/klinear/router.py:47-85)
+                         scaled weights (engine/klinear/router.py:47-85); it also
+                         appends the shared expert (bank slot E) as the last
+                         route (engine/klinear/moe.py:23-36, :284-286)
   2. w4a16_swiglu        gate/up for the k routed experts and the shared expert
-                         (bank slot E, appended as the last route,
-                         engine/klinear/moe.py:23-36, :284-286)
   3. moe_down_combine    down projection of every route + weighted combine,
                          shared route added with weight 1
 
@@ -56,11 +56,11 @@ def moe_forward(
     hidden: torch.Tensor, layer: MoELayerWeights
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """hidden bf16 [T, H] -> (output bf16 [T, H], indices [T, k], weights fp32 [T, k])."""
-    idx, weights = ops.moe_router(
+    stable, weights = ops.moe_router(
         hidden, layer.router_weight, layer.router_bias, layer.top_k,
-        routed_scaling_factor=layer.scaling,
+        routed_scaling_factor=layer.scaling, append_expert=layer.num_experts,
     )
-    stable = stable_indices(idx, layer.num_experts)
+    idx = stable[:, : layer.top_k]
     activated = ops.w4a16_swiglu(
         hidden, stable, layer.w1_packed, layer.w1_scales, layer.w3_packed, layer.w3_scales
     )

@@ -436,11 +436,14 @@ def moe_router(
     *,
     renormalize: bool = True,
     routed_scaling_factor: float = 1.0,
+    append_expert: int | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Sigmoid top-k routing of KLinearRouter.forward (router.py:47-85).
 
     Returns (indices int64 [T, top_k], weights fp32 [T, top_k]), ordered by
-    (biased score desc, expert index asc).
+    (biased score desc, expert index asc).  With ``append_expert`` the indices
+    are [T, top_k + 1] with that expert id as the last route, the
+    shape-stable layout of engine/klinear/moe.py:23-36.
     """
     if hidden_states.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise TypeError("router hidden states and weight must be BF16")
@@ -454,7 +457,8 @@ def moe_router(
         raise ValueError("router weight width does not match the hidden size")
     if not 0 < top_k <= experts:
         raise ValueError("top_k must be in the expert range")
-    idx = torch.empty((tokens, top_k), dtype=torch.long, device=flat.device)
+    extra = 0 if append_expert is None else 1
+    idx = torch.empty((tokens, top_k + extra), dtype=torch.long, device=flat.device)
     wts = torch.empty((tokens, top_k), dtype=torch.float32, device=flat.device)
     if tokens == 0:
         return idx, wts
@@ -462,7 +466,9 @@ def moe_router(
     w = _dense_contig(weight)
     b = None
     if bias is not None:
-        b = bias.detach().to(device=flat.device, dtype=torch.float32).contiguous()
+        b = bias.detach()
+        if b.dtype != torch.float32 or b.device != flat.device or not b.is_contiguous():
+            b = b.to(device=flat.device, dtype=torch.float32).contiguous()
     lib = _lib.lib()
     need = int(lib.kb_router_workspace_size(tokens, experts))
     ws = _workspace("router", flat.device, need, (tokens, experts))
@@ -470,8 +476,9 @@ def moe_router(
         "kb_router_topk",
         _p(x), c_int64(x.stride(0)), c_int64(tokens), c_int64(hidden), _p(w), _p(b),
         c_int64(experts), c_int64(top_k), 1 if renormalize else 0,
-        c_float(float(routed_scaling_factor)), _p(idx), _p(wts), _p(ws), c_size_t(ws.numel()),
-        _stream(flat.device),
+        c_float(float(routed_scaling_factor)), _p(idx),
+        c_int64(-1 if append_expert is None else int(append_expert)), _p(wts), _p(ws),
+        c_size_t(ws.numel()), _stream(flat.device),
     )
     return idx, wts
 
