@@ -19,6 +19,8 @@
 // warp reductions (max key, then min index among the lanes holding it).
 #include "kb_common.cuh"
 
+#include <algorithm>
+
 namespace kb {
 
 constexpr int RT_WARPS = 4;  // experts per CTA
@@ -67,19 +69,35 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
   pdl_wait();
   pdl_launch_dependents();
 
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint16_t* hsm = reinterpret_cast<uint16_t*>(smem_raw);  // [nt][K]
   const int expert = blockIdx.x * RT_WARPS + warp;
+  const uint16_t* wrow = weight + (size_t)min(expert, E - 1) * K;
+  // The first eight 16-byte pieces of this warp's router row are requested
+  // before the hidden states are staged, so both fetches overlap.
+  uint4 wv[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int w = u * 32 + lane;
+    wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
+  }
+  for (int e = threadIdx.x; e < nt * words; e += RT_WARPS * 32) {
+    const int m = e / words, w = e - m * words;
+    reinterpret_cast<uint4*>(hsm + (size_t)m * K)[w] =
+        __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)(t0 + m) * hs) + w);
+  }
+  __syncthreads();
   if (expert < E) {
     float acc[RT_TOK];
 #pragma unroll
     for (int m = 0; m < RT_TOK; ++m) acc[m] = 0.f;
-    const uint16_t* wrow = weight + (size_t)expert * K;
-    // Eight 16-byte pieces per lane in flight at a time.
     for (int w0 = 0; w0 < words; w0 += 32 * 8) {
-      uint4 wv[8];
+      if (w0 > 0) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int w = w0 + u * 32 + lane;
-        wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < 8; ++u) {
+          const int w = w0 + u * 32 + lane;
+          wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
+        }
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -89,8 +107,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
 #pragma unroll
           for (int m = 0; m < RT_TOK; ++m) {
             if (m < nt) {
-              const uint4 hv =
-                  __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)(t0 + m) * hs) + w);
+              const uint4 hv = reinterpret_cast<const uint4*>(hsm + (size_t)m * K)[w];
               const uint32_t hr[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -272,8 +289,8 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
              "router needs T >= 0 and K, E, top_k > 0");
   KB_REQUIRE(top_k <= E, KB_ERR_BAD_SHAPE, "top_k %lld exceeds E %lld", (long long)top_k,
              (long long)E);
-  KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 65536 && K % 8 == 0, KB_ERR_UNSUPPORTED,
-             "router supports E <= 1024, top_k <= 32, K <= 65536 with K %% 8 == 0");
+  KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 8192 && K % 8 == 0, KB_ERR_UNSUPPORTED,
+             "router supports E <= 1024, top_k <= 32, K <= 8192 with K %% 8 == 0");
   if (T == 0) return KB_OK;
   KB_REQUIRE(hidden && weight && idx_out && w_out, KB_ERR_NULL_POINTER, "NULL router pointer");
   KB_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0 && h_stride % 8 == 0 &&
@@ -288,7 +305,14 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
   int* counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + lbytes);
   const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
                   (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
-  return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), 0, stream, hidden,
+  const size_t smem = (size_t)std::min<int64_t>(T, kb::RT_TOK) * K * sizeof(uint16_t);
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(kb::router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)(kb::RT_TOK * 8192 * sizeof(uint16_t)));
+    attr_done = true;
+  }
+  return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,
                     h_stride, (int)T, (int)K, weight, bias, (int)E, (int)top_k, renormalize,
                     scaling, idx_out, append_id, w_out, logits, counters);
 }

@@ -107,17 +107,17 @@ struct Item {
   int K, N, gshift, KS, RBc;
   int r0;           // first row of the item
   int rows;         // valid rows (<= RBc*16)
-  int RS;           // padded shared-memory row stride in bytes
+  int RS;           // shared-memory row stride in bytes (K/2: rows land contiguously)
   int ng;           // scale groups per row
   bool scale_bulk;  // scales copied into the stage (else read from global memory)
   int p;            // dense problem index or grouped slot
   int abase, count; // grouped: assignment range; dense: 0, M
 };
 
-__host__ __device__ __forceinline__ int row_stride_bytes(int K) {
-  const int b = K / 2;
-  return b + ((64 - (b % 128)) + 128) % 128;
-}
+// An item's rows are contiguous in global memory and are copied with one bulk
+// copy per matrix, so they keep their global stride in shared memory.  (Large
+// copies stream at full HBM rate; per-row copies of 0.25-1 KB did not.)
+__host__ __device__ __forceinline__ int row_stride_bytes(int K) { return K / 2; }
 
 __device__ __forceinline__ bool scale_bulk_ok(const uint16_t* s, int r0, int rows, int ng) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(s + (size_t)r0 * ng);
@@ -199,12 +199,10 @@ __device__ __forceinline__ void produce_item(const Item& it, uint8_t* stage, uin
   if (it.scale_bulk) total += (uint32_t)it.mats * sbytes;
   if (lane == 0) mbar_arrive_expect_tx(full, total);
   __syncwarp();
-  const int nrows = it.mats * it.rows;
-  for (int i = lane; i < nrows; i += 32) {
-    const int m = i / it.rows, r = i - m * it.rows;
-    const uint8_t* wm = m ? it.w[1] : it.w[0];
-    bulk_g2s(stage + (m * it.RBc * 16 + r) * it.RS, wm + (size_t)(it.r0 + r) * wbytes, wbytes,
-             full, policy);
+  if (lane < it.mats) {
+    const uint8_t* wm = lane ? it.w[1] : it.w[0];
+    bulk_g2s(stage + lane * it.RBc * 16 * it.RS, wm + (size_t)it.r0 * wbytes,
+             (uint32_t)it.rows * wbytes, full, policy);
   }
   if (it.scale_bulk && lane < it.mats) {
     const uint16_t* sm = lane ? it.s[1] : it.s[0];
@@ -723,14 +721,20 @@ static int check_group(int64_t K, int64_t group, int* gshift) {
   return KB_OK;
 }
 
-// Warp split for a reduction width: KS warps share a 16-row block, each
-// covering at least four 128-wide blocks when possible; RBc row blocks per
-// item so that mats * RBc * KS == NCW.
-static void choose_split(int K, int mats, int* KS, int* RBc) {
+// Warp split for a reduction width: KS warps share a 16-row block and RBc row
+// blocks make an item, mats * RBc * KS == NCW.  KS starts where every warp
+// covers at least four 128-wide blocks; while the problem yields fewer than
+// two items per SM it doubles (smaller items), as long as each warp keeps two
+// blocks.  `row_blocks` is the number of 16-row blocks of all matrices the
+// launch covers.
+static void choose_split(int K, int mats, int64_t row_blocks, int sms, int* KS, int* RBc) {
   const int KB = (K + 127) / 128;
   const int maxks = NCW / mats;
   int ks = 1;
   while (ks * 2 <= maxks && KB / (ks * 2) >= 4) ks *= 2;
+  while (ks * 2 <= maxks && KB / (ks * 2) >= 2 &&
+         row_blocks / (maxks / ks) < 2 * (int64_t)sms)
+    ks *= 2;
   *KS = ks;
   *RBc = maxks / ks;
 }
@@ -823,12 +827,18 @@ static int dense_multi_impl(const kb_dense_problem* probs, int count, void* stre
     D.K = (int)q.K;
     D.N = (int)q.N;
     D.gshift = gs;
-    choose_split(D.K, 1, &D.KS, &D.RBc);
     maxM = std::max(maxM, D.M);
     maxK = std::max(maxK, D.K);
     P.nprob++;
   }
   if (P.nprob == 0) return KB_OK;
+  {
+    int64_t row_blocks = 0;
+    for (int i = 0; i < P.nprob; ++i) row_blocks += (P.prob[i].N + 15) / 16;
+    const int sms = num_sms(bind_stream_device(stream));
+    for (int i = 0; i < P.nprob; ++i)
+      choose_split(P.prob[i].K, 1, row_blocks, sms, &P.prob[i].KS, &P.prob[i].RBc);
+  }
   const int nsub = (maxM > 8) ? 2 : 1;
   P.tok_cap = 8 * nsub;
   P.tstride = token_stride(maxK);
@@ -926,7 +936,9 @@ static int grouped_impl(int mode, const uint16_t* x, int64_t x_stride, int64_t T
   G.E = (int)E;
   G.gshift = gs;
   const int mats = (mode == MODE_SWIGLU) ? 2 : 1;
-  choose_split(G.K, mats, &G.KS, &G.RBc);
+  const int64_t slots = std::min<int64_t>(E, T * R);
+  choose_split(G.K, mats, slots * ((N + 15) / 16), num_sms(bind_stream_device(stream)), &G.KS,
+               &G.RBc);
   G.items_rb = (G.N + 16 * G.RBc - 1) / (16 * G.RBc);
   if (mode == MODE_W2C) {
     KB_REQUIRE(out && cw, KB_ERR_NULL_POINTER, "NULL output or weights pointer");
