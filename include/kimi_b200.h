@@ -179,6 +179,26 @@ KB_API int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t T, i
                    size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* Router without a caller workspace.  No counterpart in the reference: this   */
+/* is an addition of this library for callers that cannot allocate device      */
+/* memory (a host binding the C ABI without a device allocator, or a serving   */
+/* loop that must not call cudaMalloc between steps, since cudaMalloc can      */
+/* synchronise the device and fail under memory pressure).  Same arguments and */
+/* results as kb_router_topk minus the workspace; it allocates nothing.  Its   */
+/* scratch is one fixed device array per device, kb_router_static_scratch_bytes*/
+/* bytes (528 KiB), which limits T*E to 131072 (e.g. T <= 512 at E = 256);     */
+/* larger calls return KB_ERR_WORKSPACE.  The first call on each device does a */
+/* one-time set-up with that device current (symbol lookup, counter clear on   */
+/* the given stream): make it before any stream capture.  Calls that overlap   */
+/* in time on one device share the scratch and race: serialise them.          */
+/* ------------------------------------------------------------------------- */
+KB_API size_t kb_router_static_scratch_bytes(void);
+KB_API int kb_router_topk_static(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t K,
+                   const uint16_t* weight, const float* bias, int64_t E,
+                   int64_t top_k, int renormalize, float scaling,
+                   int64_t* idx_out, int64_t append_id, float* w_out, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* KDA recurrent decode step.  Replaces kda_decode_step                        */
 /* (engine/kernels/kda_step.py:273-293, reference :173-196).  fp32 throughout: */
 /*   S' = S * exp(decay)[:,None];  p = S'^T k;  d = v - p;                      */

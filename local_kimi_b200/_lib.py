@@ -86,6 +86,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
          c_float, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p],
     ),
+    "kb_router_static_scratch_bytes": (c_size_t, []),
+    "kb_router_topk_static": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+         c_float, c_void_p, c_int64, c_void_p, c_void_p],
+    ),
     "kb_kda_decode_step": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

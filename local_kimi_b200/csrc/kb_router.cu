@@ -20,6 +20,7 @@
 #include "kb_common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace kb {
 
@@ -312,6 +313,114 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
                          (int)(kb::RT_TOK * 8192 * sizeof(uint16_t)));
     attr_done = true;
   }
+  return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,
+                    h_stride, (int)T, (int)K, weight, bias, (int)E, (int)top_k, renormalize,
+                    scaling, idx_out, append_id, w_out, logits, counters);
+}
+
+// ---------------------------------------------------------------------------
+// kb_router_topk_static: the router with its scratch in a fixed device array.
+//
+// For callers that cannot allocate device memory: a host that binds the C ABI
+// without a device allocator of its own, or a serving loop that must not call
+// cudaMalloc between steps (cudaMalloc can synchronise the device and can fail
+// under memory pressure).  This entry point calls no allocating routine; its
+// scratch is the file-scope array below, one copy per device.
+//
+// Layout of the scratch: arrival counters first, at a fixed offset, so calls of
+// any shape find them where the previous call left them; logits after them.
+// The counters must start at zero: device storage without an initialiser is
+// zero-filled when the module loads, the set-up clears them once more on the
+// caller's stream, and every launch returns them to zero.  The logits need no
+// initial value (each launch writes them before it reads them).
+//
+// The first call on each device does the set-up (symbol address, dynamic
+// shared-memory limit, counter clear) with that device current; make that first
+// call before any stream capture.  All calls on one device share the one
+// scratch array, so calls that overlap in time on that device (other streams,
+// other host threads) race and give wrong results: serialise them.
+// ---------------------------------------------------------------------------
+namespace kb {
+
+constexpr size_t RT_STATIC_COUNTERS = 1024;                          // token blocks (T <= 8192)
+constexpr size_t RT_STATIC_LOGITS = 131072;                          // T * E floats (512 KiB)
+constexpr size_t RT_STATIC_COUNTER_BYTES = RT_STATIC_COUNTERS * sizeof(int);
+constexpr size_t RT_STATIC_BYTES =
+    RT_STATIC_COUNTER_BYTES + RT_STATIC_LOGITS * sizeof(float);      // 528 KiB
+
+static __device__ __align__(256) uint8_t g_router_static_scratch[RT_STATIC_BYTES];
+
+constexpr int RT_STATIC_MAX_DEVICES = 64;
+static std::mutex g_router_static_mu;
+static void* g_router_static_ptr[RT_STATIC_MAX_DEVICES] = {};
+
+// Per-device set-up; returns the scratch address on the current device or NULL
+// after recording the error.
+static void* router_static_scratch(int* status, cudaStream_t stream) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= RT_STATIC_MAX_DEVICES) {
+    set_error("router (static scratch): no usable current device (%s)", cudaGetErrorString(e));
+    *status = KB_ERR_DEVICE;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_router_static_mu);
+  if (g_router_static_ptr[dev]) return g_router_static_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_router_static_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_error("router (static scratch): cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    *status = KB_ERR_DEVICE;
+    return nullptr;
+  }
+  e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(RT_TOK * 8192 * sizeof(uint16_t)));
+  if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, RT_STATIC_COUNTER_BYTES, stream);
+  if (e != cudaSuccess) {
+    set_error("router (static scratch): set-up failed: %s", cudaGetErrorString(e));
+    *status = KB_ERR_DEVICE;
+    return nullptr;
+  }
+  g_router_static_ptr[dev] = p;
+  return p;
+}
+
+}  // namespace kb
+
+extern "C" size_t kb_router_static_scratch_bytes(void) { return kb::RT_STATIC_BYTES; }
+
+extern "C" int kb_router_topk_static(const uint16_t* hidden, int64_t h_stride, int64_t T,
+                                     int64_t K, const uint16_t* weight, const float* bias,
+                                     int64_t E, int64_t top_k, int renormalize, float scaling,
+                                     int64_t* idx_out, int64_t append_id, float* w_out,
+                                     void* stream) {
+  kb::clear_error();
+  KB_REQUIRE(T >= 0 && K > 0 && E > 0 && top_k > 0, KB_ERR_BAD_SHAPE,
+             "router needs T >= 0 and K, E, top_k > 0");
+  KB_REQUIRE(top_k <= E, KB_ERR_BAD_SHAPE, "top_k %lld exceeds E %lld", (long long)top_k,
+             (long long)E);
+  KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 8192 && K % 8 == 0, KB_ERR_UNSUPPORTED,
+             "router supports E <= 1024, top_k <= 32, K <= 8192 with K %% 8 == 0");
+  KB_REQUIRE((size_t)T * (size_t)E <= kb::RT_STATIC_LOGITS &&
+                 (size_t)(T + kb::RT_TOK - 1) / kb::RT_TOK <= kb::RT_STATIC_COUNTERS,
+             KB_ERR_WORKSPACE,
+             "router (static scratch): T*E = %lld exceeds the fixed scratch of %zu logits; "
+             "use kb_router_topk with a caller workspace",
+             (long long)(T * E), kb::RT_STATIC_LOGITS);
+  if (T == 0) return KB_OK;
+  KB_REQUIRE(hidden && weight && idx_out && w_out, KB_ERR_NULL_POINTER, "NULL router pointer");
+  KB_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0 && h_stride % 8 == 0 &&
+                 reinterpret_cast<uintptr_t>(weight) % 16 == 0,
+             KB_ERR_ALIGNMENT, "hidden/weight must be 16-byte aligned with row stride %% 8 == 0");
+  int status = KB_OK;
+  void* scratch = kb::router_static_scratch(&status, static_cast<cudaStream_t>(stream));
+  if (!scratch) return status;
+  int* counters = reinterpret_cast<int*>(scratch);
+  float* logits =
+      reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kb::RT_STATIC_COUNTER_BYTES);
+  const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
+                  (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
+  const size_t smem = (size_t)std::min<int64_t>(T, kb::RT_TOK) * K * sizeof(uint16_t);
   return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,
                     h_stride, (int)T, (int)K, weight, bias, (int)E, (int)top_k, renormalize,
                     scaling, idx_out, append_id, w_out, logits, counters);
