@@ -58,6 +58,10 @@ def _args() -> argparse.Namespace:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--case", choices=("step", "lm_head", "moe", "eager"), default="step",
+                    help="step = the benchmark; the others run one op family eagerly for "
+                         "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
+                         "combine of one layer; eager: uncaptured decode steps)")
     return ap.parse_args()
 
 
@@ -526,9 +530,67 @@ def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
+def run_case(args) -> dict:
+    """One op family at full shape, launched eagerly K times after W warm-ups
+    (for profilers: every launch is a separate kernel, no graph)."""
+    import __graft_entry__ as entry
+
+    entry.build()
+    from local_kimi_b200 import _lib, ops
+    from local_kimi_b200.decode import HotPathDecoder, KimiLinearShape
+    from local_kimi_b200.moe import moe_forward
+
+    _lib.set_pdl(not args.no_pdl)
+    s = KimiLinearShape()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    x = torch.randn((args.batch, s.hidden), generator=gen, device="cuda").to(torch.bfloat16)
+    if args.case == "lm_head":
+        w = (torch.randn((s.vocab_size, s.hidden), generator=gen, device="cuda") * 0.02)
+        packed, scales = ops.quantise(w.to(torch.bfloat16), args.group)
+        del w
+        fn = lambda: ops.w4a16_dense(x, packed, scales)  # noqa: E731
+        nbytes = packed.numel() + scales.numel() * 2
+        per_step = 1
+    elif args.case == "moe":
+        model = HotPathDecoder(args.batch, group=args.group, layers=2)
+        layer = model.layers[1].moe
+        fn = lambda: moe_forward(x, layer)  # noqa: E731
+        nbytes = None
+        per_step = 3
+    else:
+        model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
+        fn = lambda: model.step(x)  # noqa: E731
+        nbytes = None
+        per_step = model.launches_per_step
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    t = start.elapsed_time(end) / 1e3 / args.steps
+    out = {"case": args.case, "batch": args.batch, "group_size": args.group,
+           "steps": args.steps, "warmup": args.warmup, "launches_per_iteration": per_step,
+           "us_per_iteration": round(t * 1e6, 2)}
+    if args.case == "eager":
+        nbytes = model.step_bytes(model.touched_experts(x))["total"]
+    if nbytes:
+        out["bytes_per_iteration"] = nbytes
+        out["gbs"] = round(nbytes / t / 1e9, 1)
+    return out
+
+
 def main() -> None:
     args = _args()
     rank, world, local_rank = _dist_env()
+    if args.case != "step":
+        if rank == 0:
+            print(json.dumps(run_case(args)), flush=True)
+        return
     if args.impl == "reference":
         out = run_reference(args, rank, world, local_rank)
     else:

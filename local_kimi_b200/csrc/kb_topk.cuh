@@ -1,0 +1,110 @@
+// kb_topk.cuh - warp-wide biased top-k selection of the sigmoid router,
+// shared by the router kernel (kb_router.cu) and the decode-step executor
+// (kb_step.cu).  Reference: engine/klinear/router.py:47-85.
+#pragma once
+
+#include "kb_common.cuh"
+
+namespace kb {
+
+// Order-preserving map of a choice score to uint32 (larger is better); NaN
+// maps to 0, below every number, and -0 is folded into +0.
+__device__ __forceinline__ uint32_t choice_key(float x) {
+  if (x != x) return 0u;
+  const uint32_t b = __float_as_uint(x + 0.0f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ bool choice_better(uint32_t ka, int ia, uint32_t kb, int ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+template <int N>
+__device__ __forceinline__ void cswap(uint32_t (&k)[N], int (&id)[N], float (&sc)[N], int i,
+                                      int j) {
+  if (choice_better(k[j], id[j], k[i], id[i])) {
+    const uint32_t tk = k[i];
+    k[i] = k[j];
+    k[j] = tk;
+    const int ti = id[i];
+    id[i] = id[j];
+    id[j] = ti;
+    const float ts = sc[i];
+    sc[i] = sc[j];
+    sc[j] = ts;
+  }
+}
+
+// Top-k of one token over E <= 256 experts, one warp.  lrow holds the fp32
+// logits (read with L2-only loads: another CTA may have written them in the
+// same kernel).  scores = sigmoid(logit); choice = score + bias; the k picks
+// are made in (choice desc, index asc) order.  Lane r < top_k receives pick r
+// (my_idx, my_score = unbiased score); every lane receives wsum, the sum of
+// the picked scores in pick order.
+__device__ __forceinline__ void warp_topk256(const float* lrow, const float* bias, int E,
+                                             int top_k, int lane, int& my_idx, float& my_score,
+                                             float& wsum) {
+  uint32_t key[8];
+  int id[8];
+  float sc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) {
+      const float lg = __ldcg(&lrow[e]);
+      sc[j] = 1.0f / (1.0f + expf(-lg));
+      key[j] = choice_key(sc[j] + (bias ? bias[e] : 0.f));
+      id[j] = e;
+    } else {
+      sc[j] = 0.f;
+      key[j] = 0u;
+      id[j] = 0x7fffffff;
+    }
+  }
+  // Sort descending by (key, -index): optimal 19-comparator network.
+  cswap(key, id, sc, 0, 2);
+  cswap(key, id, sc, 1, 3);
+  cswap(key, id, sc, 4, 6);
+  cswap(key, id, sc, 5, 7);
+  cswap(key, id, sc, 0, 4);
+  cswap(key, id, sc, 1, 5);
+  cswap(key, id, sc, 2, 6);
+  cswap(key, id, sc, 3, 7);
+  cswap(key, id, sc, 0, 1);
+  cswap(key, id, sc, 2, 3);
+  cswap(key, id, sc, 4, 5);
+  cswap(key, id, sc, 6, 7);
+  cswap(key, id, sc, 2, 4);
+  cswap(key, id, sc, 3, 5);
+  cswap(key, id, sc, 1, 4);
+  cswap(key, id, sc, 3, 6);
+  cswap(key, id, sc, 1, 2);
+  cswap(key, id, sc, 3, 4);
+  cswap(key, id, sc, 5, 6);
+  for (int sel = 0; sel < top_k; ++sel) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+    const uint32_t cand = (key[0] == best) ? (uint32_t)id[0] : 0xffffffffu;
+    const int win = (int)__reduce_min_sync(0xffffffffu, cand);
+    float s = 0.f;
+    if (id[0] == win) {
+      s = sc[0];
+#pragma unroll
+      for (int j = 0; j < 7; ++j) {
+        key[j] = key[j + 1];
+        id[j] = id[j + 1];
+        sc[j] = sc[j + 1];
+      }
+      key[7] = 0u;
+      id[7] = 0x7fffffff;
+      sc[7] = 0.f;
+    }
+    s = __shfl_sync(0xffffffffu, s, win & 31);
+    wsum += s;
+    if (lane == sel) {
+      my_score = s;
+      my_idx = win;
+    }
+  }
+}
+
+}  // namespace kb
