@@ -213,6 +213,68 @@ KB_API int kb_kda_decode_step(float* state, int64_t sb, int64_t sh, int64_t sk,
                        int64_t H, int64_t Dk, int64_t Dv, float scale,
                        float* out, uint16_t* out_bf16, void* stream);
 
+/* ------------------------------------------------------------------------- */
+/* Decode-step executor.  Runs a whole program of the operations above in one  */
+/* persistent launch (one CTA per SM): the weight stream of every operation    */
+/* runs ahead of the dependencies between operations, which are enforced with */
+/* device completion counters.  It replaces the sequence of registry calls of  */
+/* one decode step of the reference (engine/klinear/model.py:134-160 calling   */
+/* the layers of engine/klinear/layers.py, captured as one CUDA graph by       */
+/* engine/klinear/generate.py:226-276) for the operations of the hot path.     */
+/* Every pointer is bound when the operation is added (the same static buffers */
+/* a captured graph uses); each kb_step_launch runs the whole program.         */
+/* An operation's consumers wait for the operations listed in deps before      */
+/* they read their inputs; list every earlier operation that writes an input  */
+/* or that reads a buffer the operation writes.  Results equal the            */
+/* per-operation entry points up to fp32 summation order (router logits, KDA   */
+/* partials).  Limits: 1 <= tokens <= KB_STEP_MAX_TOKENS, K % 128 == 0, E <=   */
+/* 256, top_k <= 8, Dk <= 128.  kb_step_finalize uploads the program           */
+/* (allocates device memory) on the current device.                           */
+/* ------------------------------------------------------------------------- */
+#define KB_STEP_MAX_TOKENS 8
+#define KB_STEP_MAX_DEPS 4
+typedef struct kb_step kb_step;
+KB_API int kb_step_create(int64_t tokens, kb_step** out);
+KB_API void kb_step_destroy(kb_step* step);
+/* One to three INT4 projections of the same tokens (problem M == tokens). */
+KB_API int kb_step_add_dense(kb_step* step, const kb_dense_problem* problems, int count,
+                   const int* deps, int ndeps, int* op_out);
+/* Dense gate/up + SwiGLU: y = bf16(silu(bf16 x.w1^T)) * bf16(x.w3^T).       */
+KB_API int kb_step_add_swiglu(kb_step* step, const uint16_t* x, int64_t x_stride, int64_t K,
+                   const uint8_t* w1_packed, const uint16_t* w1_scales,
+                   const uint8_t* w3_packed, const uint16_t* w3_scales, int64_t N,
+                   int64_t group, uint16_t* y, int64_t y_stride, const int* deps,
+                   int ndeps, int* op_out);
+/* Router logits; the selection runs in the expert operation that uses it.   */
+/* logits fp32 [tokens, E] scratch; idx_out int64 [tokens, top_k+1] (shared  */
+/* expert id E appended), w_out fp32 [tokens, top_k].                         */
+KB_API int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride,
+                   int64_t K, const uint16_t* weight, const float* bias, int64_t E,
+                   int64_t top_k, int renormalize, float scaling, float* logits,
+                   int64_t* idx_out, float* w_out, const int* deps, int ndeps,
+                   int* op_out);
+/* Expert block of one MoE layer on banks [E+1, ...] (slot E = shared expert):*/
+/* gate/up + SwiGLU into activated [tokens*(top_k+1), I], down projection of  */
+/* every route into routed_out [tokens*(top_k+1), H], combine into out        */
+/* [tokens, H].  op_out receives the index of the down/combine operation,     */
+/* the one later operations depend on.                                        */
+KB_API int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden,
+                   int64_t h_stride, int64_t H, const uint8_t* w1_packed,
+                   const uint16_t* w1_scales, const uint8_t* w3_packed,
+                   const uint16_t* w3_scales, const uint8_t* w2_packed,
+                   const uint16_t* w2_scales, int64_t I, int64_t group,
+                   uint16_t* activated, uint16_t* routed_out, uint16_t* out,
+                   const int* deps, int ndeps, int* op_out);
+KB_API int kb_step_add_kda(kb_step* step, float* state, int64_t sb, int64_t sh, int64_t sk,
+                   const float* q, const float* k, const float* v, const float* decay,
+                   const float* beta, int64_t B, int64_t H, int64_t Dk, int64_t Dv,
+                   float scale, float* out, uint16_t* out_bf16, const int* deps,
+                   int ndeps, int* op_out);
+KB_API int kb_step_finalize(kb_step* step);
+KB_API int kb_step_launch(kb_step* step, void* stream);
+KB_API int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage_bytes,
+                   size_t* smem_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,41 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
          c_float, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "kb_step_create": (c_int, [c_int64, ctypes.POINTER(c_void_p)]),
+    "kb_step_destroy": (None, [c_void_p]),
+    "kb_step_add_dense": (
+        c_int,
+        [c_void_p, ctypes.POINTER(DenseProblem), c_int, c_void_p, c_int, ctypes.POINTER(c_int)],
+    ),
+    "kb_step_add_swiglu": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+         c_int64, c_void_p, c_int64, c_void_p, c_int, ctypes.POINTER(c_int)],
+    ),
+    "kb_step_add_router": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+         c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, ctypes.POINTER(c_int)],
+    ),
+    "kb_step_add_moe": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+         ctypes.POINTER(c_int)],
+    ),
+    "kb_step_add_kda": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p,
+         c_int, ctypes.POINTER(c_int)],
+    ),
+    "kb_step_finalize": (c_int, [c_void_p]),
+    "kb_step_launch": (c_int, [c_void_p, c_void_p]),
+    "kb_step_info": (
+        c_int,
+        [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+         ctypes.POINTER(c_size_t)],
+    ),
     "kb_kda_decode_step": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

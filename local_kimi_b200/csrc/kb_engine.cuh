@@ -242,7 +242,7 @@ inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
 
-inline int token_stride(int K) {
+__host__ __device__ inline int token_stride(int K) {
   const int bytes = 2 * K;
   const int pad = (64 - (bytes % 128) + 128) % 128;
   return bytes + pad;

@@ -1,0 +1,1615 @@
+// kb_step.cu - decode-step executor for sm_100a: one persistent launch runs a
+// whole program of hot-path operations.
+//
+// A decode step of the hot path is ~150 dependent operations (per layer: the
+// attention projections, the KDA state step, the router, the expert gate/up
+// and down+combine; then the lm_head), each of which moves a few MB.  Issued
+// as separate kernels every operation pays launch, ramp-up, DRAM latency and
+// drain (several microseconds) although its data takes well under one at HBM
+// rate.  This executor keeps one CTA per SM resident for the whole step:
+//
+//  * The producer warp of every CTA walks the program and streams the weights
+//    of every item assigned to its CTA (plain cp.async.bulk, L2 evict-first)
+//    into a ring of shared-memory stages, as far ahead as the ring allows.
+//    Weights never depend on the step's activations, so the stream runs across
+//    the dependencies between operations; only the routed experts wait for
+//    the routing of their layer.
+//  * The consumer warps walk the same program.  Before an operation reads its
+//    inputs they wait on device completion counters of the operations that
+//    produce them (published with a release fence + atomic add by the warps
+//    that wrote them, observed with acquire loads; every wait is bounded in
+//    time and a shared abort flag ends the launch on any failure).
+//  * Item arithmetic is the projection engine's (kb_engine.cuh): bf16(code *
+//    scale) decode, mma.sync m16n8k16, fp32 sums in a fixed order.
+//
+// Operations: OP_DENSE (up to three INT4 projections), OP_ROUTER (fp32 router
+// logits of eight experts per item), OP_MOE_UP (top-k selection and expert
+// plan, then gate/up + SwiGLU of the shared expert and the routed experts),
+// OP_MOE_DOWN (down projection of every route, then the weighted combine by
+// the CTA that completes a (token, row group)), OP_KDA (recurrent state step).
+// Results equal those of the per-operation kernels up to fp32 summation order
+// (KDA row partials, router logits).
+//
+// Reference semantics: engine/kernels/w4a16_gemv.py:56-174 (decode and
+// projections), engine/kernels/__init__.py:182-218 (SwiGLU contract),
+// engine/klinear/router.py:47-85 (router), engine/klinear/moe.py:278-334 and
+// engine/kernels/moe_combine.py:209-261 (expert dispatch and combine),
+// engine/kernels/kda_step.py:173-196 (KDA step).
+#include "kb_engine.cuh"
+#include "kb_topk.cuh"
+
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+namespace kb {
+
+enum : int { OP_DENSE = 0, OP_ROUTER = 1, OP_MOE_UP = 2, OP_MOE_DOWN = 3, OP_KDA = 4 };
+
+constexpr int ST_MAX_DEPS = KB_STEP_MAX_DEPS;
+constexpr int ST_MAX_PROB = 3;
+constexpr int ST_MAX_T = KB_STEP_MAX_TOKENS;
+constexpr int ST_MAX_TOPK = 8;
+constexpr int ST_MAX_R = ST_MAX_TOPK + 1;
+constexpr int ST_MAX_E = 256;
+constexpr int ST_MAX_SLOTS = 1 + ST_MAX_T * ST_MAX_TOPK;
+constexpr int ST_RT_EXPERTS = 8;          // router experts per item (two warps each)
+constexpr int ST_KDA_COLS = 32;
+constexpr int ST_STAGE_TARGET = 40 * 1024;  // preferred bytes per item
+constexpr long long ST_WAIT_NS = 2000000000LL;  // 2 s per wait
+
+struct StDense {
+  const uint16_t* x;
+  int64_t xs;
+  const uint8_t* w;
+  const uint16_t* s;
+  const uint8_t* w3;   // gate/up pair: up matrix (mats == 2), SwiGLU epilogue
+  const uint16_t* s3;
+  uint16_t* y;
+  int64_t ys;
+  int K, N, gshift, KS, RBc, nchunk, mats;
+  int items, item_begin, x_off;
+};
+
+struct StOp {
+  int type;
+  int ndeps;
+  int dep[ST_MAX_DEPS];
+  int done;    // sync index of the completion counter
+  int target;  // completion count (every op but OP_MOE_UP)
+  int rot;     // item i runs on CTA (i + rot) % grid
+  int T;
+  int items;   // static items (dense, router, KDA)
+  // dense
+  int nprob;
+  StDense p[ST_MAX_PROB];
+  // router
+  const uint16_t* rx;
+  int64_t rxs;
+  const uint16_t* rw;
+  const float* rbias;
+  int E, K, top_k, renorm;
+  float scaling;
+  float* logits;
+  int64_t* idx_out;
+  float* w_out;
+  // experts (up and down)
+  int router_op;
+  int slot_cnt;  // sync index of the up op's per-slot counters
+  int arrive;    // down: sync index of the (token, row group) arrival counters
+  const uint16_t* mx;
+  int64_t mxs;
+  const uint8_t* w0;
+  const uint16_t* s0;
+  const uint8_t* w1;
+  const uint16_t* s1;
+  int64_t wse, sse;
+  int N, gshift, KS, RBc, items_rb, R, up_rb;
+  uint16_t* y;
+  uint16_t* out;
+  uint16_t* wsy;
+  // KDA
+  float* state;
+  int64_t sb, sh, sk;
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* decay;
+  const float* beta;
+  int B, H, Dk, Dv;
+  float scale;
+  float* kout;
+  uint16_t* kout_bf16;
+};
+
+struct StepParams {
+  const StOp* ops;
+  int nops;
+  int* sync;
+  int nsync;
+  int exit_idx, abort_idx;
+  uint32_t* err;
+  int stages, stage_bytes;
+  int ring_off, red_off, scr_off, bar_off;
+  int tstride_max;
+};
+
+// Per-CTA routing state and plan (shared memory scratch).
+struct StPlan {
+  int route_e[ST_MAX_T * ST_MAX_R];     // expert of assignment t*R + r
+  float route_w[ST_MAX_T * ST_MAX_TOPK];
+  int slot_expert[ST_MAX_SLOTS];
+  int slot_start[ST_MAX_SLOTS + 1];
+  int assign[ST_MAX_T * ST_MAX_R];
+  int slot_id[ST_MAX_T * ST_MAX_TOPK];
+  int slot_of[ST_MAX_E + 1];
+  int nslots;
+  int done_tok[ST_MAX_T];
+  int abort;
+  int last;
+};
+
+struct StKda {
+  float ed[256], k[256], bk[256], q[256];
+  float red[NCW][32];
+};
+
+// ---------------------------------------------------------------------------
+// Device-side synchronisation.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ long long now_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void raise_abort(const StepParams& P, StPlan* pl, uint32_t bits) {
+  atomicOr(P.err, bits);
+  atomicExch(&P.sync[P.abort_idx], 1);
+  pl->abort = 1;
+}
+
+// Thread 0 of the consumers waits until sync[idx] >= target (bounded), then
+// all consumers pass a barrier.  Consumers never leave the common sequence of
+// barriers early: after a failure every later wait returns at once and the
+// launch runs to its end with the error recorded.
+__device__ void consumers_wait(const StepParams& P, StPlan* pl, int idx, int target) {
+  if (threadIdx.x == 0 && !pl->abort && target > 0) {
+    const long long t0 = now_ns();
+    int spins = 0;
+    while (ld_acquire(&P.sync[idx]) < target) {
+      if (((++spins) & 15) == 0) {
+        if (*((volatile int*)&P.sync[P.abort_idx]) != 0) {
+          pl->abort = 1;
+          break;
+        }
+        if (now_ns() - t0 > ST_WAIT_NS) {
+          raise_abort(P, pl, ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  named_barrier(CBAR, NCT);
+}
+
+__device__ void wait_deps(const StepParams& P, StPlan* pl, const StOp& op) {
+  for (int d = 0; d < op.ndeps; ++d) {
+    const StOp& dop = P.ops[op.dep[d]];
+    consumers_wait(P, pl, dop.done, dop.target);
+  }
+  if (op.ndeps == 0) named_barrier(CBAR, NCT);
+}
+
+// Release: the writes of this warp (ordered by __syncwarp) before the add.
+__device__ __forceinline__ void warp_signal(int* counter, int v) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    __threadfence();
+    atomicAdd(counter, v);
+  }
+}
+
+// Bounded mbarrier wait that also gives up when the CTA is aborting.
+__device__ bool stage_wait(uint64_t* bar, uint32_t parity, const StPlan* pl) {
+  const long long t0 = now_ns();
+  int spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (((++spins) & 15) == 0) {
+      if (*((volatile const int*)&pl->abort) != 0) return false;
+      if (now_ns() - t0 > ST_WAIT_NS) return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ int first_item(int rot) {
+  const int G = gridDim.x;
+  return ((int)blockIdx.x - rot % G + G) % G;
+}
+
+// Activation row into the B-fragment layout, read with L2-only loads (the row
+// may have been written by another CTA of this launch).
+__device__ __forceinline__ void stage_row_cg(uint8_t* xs_row, const uint16_t* src, int K,
+                                             int first, int step) {
+  const int NC = K >> 5;
+  const int words = K >> 3;
+  for (int w = first; w < words; w += step) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + w);
+    const int c = w >> 2, j = w & 3;
+    *reinterpret_cast<uint4*>(xs_row + (j * NC + c) * 16) = permute_pairs(v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Item descriptions (identical on the producer and consumer side).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_describe_dense(const StOp& op, int item, Item& it) {
+  int p = 0;
+  while (p + 1 < op.nprob && item >= op.p[p + 1].item_begin) ++p;
+  const StDense& D = op.p[p];
+  const int rbg = item - D.item_begin;
+  it.mats = D.mats;
+  it.w[0] = D.w;
+  it.s[0] = D.s;
+  it.w[1] = D.w3;
+  it.s[1] = D.s3;
+  it.K = D.K;
+  it.N = D.N;
+  it.gshift = D.gshift;
+  it.KS = D.KS;
+  it.RBc = D.RBc;
+  it.r0 = rbg * D.RBc * 16;
+  it.rows = min(D.RBc * 16, D.N - it.r0);
+  it.ng = D.K >> (5 + D.gshift);
+  it.RS = (D.nchunk > 1) ? D.K / (2 * D.nchunk) : row_stride_bytes(D.K);
+  it.scale_bulk = D.nchunk == 1 && scale_bulk_ok(D.s, it.r0, it.rows, it.ng) &&
+                  (D.mats == 1 || scale_bulk_ok(D.s3, it.r0, it.rows, it.ng));
+  it.p = p;
+  it.abase = 0;
+  it.count = op.T;
+}
+
+// Slot s of the plan: expert slot_expert[s], assignments assign[start..end).
+__device__ __forceinline__ void st_describe_moe(const StOp& op, const StPlan* pl, int item,
+                                                Item& it) {
+  const int slot = item / op.items_rb;
+  const int rbg = item - slot * op.items_rb;
+  const int e = pl->slot_expert[slot];
+  it.mats = (op.type == OP_MOE_UP) ? 2 : 1;
+  it.w[0] = op.w0 + (size_t)e * (size_t)op.wse;
+  it.s[0] = op.s0 + (size_t)e * (size_t)op.sse;
+  it.w[1] = (it.mats == 2) ? op.w1 + (size_t)e * (size_t)op.wse : nullptr;
+  it.s[1] = (it.mats == 2) ? op.s1 + (size_t)e * (size_t)op.sse : nullptr;
+  it.K = op.K;
+  it.N = op.N;
+  it.gshift = op.gshift;
+  it.KS = op.KS;
+  it.RBc = op.RBc;
+  it.r0 = rbg * op.RBc * 16;
+  it.rows = min(op.RBc * 16, op.N - it.r0);
+  it.RS = row_stride_bytes(op.K);
+  it.ng = op.K >> (5 + op.gshift);
+  it.scale_bulk = scale_bulk_ok(it.s[0], it.r0, it.rows, it.ng) &&
+                  (it.mats == 1 || scale_bulk_ok(it.s[1], it.r0, it.rows, it.ng));
+  it.p = slot;
+  it.abase = pl->slot_start[slot];
+  it.count = pl->slot_start[slot + 1] - it.abase;
+}
+
+// Shared slot 0 (the shared expert, every token) before the plan exists.
+__device__ __forceinline__ void st_describe_shared(const StOp& op, int item, Item& it) {
+  const int rbg = item;
+  const int e = op.E;
+  it.mats = (op.type == OP_MOE_UP) ? 2 : 1;
+  it.w[0] = op.w0 + (size_t)e * (size_t)op.wse;
+  it.s[0] = op.s0 + (size_t)e * (size_t)op.sse;
+  it.w[1] = (it.mats == 2) ? op.w1 + (size_t)e * (size_t)op.wse : nullptr;
+  it.s[1] = (it.mats == 2) ? op.s1 + (size_t)e * (size_t)op.sse : nullptr;
+  it.K = op.K;
+  it.N = op.N;
+  it.gshift = op.gshift;
+  it.KS = op.KS;
+  it.RBc = op.RBc;
+  it.r0 = rbg * op.RBc * 16;
+  it.rows = min(op.RBc * 16, op.N - it.r0);
+  it.RS = row_stride_bytes(op.K);
+  it.ng = op.K >> (5 + op.gshift);
+  it.scale_bulk = scale_bulk_ok(it.s[0], it.r0, it.rows, it.ng) &&
+                  (it.mats == 1 || scale_bulk_ok(it.s[1], it.r0, it.rows, it.ng));
+  it.p = 0;
+  it.abase = 0;
+  it.count = op.T;
+}
+
+// One reduction chunk of a chunked dense item: rows copied one by one.
+__device__ __forceinline__ void produce_chunk(const Item& it, int nchunk, int ci, uint8_t* stage,
+                                              uint64_t* full, uint64_t policy) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t cbytes = (uint32_t)(it.K / (2 * nchunk));
+  if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)it.rows * cbytes);
+  __syncwarp();
+  for (int r = lane; r < it.rows; r += 32)
+    bulk_g2s(stage + (size_t)r * cbytes,
+             it.w[0] + (size_t)(it.r0 + r) * (it.K / 2) + (size_t)ci * cbytes, cbytes, full,
+             policy);
+}
+
+// ---------------------------------------------------------------------------
+// Producer warp.
+// ---------------------------------------------------------------------------
+struct Ring {
+  uint8_t* base;
+  uint64_t* full;
+  uint64_t* empty;
+  int stages, stage_bytes;
+  int use;
+};
+
+__device__ bool ring_acquire(Ring& R, const StPlan* pl, uint8_t** stage, uint64_t** full) {
+  const int s = R.use % R.stages;
+  const uint32_t ph = (R.use / R.stages) & 1;
+  if (!stage_wait(&R.empty[s], ph ^ 1, pl)) return false;
+  *stage = R.base + (size_t)s * R.stage_bytes;
+  *full = &R.full[s];
+  ++R.use;
+  return true;
+}
+
+__device__ void producer_main(const StepParams& P, StPlan* pl, Ring& R, uint64_t* plan_bar,
+                              uint64_t* plan_ack) {
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const uint64_t pol = l2_evict_first_policy();
+  uint32_t plan_phase = 0;
+  bool ok = true;
+  for (int o = 0; o < P.nops && ok; ++o) {
+    const StOp& op = P.ops[o];
+    uint8_t* stage;
+    uint64_t* full;
+    if (op.type == OP_DENSE) {
+      const int n = op.p[op.nprob - 1].item_begin + op.p[op.nprob - 1].items;
+      for (int i = first_item(op.rot); i < n && ok; i += G) {
+        Item it;
+        st_describe_dense(op, i, it);
+        const int nchunk = op.p[it.p].nchunk;
+        for (int ci = 0; ci < nchunk && ok; ++ci) {
+          ok = ring_acquire(R, pl, &stage, &full);
+          if (!ok) break;
+          if (nchunk == 1)
+            produce_item(it, stage, full, pol);
+          else
+            produce_chunk(it, nchunk, ci, stage, full, pol);
+        }
+      }
+    } else if (op.type == OP_ROUTER) {
+      for (int i = first_item(op.rot); i < op.items && ok; i += G) {
+        ok = ring_acquire(R, pl, &stage, &full);
+        if (!ok) break;
+        const int e0 = i * ST_RT_EXPERTS;
+        const int ne = min(ST_RT_EXPERTS, op.E - e0);
+        const uint32_t bytes = (uint32_t)ne * op.K * 2;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full, bytes);
+          bulk_g2s(stage, op.rw + (size_t)e0 * op.K, bytes, full, pol);
+        }
+        __syncwarp();
+      }
+    } else if (op.type == OP_MOE_UP) {
+      int i = first_item(op.rot);
+      for (; i < op.items_rb && ok; i += G) {
+        ok = ring_acquire(R, pl, &stage, &full);
+        if (!ok) break;
+        Item it;
+        st_describe_shared(op, i, it);
+        produce_item(it, stage, full, pol);
+      }
+      if (!ok) break;
+      ok = stage_wait(plan_bar, plan_phase, pl);
+      if (!ok) break;
+      const int n = pl->nslots * op.items_rb;
+      for (; i < n && ok; i += G) {
+        ok = ring_acquire(R, pl, &stage, &full);
+        if (!ok) break;
+        Item it;
+        st_describe_moe(op, pl, i, it);
+        produce_item(it, stage, full, pol);
+      }
+    } else if (op.type == OP_MOE_DOWN) {
+      const int n = pl->nslots * op.items_rb;
+      for (int i = first_item(op.rot); i < n && ok; i += G) {
+        ok = ring_acquire(R, pl, &stage, &full);
+        if (!ok) break;
+        Item it;
+        st_describe_moe(op, pl, i, it);
+        produce_item(it, stage, full, pol);
+      }
+      // The plan of this router may now be replaced by the consumers.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(plan_ack);
+      plan_phase ^= 1;
+    }
+  }
+  if (!ok && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
+  // Every copy this warp issued must land before the CTA may exit.
+  const int outstanding = min(R.use, R.stages);
+  for (int u = R.use - outstanding; u < R.use; ++u) {
+    const int s = u % R.stages;
+    const uint32_t ph = (u / R.stages) & 1;
+    const long long t0 = now_ns();
+    while (!mbar_try_wait(&R.full[s], ph))
+      if (now_ns() - t0 > ST_WAIT_NS) break;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumers: projection items.
+// ---------------------------------------------------------------------------
+struct Split {
+  int mat, rb, ks, rb_rows;
+  const uint8_t* wtile;
+  const uint16_t* srow;
+};
+
+__device__ __forceinline__ Split split_of(const Item& it, const uint8_t* stage) {
+  const int warp = threadIdx.x >> 5;
+  Split sp;
+  const int per_mat = it.RBc * it.KS;
+  sp.mat = warp / per_mat;
+  const int rem = warp - sp.mat * per_mat;
+  sp.rb = rem / it.KS;
+  sp.ks = rem - sp.rb * it.KS;
+  sp.rb_rows = min(16, it.rows - sp.rb * 16);
+  sp.wtile = stage + (sp.mat * it.RBc * 16 + sp.rb * 16) * it.RS;
+  sp.srow = it.scale_bulk
+                ? reinterpret_cast<const uint16_t*>(stage + stage_scale_offset(it) +
+                                                    sp.mat * stage_scale_stride(it)) +
+                      sp.rb * 16 * it.ng
+                : (sp.mat ? it.s[1] : it.s[0]) + (size_t)(it.r0 + sp.rb * 16) * it.ng;
+  return sp;
+}
+
+// Partial sums of this warp's row block over the kblocks [kb_lo, kb_hi) of
+// the item split among its KS warps.
+__device__ __forceinline__ void split_compute(const Item& it, const Split& sp,
+                                              const uint8_t* wtile, int kb_lo, int kb_hi,
+                                              const uint8_t* (&xrow)[1], float (&acc)[1][4]) {
+  const int n = kb_hi - kb_lo;
+  const int kb0 = kb_lo + n * sp.ks / it.KS, kb1 = kb_lo + n * (sp.ks + 1) / it.KS;
+  if (sp.rb_rows > 0 && kb1 > kb0)
+    rowblock_compute<1>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0, kb1,
+                        xrow, 1, acc);
+}
+
+// Reduction of the KS slices through shared memory; the reducing warps
+// (mat 0, ks 0) get v0 (and v1 = the second matrix for gate/up) and return
+// true.  D fragment: element i is row g + 8*(i>>1), token 2t + (i&1).
+__device__ __forceinline__ bool split_reduce(const Item& it, const Split& sp, float* red,
+                                             int& rslot, const float (&acc)[1][4], float (&v0)[4],
+                                             float (&v1)[4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* rbuf = red + rslot * (NCW * 128);
+  rslot ^= 1;
+  *reinterpret_cast<float4*>(rbuf + (warp * 32 + lane) * 4) =
+      make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+  named_barrier(CBAR, NCT);
+  if (!(sp.mat == 0 && sp.ks == 0 && sp.rb_rows > 0)) return false;
+  const int per_mat = it.RBc * it.KS;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v0[i] = v1[i] = 0.f;
+  for (int k2 = 0; k2 < it.KS; ++k2) {
+    const float4 pv = *reinterpret_cast<const float4*>(rbuf + ((warp + k2) * 32 + lane) * 4);
+    v0[0] += pv.x;
+    v0[1] += pv.y;
+    v0[2] += pv.z;
+    v0[3] += pv.w;
+    if (it.mats == 2) {
+      const float4 uv =
+          *reinterpret_cast<const float4*>(rbuf + ((warp + per_mat + k2) * 32 + lane) * 4);
+      v1[0] += uv.x;
+      v1[1] += uv.y;
+      v1[2] += uv.z;
+      v1[3] += uv.w;
+    }
+  }
+  return true;
+}
+
+// Waits for the next ring stage.  A failed wait records the error and the
+// consumers carry on with the stage as it is (its contents are then unused
+// garbage), so every warp keeps the same sequence of barriers.
+__device__ __forceinline__ const uint8_t* consume_stage(const StepParams& P, Ring& R,
+                                                        StPlan* pl, int* slot) {
+  const int s = R.use % R.stages;
+  const uint32_t ph = (R.use / R.stages) & 1;
+  ++R.use;
+  *slot = s;
+  if (!stage_wait(&R.full[s], ph, pl) && (threadIdx.x & 31) == 0 && !pl->abort)
+    raise_abort(P, pl, ERR_TIMEOUT);
+  return R.base + (size_t)s * R.stage_bytes;
+}
+
+__device__ __forceinline__ void release_stage(Ring& R, int s) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&R.empty[s]);
+}
+
+// ---------------------------------------------------------------------------
+// Consumer operations.
+// ---------------------------------------------------------------------------
+__device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
+                          float* red, int& rslot) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = gridDim.x;
+  wait_deps(P, pl, op);
+  for (int p = 0; p < op.nprob; ++p) {
+    const StDense& D = op.p[p];
+    if (D.nchunk > 1) continue;  // staged chunk by chunk below
+    bool dup = false;
+    for (int q = 0; q < p; ++q) dup |= (op.p[q].x_off == D.x_off);
+    if (dup) continue;
+    const int ts = token_stride(D.K);
+    for (int m = 0; m < op.T; ++m)
+      stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+  }
+  named_barrier(CBAR, NCT);
+  int* done = &P.sync[op.done];
+  for (int i = first_item(op.rot); i < op.items; i += G) {
+    Item it;
+    st_describe_dense(op, i, it);
+    const StDense& D = op.p[it.p];
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    Split sp;
+    if (D.nchunk == 1) {
+      const uint8_t* xrow[1] = {xs + D.x_off + min(g, op.T - 1) * token_stride(D.K)};
+      int s;
+      const uint8_t* stage = consume_stage(P, R, pl, &s);
+      sp = split_of(it, stage);
+      split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
+      release_stage(R, s);
+    } else {
+      // Reduction chunks of kc columns: each stage holds kc/2 bytes of every
+      // row; the activations of the chunk are staged in a chunk-local layout
+      // and the chunk is contracted as a problem of width kc.
+      const int kc = D.K / D.nchunk;
+      const int tsc = token_stride(kc);
+      const int gpc = kc >> (5 + D.gshift);  // scale groups per chunk
+      Item ic = it;
+      ic.K = kc;
+      const uint8_t* xrow[1] = {xs + min(g, op.T - 1) * tsc};
+      for (int ci = 0; ci < D.nchunk; ++ci) {
+        named_barrier(CBAR, NCT);
+        for (int m = 0; m < op.T; ++m)
+          stage_row_cg(xs + m * tsc, D.x + (size_t)m * D.xs + (size_t)ci * kc, kc, threadIdx.x,
+                       NCT);
+        named_barrier(CBAR, NCT);
+        int s;
+        const uint8_t* stage = consume_stage(P, R, pl, &s);
+        sp = split_of(ic, stage);
+        sp.srow += ci * gpc;
+        split_compute(ic, sp, sp.wtile, 0, (kc + 127) >> 7, xrow, acc);
+        release_stage(R, s);
+      }
+    }
+    float v0[4], v1[4];
+    if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
+        const int tok = 2 * t + (e & 1);
+        if (rloc < it.rows && tok < op.T) {
+          const float val = (D.mats == 2) ? swiglu_contract(v0[e], v1[e]) : v0[e];
+          D.y[(size_t)tok * D.ys + it.r0 + rloc] = float_to_bf16_bits(val);
+        }
+      }
+      warp_signal(done, 1);
+    }
+  }
+}
+
+__device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
+                           float* red, int& rslot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  wait_deps(P, pl, op);
+  const int K = op.K, words = K >> 3;
+  for (int m = 0; m < op.T; ++m) {
+    const uint4* src = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
+    uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)m * K * 2);
+    for (int w = threadIdx.x; w < words; w += NCT) dst[w] = __ldcg(src + w);
+  }
+  named_barrier(CBAR, NCT);
+  int* done = &P.sync[op.done];
+  // Warp j < 8 computes expert i*8 + j over the whole row in the order of the
+  // router kernel (lane-strided 16-byte words, a xor butterfly), so logits
+  // equal kb_router_topk's bit for bit; warps 8..15 only keep the barriers.
+  for (int i = first_item(op.rot); i < op.items; i += G) {
+    int s;
+    const uint8_t* stage = consume_stage(P, R, pl, &s);
+    const int e = i * ST_RT_EXPERTS + warp;
+    if (warp < ST_RT_EXPERTS && e < op.E) {
+      float acc[ST_MAX_T];
+#pragma unroll
+      for (int m = 0; m < ST_MAX_T; ++m) acc[m] = 0.f;
+      const uint8_t* wr = stage + (size_t)warp * K * 2;
+      for (int w = lane; w < words; w += 32) {
+        const uint4 wv = lds_v4(wr + (size_t)w * 16);
+        const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int m = 0; m < ST_MAX_T; ++m) {
+          if (m < op.T) {
+            const uint4 hv = lds_v4(xs + (size_t)m * K * 2 + (size_t)w * 16);
+            const uint32_t hq[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              acc[m] = __fmaf_rn(__uint_as_float(hq[q] << 16), __uint_as_float(wq[q] << 16),
+                                 acc[m]);
+              acc[m] = __fmaf_rn(__uint_as_float(hq[q] & 0xFFFF0000u),
+                                 __uint_as_float(wq[q] & 0xFFFF0000u), acc[m]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < ST_MAX_T; ++m) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+        if (lane == 0 && m < op.T) op.logits[(size_t)m * op.E + e] = acc[m];
+      }
+      release_stage(R, s);
+      warp_signal(done, 1);
+    } else {
+      release_stage(R, s);
+    }
+  }
+  (void)red;
+  (void)rslot;
+}
+
+// Top-k for every token (warp per token) and the expert plan (warp 0), in
+// every CTA from the same logits, so every CTA holds the same plan.  Slot 0
+// is the shared expert (bank slot E, every token, route R-1); routed experts
+// follow in order of first use (token-major, then route order).  Indices are
+// always in [0, E), whatever the logits hold.
+__device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const StOp& rop = P.ops[up.router_op];
+  consumers_wait(P, pl, rop.done, rop.target);
+  const int T = up.T, R = up.R, top_k = rop.top_k, E = rop.E;
+  for (int t = warp; t < T; t += NCW) {
+    int my_idx = 0;
+    float my_score = 0.f, wsum = 0.f;
+    warp_topk256(rop.logits + (size_t)t * E, rop.rbias, E, top_k, lane, my_idx, my_score, wsum);
+    my_idx = min(max(my_idx, 0), E - 1);
+    if (lane < top_k) {
+      float wv = my_score;
+      if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
+      wv *= rop.scaling;
+      pl->route_e[t * R + lane] = my_idx;
+      pl->route_w[t * top_k + lane] = wv;
+      if (blockIdx.x == 0) {
+        rop.idx_out[(size_t)t * (top_k + 1) + lane] = my_idx;
+        rop.w_out[(size_t)t * top_k + lane] = wv;
+      }
+    }
+    if (lane == 0) {
+      pl->route_e[t * R + R - 1] = E;
+      if (blockIdx.x == 0) rop.idx_out[(size_t)t * (top_k + 1) + top_k] = E;
+    }
+  }
+  named_barrier(CBAR, NCT);
+  if (warp == 0) {
+    if (lane < T) pl->assign[lane] = lane * R + R - 1;
+    if (lane == 0) {
+      pl->slot_expert[0] = E;
+      pl->slot_start[0] = 0;
+    }
+    const int n = T * top_k;
+    int nslot = 1;
+    for (int base = 0; base < n; base += 32) {
+      const int a = base + lane;
+      const bool valid = a < n;
+      const int e = valid ? pl->route_e[(a / top_k) * R + (a % top_k)] : -1 - lane;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int leader = __ffs(peers) - 1;
+      const int known = valid ? pl->slot_of[e] : 0;
+      __syncwarp();
+      const bool fresh = valid && known < 0 && lane == leader;
+      const unsigned nb = __ballot_sync(0xffffffffu, fresh);
+      if (fresh) {
+        const int sl = nslot + __popc(nb & ((1u << lane) - 1u));
+        pl->slot_of[e] = sl;
+        pl->slot_expert[sl] = e;
+      }
+      nslot += __popc(nb);
+      __syncwarp();
+      if (valid) pl->slot_id[a] = pl->slot_of[e];
+      __syncwarp();
+    }
+    // Counts per routed slot, exclusive prefix after the T shared assignments.
+    int running = T;
+    for (int sb = 1; sb < nslot; sb += 32) {
+      const int sl = sb + lane;
+      int c = 0;
+      if (sl < nslot)
+        for (int a = 0; a < n; ++a) c += (pl->slot_id[a] == sl);
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (sl < nslot) pl->slot_start[sl] = running + incl - c;
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      pl->slot_start[nslot] = running;
+      pl->nslots = nslot;
+    }
+    __syncwarp();
+    // Stable scatter of the routed assignments.
+    for (int a = lane; a < n; a += 32) {
+      const int sl = pl->slot_id[a];
+      int rank = 0;
+      for (int b = 0; b < a; ++b) rank += (pl->slot_id[b] == sl);
+      pl->assign[pl->slot_start[sl] + rank] = (a / top_k) * R + (a % top_k);
+    }
+    __syncwarp();
+    for (int sl = 1 + lane; sl < nslot; sl += 32) pl->slot_of[pl->slot_expert[sl]] = -1;
+  }
+  named_barrier(CBAR, NCT);
+}
+
+// Gate/up + SwiGLU of one item; signals the slot counter per reducing warp.
+__device__ void moe_up_item(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
+                            const uint8_t* xs, float* red, int& rslot, const Item& it) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int ts = token_stride(op.K);
+  const int m = min(g, it.count - 1);
+  const int a = pl->assign[it.abase + m];
+  const uint8_t* xrow[1] = {xs + (a / op.R) * ts};
+  float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+  int s;
+  const uint8_t* stage = consume_stage(P, R, pl, &s);
+  const Split sp = split_of(it, stage);
+  split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
+  release_stage(R, s);
+  float v0[4], v1[4];
+  if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
+      const int tok = 2 * t + (e & 1);
+      if (rloc < it.rows && tok < it.count) {
+        const int aa = pl->assign[it.abase + tok];
+        op.y[(size_t)aa * op.N + it.r0 + rloc] =
+            float_to_bf16_bits(swiglu_contract(v0[e], v1[e]));
+      }
+    }
+    warp_signal(&P.sync[op.slot_cnt + it.p], 1);
+  }
+}
+
+__device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
+                           uint64_t* plan_bar, uint64_t* plan_ack, uint32_t& plan_round,
+                           uint8_t* xs, float* red, int& rslot) {
+  const int G = gridDim.x;
+  wait_deps(P, pl, op);
+  const int ts = token_stride(op.K);
+  for (int m = 0; m < op.T; ++m)
+    stage_row_cg(xs + m * ts, op.mx + (size_t)m * op.mxs, op.K, threadIdx.x, NCT);
+  // The shared slot needs no routing: its assignments are t*R + R-1 (the
+  // producer may still be reading the previous plan, which holds the same
+  // values for slot 0).
+  if (threadIdx.x < op.T) pl->assign[threadIdx.x] = threadIdx.x * op.R + op.R - 1;
+  if (threadIdx.x == 0) {
+    pl->slot_start[0] = 0;
+    pl->slot_start[1] = op.T;
+    pl->slot_expert[0] = op.E;
+  }
+  named_barrier(CBAR, NCT);
+  int i = first_item(op.rot);
+  for (; i < op.items_rb; i += G) {
+    Item it;
+    st_describe_shared(op, i, it);
+    moe_up_item(P, op, pl, R, xs, red, rslot, it);
+  }
+  // The producer must be done with the previous plan before it is replaced.
+  if (plan_round > 0) {
+    if (threadIdx.x == 0 && !stage_wait(plan_ack, (plan_round - 1) & 1, pl) && !pl->abort)
+      raise_abort(P, pl, ERR_TIMEOUT);
+    named_barrier(CBAR, NCT);
+  }
+  build_routing(P, op, pl);
+  if (threadIdx.x == 0) mbar_arrive(plan_bar);
+  ++plan_round;
+  const int n = pl->nslots * op.items_rb;
+  for (; i < n; i += G) {
+    Item it;
+    st_describe_moe(op, pl, i, it);
+    moe_up_item(P, op, pl, R, xs, red, rslot, it);
+  }
+}
+
+__device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
+                             uint8_t* xs, float* red, int& rslot) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = gridDim.x;
+  const int n = pl->nslots * op.items_rb;
+  const int ts = token_stride(op.K);
+  const int top_k = op.R - 1;
+  for (int i = first_item(op.rot); i < n; i += G) {
+    Item it;
+    st_describe_moe(op, pl, i, it);
+    // Inputs: the activated rows of this slot, complete once every row block
+    // of the slot's gate/up has been signalled.
+    consumers_wait(P, pl, op.slot_cnt + it.p, op.up_rb);
+    for (int m = 0; m < it.count; ++m)
+      stage_row_cg(xs + m * ts, op.mx + (size_t)pl->assign[it.abase + m] * op.mxs, op.K,
+                   threadIdx.x, NCT);
+    named_barrier(CBAR, NCT);
+    const uint8_t* xrow[1] = {xs + min(g, it.count - 1) * ts};
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    int s;
+    const uint8_t* stage = consume_stage(P, R, pl, &s);
+    const Split sp = split_of(it, stage);
+    split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
+    release_stage(R, s);
+    float v0[4], v1[4];
+    if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
+        const int tok = 2 * t + (e & 1);
+        if (rloc < it.rows && tok < it.count) {
+          const int aa = pl->assign[it.abase + tok];
+          op.wsy[(size_t)aa * op.N + it.r0 + rloc] = float_to_bf16_bits(v0[e]);
+        }
+      }
+    }
+    // Arrival per (token, row group): the CTA that brings the count to R
+    // combines the routes in route order.
+    named_barrier(CBAR, NCT);
+    const int rbg = it.r0 / (op.RBc * 16);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      for (int m = 0; m < it.count; ++m) {
+        const int tok = pl->assign[it.abase + m] / op.R;
+        const int old = atomicAdd(&P.sync[op.arrive + tok * op.items_rb + rbg], 1);
+        pl->done_tok[m] = (old == op.R - 1) ? tok : -1;
+      }
+      __threadfence();
+    }
+    named_barrier(CBAR, NCT);
+    int ndone = 0;
+    for (int m = 0; m < it.count; ++m) {
+      const int tok = pl->done_tok[m];
+      if (tok < 0) continue;
+      ++ndone;
+      for (int rl = threadIdx.x; rl < it.rows; rl += NCT) {
+        const int row = it.r0 + rl;
+        float accum = 0.f;
+        for (int r = 0; r < top_k; ++r) {
+          const uint16_t ov = __ldcg(&op.wsy[((size_t)tok * op.R + r) * op.N + row]);
+          accum += bf16_bits_to_float(ov) * pl->route_w[tok * top_k + r];
+        }
+        const uint16_t sv = __ldcg(&op.wsy[((size_t)tok * op.R + op.R - 1) * op.N + row]);
+        op.out[(size_t)tok * op.N + row] =
+            float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
+      }
+    }
+    named_barrier(CBAR, NCT);
+    if (threadIdx.x == 0 && ndone > 0) {
+      __threadfence();
+      atomicAdd(&P.sync[op.done], ndone);
+    }
+  }
+}
+
+// Warps 0..7 own rows i = r*8 + warp (r < 16) of a 32-column slice, as the
+// KDA kernel does, so the arithmetic (and its rounding) is the same; warps
+// 8..15 only keep the barriers.
+__device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* kd) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  constexpr int KW = 8;    // computing warps
+  constexpr int RPW = 16;  // rows per computing warp (Dk <= 128)
+  const bool worker = warp < KW;
+  const int nsl = (op.Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
+  bool waited = false;
+  for (int u = first_item(op.rot); u < op.items; u += G) {
+    const int bh = u / nsl, sl = u - bh * nsl;
+    const int b = bh / op.H, h = bh - b * op.H;
+    const int col = sl * ST_KDA_COLS + lane;
+    const bool col_ok = worker && col < op.Dv;
+    float* base = op.state + (size_t)b * op.sb + (size_t)h * op.sh + col;
+    // The state depends on no operation of this launch: read it before the
+    // wait for the inputs.
+    float c[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int i = r * KW + warp;
+      c[r] = (col_ok && i < op.Dk) ? base[(size_t)i * op.sk] : 0.f;
+    }
+    if (!waited) {
+      wait_deps(P, pl, op);
+      waited = true;
+    }
+    const size_t vec = (size_t)bh * op.Dk;
+    const float bt = __ldcg(&op.beta[bh]);
+    for (int i = threadIdx.x; i < op.Dk; i += NCT) {
+      const float kv = __ldcg(&op.k[vec + i]);
+      kd->ed[i] = expf(__ldcg(&op.decay[vec + i]));
+      kd->k[i] = kv;
+      kd->bk[i] = __fmul_rn(bt, kv);
+      kd->q[i] = __fmul_rn(__ldcg(&op.q[vec + i]), op.scale);
+    }
+    named_barrier(CBAR, NCT);
+    float part = 0.f;
+    if (worker) {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = r * KW + warp;
+        if (i < op.Dk) {
+          c[r] = __fmul_rn(c[r], kd->ed[i]);
+          part = __fadd_rn(part, __fmul_rn(c[r], kd->k[i]));
+        }
+      }
+      kd->red[warp][lane] = part;
+    }
+    named_barrier(CBAR, NCT);
+    float pred = 0.f;
+#pragma unroll
+    for (int w = 0; w < KW; ++w) pred = __fadd_rn(pred, kd->red[w][lane]);
+    const float delta = col_ok ? __fsub_rn(__ldcg(&op.v[(size_t)bh * op.Dv + col]), pred) : 0.f;
+    named_barrier(CBAR, NCT);
+    if (worker) {
+      float opart = 0.f;
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = r * KW + warp;
+        if (i < op.Dk) {
+          c[r] = __fadd_rn(c[r], __fmul_rn(kd->bk[i], delta));
+          opart = __fadd_rn(opart, __fmul_rn(c[r], kd->q[i]));
+          if (col_ok) base[(size_t)i * op.sk] = c[r];
+        }
+      }
+      kd->red[warp][lane] = opart;
+    }
+    named_barrier(CBAR, NCT);
+    if (warp == 0) {
+      const bool ok_col = sl * ST_KDA_COLS + lane < op.Dv;
+      if (ok_col) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
+        if (op.kout) op.kout[(size_t)bh * op.Dv + col] = o;
+        if (op.kout_bf16) op.kout_bf16[(size_t)bh * op.Dv + col] = float_to_bf16_bits(o);
+      }
+      warp_signal(&P.sync[op.done], 1);
+    }
+    named_barrier(CBAR, NCT);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant__ StepParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  uint8_t* xs = smem;
+  float* red = reinterpret_cast<float*>(smem + P.red_off);
+  StPlan* pl = reinterpret_cast<StPlan*>(smem + P.scr_off);
+  StKda* kd = reinterpret_cast<StKda*>(smem + P.scr_off + sizeof(StPlan));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
+  Ring R;
+  R.base = smem + P.ring_off;
+  R.full = bars;
+  R.empty = bars + P.stages;
+  R.stages = P.stages;
+  R.stage_bytes = P.stage_bytes;
+  R.use = 0;
+  uint64_t* plan_bar = bars + 2 * P.stages;
+  uint64_t* plan_ack = plan_bar + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.stages; ++s) {
+      mbar_init(&R.full[s], 1);
+      mbar_init(&R.empty[s], NCW);
+    }
+    mbar_init(plan_bar, 1);
+    mbar_init(plan_ack, 1);
+    mbar_fence_init();
+    pl->abort = 0;
+    pl->nslots = 0;
+  }
+  for (int e = threadIdx.x; e <= ST_MAX_E; e += NTHREADS) pl->slot_of[e] = -1;
+  __syncthreads();
+
+  if (warp == NCW) {
+    // Weights are constant: stream them at once; only the routed experts
+    // wait for the consumers' plan.
+    producer_main(P, pl, R, plan_bar, plan_ack);
+    return;
+  }
+
+  // Counters are reset by the previous launch; wait for it to finish.
+  pdl_wait();
+  int rslot = 0;
+  uint32_t plan_round = 0;
+  for (int o = 0; o < P.nops; ++o) {
+    const StOp& op = P.ops[o];
+    switch (op.type) {
+      case OP_DENSE:
+        run_dense(P, op, pl, R, xs, red, rslot);
+        break;
+      case OP_ROUTER:
+        run_router(P, op, pl, R, xs, red, rslot);
+        break;
+      case OP_MOE_UP:
+        run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, red, rslot);
+        break;
+      case OP_MOE_DOWN:
+        run_moe_down(P, op, pl, R, xs, red, rslot);
+        break;
+      case OP_KDA:
+        run_kda(P, op, pl, kd);
+        break;
+      default:
+        break;
+    }
+  }
+  // Exit: the last CTA resets every counter for the next launch (all of its
+  // consumer threads; the exit counter last).
+  named_barrier(CBAR, NCT);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(&P.sync[P.exit_idx], 1);
+    pl->last = (old == (int)gridDim.x - 1);
+    if (pl->last) __threadfence();
+  }
+  named_barrier(CBAR, NCT);
+  if (pl->last) {
+    for (int i = threadIdx.x; i < P.nsync; i += NCT)
+      if (i != P.exit_idx) P.sync[i] = 0;
+    __threadfence();
+    named_barrier(CBAR, NCT);
+    if (threadIdx.x == 0) P.sync[P.exit_idx] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: program construction.
+// ---------------------------------------------------------------------------
+struct StepProgram {
+  int T = 0;
+  std::vector<StOp> ops;
+  int nsync = 0;
+  bool finalized = false;
+  int device = -1;
+  StOp* d_ops = nullptr;
+  int* d_sync = nullptr;
+  StepParams params = {};
+  size_t smem = 0;
+  int grid = 0;
+};
+
+static int add_sync(StepProgram* pr, int n) {
+  const int at = pr->nsync;
+  pr->nsync += n;
+  return at;
+}
+
+static int check_deps(StepProgram* pr, const int* deps, int ndeps, StOp& op) {
+  KB_REQUIRE(ndeps >= 0 && ndeps <= ST_MAX_DEPS, KB_ERR_UNSUPPORTED,
+             "at most %d dependencies per operation", ST_MAX_DEPS);
+  KB_REQUIRE(ndeps == 0 || deps, KB_ERR_NULL_POINTER, "deps is NULL");
+  op.ndeps = ndeps;
+  for (int d = 0; d < ndeps; ++d) {
+    KB_REQUIRE(deps[d] >= 0 && deps[d] < (int)pr->ops.size(), KB_ERR_BAD_SHAPE,
+               "dependency %d is not an earlier operation", deps[d]);
+    KB_REQUIRE(pr->ops[deps[d]].type != OP_MOE_UP, KB_ERR_BAD_SHAPE,
+               "depend on the expert block's down operation, not its gate/up");
+    op.dep[d] = deps[d];
+  }
+  return KB_OK;
+}
+
+// Warp split for the executor: items of at most ST_STAGE_TARGET bytes (dense
+// rows longer than that are split into reduction chunks, one stage each),
+// smaller items while the operation has fewer items than CTAs, and at least
+// one 128-wide block per warp.
+static void step_split(int K, int mats, int64_t row_blocks, int grid, int* KS, int* RBc,
+                       int* nchunk) {
+  const int KB = (K + 127) / 128;
+  const int maxks = NCW / mats;
+  int chunks = 1;
+  if (mats == 1)
+    while ((int64_t)16 * (K / chunks) / 2 > ST_STAGE_TARGET && KB % (chunks * 2) == 0)
+      chunks *= 2;
+  const int KBc = KB / chunks;
+  int rbc = maxks;
+  while (rbc > 1 && (int64_t)rbc * 16 * (K / chunks) / 2 * mats > ST_STAGE_TARGET) rbc /= 2;
+  while (rbc > 1 && (row_blocks + rbc - 1) / rbc < grid && KBc >= maxks / (rbc / 2)) rbc /= 2;
+  int ks = maxks / rbc;
+  while (ks > 1 && KBc < ks) {
+    ks /= 2;
+    rbc *= 2;
+  }
+  *KS = ks;
+  *RBc = rbc;
+  *nchunk = chunks;
+}
+
+static int current_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  const int n = num_sms(dev);
+  return n > 0 ? n : 148;
+}
+
+}  // namespace kb
+
+using kb::StepProgram;
+
+extern "C" {
+
+int kb_step_create(int64_t tokens, kb_step** out) {
+  kb::clear_error();
+  KB_REQUIRE(out, KB_ERR_NULL_POINTER, "out is NULL");
+  *out = nullptr;
+  KB_REQUIRE(tokens >= 1 && tokens <= kb::ST_MAX_T, KB_ERR_UNSUPPORTED,
+             "the step executor supports 1 to %d tokens", kb::ST_MAX_T);
+  StepProgram* pr = new (std::nothrow) StepProgram();
+  KB_REQUIRE(pr, KB_ERR_DEVICE, "out of host memory");
+  pr->T = (int)tokens;
+  *out = reinterpret_cast<kb_step*>(pr);
+  return KB_OK;
+}
+
+void kb_step_destroy(kb_step* step) {
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  if (!pr) return;
+  if (pr->d_ops || pr->d_sync) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (pr->device >= 0) cudaSetDevice(pr->device);
+    cudaFree(pr->d_ops);
+    cudaFree(pr->d_sync);
+    if (cur >= 0) cudaSetDevice(cur);
+  }
+  delete pr;
+}
+
+int kb_step_add_dense(kb_step* step, const kb_dense_problem* problems, int count,
+                      const int* deps, int ndeps, int* op_out) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr && problems && op_out, KB_ERR_NULL_POINTER, "NULL argument");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(count >= 1 && count <= kb::ST_MAX_PROB, KB_ERR_UNSUPPORTED,
+             "1 to %d problems per dense operation", kb::ST_MAX_PROB);
+  kb::StOp op = {};
+  op.type = kb::OP_DENSE;
+  op.T = pr->T;
+  int rc = kb::check_deps(pr, deps, ndeps, op);
+  if (rc) return rc;
+  int64_t row_blocks = 0;
+  for (int i = 0; i < count; ++i) row_blocks += (problems[i].N + 15) / 16;
+  int items = 0, xbytes = 0;
+  for (int i = 0; i < count; ++i) {
+    const kb_dense_problem& q = problems[i];
+    KB_REQUIRE(q.M == pr->T, KB_ERR_BAD_SHAPE, "problem %d: M=%lld differs from the step's %d",
+               i, (long long)q.M, pr->T);
+    KB_REQUIRE(q.K > 0 && q.K % 128 == 0 && q.K <= 16384 && q.N > 0 && q.N < (1 << 24),
+               KB_ERR_UNSUPPORTED, "problem %d: need K %% 128 == 0, K <= 16384", i);
+    int gs = 0;
+    rc = kb::check_group(q.K, q.group, &gs);
+    if (rc) return rc;
+    KB_REQUIRE(q.x && q.packed && q.scales && q.y, KB_ERR_NULL_POINTER,
+               "problem %d: NULL pointer", i);
+    KB_REQUIRE(kb::aligned(q.x, 16) && q.x_stride % 8 == 0 && kb::aligned(q.packed, 16) &&
+                   kb::aligned(q.scales, 2) && q.y_stride >= q.N,
+               KB_ERR_ALIGNMENT, "problem %d: misaligned operand", i);
+    kb::StDense& D = op.p[i];
+    D.x = q.x;
+    D.xs = q.x_stride;
+    D.w = q.packed;
+    D.s = q.scales;
+    D.y = q.y;
+    D.ys = q.y_stride;
+    D.K = (int)q.K;
+    D.N = (int)q.N;
+    D.gshift = gs;
+    kb::step_split(D.K, 1, row_blocks, kb::current_sms(), &D.KS, &D.RBc, &D.nchunk);
+    D.mats = 1;
+    KB_REQUIRE(D.nchunk == 1 || count == 1, KB_ERR_UNSUPPORTED,
+               "problem %d: a reduction width of %lld needs an operation of its own", i,
+               (long long)q.K);
+    D.items = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
+    D.item_begin = items;
+    items += D.items;
+    D.x_off = -1;
+    for (int j = 0; j < i; ++j)
+      if (op.p[j].x == D.x && op.p[j].K == D.K) D.x_off = op.p[j].x_off;
+    if (D.x_off < 0) {
+      D.x_off = xbytes;
+      xbytes += pr->T * kb::token_stride(D.K);
+    }
+    op.target += (D.N + 15) / 16;
+  }
+  op.nprob = count;
+  op.items = items;
+  op.done = kb::add_sync(pr, 1);
+  *op_out = (int)pr->ops.size();
+  pr->ops.push_back(op);
+  return KB_OK;
+}
+
+int kb_step_add_swiglu(kb_step* step, const uint16_t* x, int64_t x_stride, int64_t K,
+                       const uint8_t* w1_packed, const uint16_t* w1_scales,
+                       const uint8_t* w3_packed, const uint16_t* w3_scales, int64_t N,
+                       int64_t group, uint16_t* y, int64_t y_stride, const int* deps, int ndeps,
+                       int* op_out) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr && x && w1_packed && w1_scales && w3_packed && w3_scales && y && op_out,
+             KB_ERR_NULL_POINTER, "NULL argument");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(K > 0 && K % 128 == 0 && K <= 16384 && N > 0 && N < (1 << 24),
+             KB_ERR_UNSUPPORTED, "need K %% 128 == 0, K <= 16384");
+  int gs = 0;
+  int rc = kb::check_group(K, group, &gs);
+  if (rc) return rc;
+  KB_REQUIRE(kb::aligned(x, 16) && x_stride % 8 == 0 && kb::aligned(w1_packed, 16) &&
+                 kb::aligned(w3_packed, 16) && kb::aligned(w1_scales, 2) &&
+                 kb::aligned(w3_scales, 2) && y_stride >= N,
+             KB_ERR_ALIGNMENT, "misaligned operand");
+  kb::StOp op = {};
+  op.type = kb::OP_DENSE;
+  op.T = pr->T;
+  rc = kb::check_deps(pr, deps, ndeps, op);
+  if (rc) return rc;
+  kb::StDense& D = op.p[0];
+  D.x = x;
+  D.xs = x_stride;
+  D.w = w1_packed;
+  D.s = w1_scales;
+  D.w3 = w3_packed;
+  D.s3 = w3_scales;
+  D.y = y;
+  D.ys = y_stride;
+  D.K = (int)K;
+  D.N = (int)N;
+  D.gshift = gs;
+  D.mats = 2;
+  kb::step_split(D.K, 2, (N + 15) / 16, kb::current_sms(), &D.KS, &D.RBc, &D.nchunk);
+  D.items = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
+  D.item_begin = 0;
+  D.x_off = 0;
+  op.nprob = 1;
+  op.items = D.items;
+  op.target = (D.N + 15) / 16;
+  op.done = kb::add_sync(pr, 1);
+  *op_out = (int)pr->ops.size();
+  pr->ops.push_back(op);
+  return KB_OK;
+}
+
+int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride, int64_t K,
+                       const uint16_t* weight, const float* bias, int64_t E, int64_t top_k,
+                       int renormalize, float scaling, float* logits, int64_t* idx_out,
+                       float* w_out, const int* deps, int ndeps, int* op_out) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr && hidden && weight && logits && idx_out && w_out && op_out,
+             KB_ERR_NULL_POINTER, "NULL argument");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(E >= 1 && E <= kb::ST_MAX_E && top_k >= 1 && top_k <= kb::ST_MAX_TOPK &&
+                 top_k <= E && K > 0 && K % 8 == 0 && K <= 8192,
+             KB_ERR_UNSUPPORTED, "step router supports E <= %d, top_k <= %d, K %% 8 == 0",
+             kb::ST_MAX_E, kb::ST_MAX_TOPK);
+  KB_REQUIRE(kb::aligned(hidden, 16) && h_stride % 8 == 0 && kb::aligned(weight, 16),
+             KB_ERR_ALIGNMENT, "hidden/weight must be 16-byte aligned");
+  kb::StOp op = {};
+  op.type = kb::OP_ROUTER;
+  op.T = pr->T;
+  int rc = kb::check_deps(pr, deps, ndeps, op);
+  if (rc) return rc;
+  op.rx = hidden;
+  op.rxs = h_stride;
+  op.rw = weight;
+  op.rbias = bias;
+  op.E = (int)E;
+  op.K = (int)K;
+  op.top_k = (int)top_k;
+  op.renorm = renormalize;
+  op.scaling = scaling;
+  op.logits = logits;
+  op.idx_out = idx_out;
+  op.w_out = w_out;
+  op.items = (int)((E + kb::ST_RT_EXPERTS - 1) / kb::ST_RT_EXPERTS);
+  op.target = (int)E;
+  op.done = kb::add_sync(pr, 1);
+  *op_out = (int)pr->ops.size();
+  pr->ops.push_back(op);
+  return KB_OK;
+}
+
+int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden, int64_t h_stride,
+                    int64_t H, const uint8_t* w1_packed, const uint16_t* w1_scales,
+                    const uint8_t* w3_packed, const uint16_t* w3_scales,
+                    const uint8_t* w2_packed, const uint16_t* w2_scales, int64_t I,
+                    int64_t group, uint16_t* activated, uint16_t* routed_out, uint16_t* out,
+                    const int* deps, int ndeps, int* op_out) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr && hidden && w1_packed && w1_scales && w3_packed && w3_scales && w2_packed &&
+                 w2_scales && activated && routed_out && out && op_out,
+             KB_ERR_NULL_POINTER, "NULL argument");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(router_op >= 0 && router_op < (int)pr->ops.size() &&
+                 pr->ops[router_op].type == kb::OP_ROUTER,
+             KB_ERR_BAD_SHAPE, "router_op %d is not a router operation", router_op);
+  const kb::StOp& rop = pr->ops[router_op];
+  KB_REQUIRE(rop.K == H, KB_ERR_BAD_SHAPE, "hidden width %lld differs from the router's %d",
+             (long long)H, rop.K);
+  KB_REQUIRE(H % 128 == 0 && I % 128 == 0 && H <= 16384 && I <= 16384, KB_ERR_UNSUPPORTED,
+             "hidden and intermediate widths must be multiples of 128");
+  int gs_up = 0, gs_dn = 0;
+  int rc = kb::check_group(H, group, &gs_up);
+  if (rc) return rc;
+  rc = kb::check_group(I, group, &gs_dn);
+  if (rc) return rc;
+  KB_REQUIRE(kb::aligned(hidden, 16) && h_stride % 8 == 0 && kb::aligned(w1_packed, 16) &&
+                 kb::aligned(w3_packed, 16) && kb::aligned(w2_packed, 16) &&
+                 kb::aligned(activated, 16),
+             KB_ERR_ALIGNMENT, "misaligned expert operand");
+  const int T = pr->T, E = rop.E, R = rop.top_k + 1;
+  kb::StOp up = {};
+  up.type = kb::OP_MOE_UP;
+  up.T = T;
+  rc = kb::check_deps(pr, deps, ndeps, up);
+  if (rc) return rc;
+  up.router_op = router_op;
+  up.E = E;
+  up.R = R;
+  up.mx = hidden;
+  up.mxs = h_stride;
+  up.w0 = w1_packed;
+  up.s0 = w1_scales;
+  up.w1 = w3_packed;
+  up.s1 = w3_scales;
+  up.wse = I * (H / 2);
+  up.sse = I * (H / group);
+  up.K = (int)H;
+  up.N = (int)I;
+  up.gshift = gs_up;
+  int nchunk = 1;
+  kb::step_split(up.K, 2, (int64_t)(1 + T * rop.top_k) * ((I + 15) / 16), kb::current_sms(),
+                 &up.KS, &up.RBc, &nchunk);
+  up.items_rb = (int)((I + 16 * up.RBc - 1) / (16 * up.RBc));
+  up.y = activated;
+  up.rot = ((int)pr->ops.size() * 37) % kb::current_sms();
+  up.done = kb::add_sync(pr, 1);
+  up.slot_cnt = kb::add_sync(pr, kb::ST_MAX_SLOTS);
+  up.target = 0;
+  const int up_index = (int)pr->ops.size();
+  pr->ops.push_back(up);
+
+  kb::StOp dn = {};
+  dn.type = kb::OP_MOE_DOWN;
+  dn.T = T;
+  dn.ndeps = 0;
+  dn.router_op = router_op;
+  dn.E = E;
+  dn.R = R;
+  dn.mx = activated;
+  dn.mxs = I;
+  dn.w0 = w2_packed;
+  dn.s0 = w2_scales;
+  dn.wse = H * (I / 2);
+  dn.sse = H * (I / group);
+  dn.K = (int)I;
+  dn.N = (int)H;
+  dn.gshift = gs_dn;
+  kb::step_split(dn.K, 1, (int64_t)(1 + T * rop.top_k) * ((H + 15) / 16), kb::current_sms(),
+                 &dn.KS, &dn.RBc, &nchunk);
+  dn.items_rb = (int)((H + 16 * dn.RBc - 1) / (16 * dn.RBc));
+  dn.up_rb = (int)((I + 15) / 16);
+  dn.slot_cnt = pr->ops[up_index].slot_cnt;
+  dn.wsy = routed_out;
+  dn.out = out;
+  dn.rot = ((up_index + 1) * 37) % kb::current_sms();
+  dn.done = kb::add_sync(pr, 1);
+  dn.arrive = kb::add_sync(pr, T * dn.items_rb);
+  dn.target = T * dn.items_rb;
+  *op_out = (int)pr->ops.size();
+  pr->ops.push_back(dn);
+  return KB_OK;
+}
+
+int kb_step_add_kda(kb_step* step, float* state, int64_t sb, int64_t sh, int64_t sk,
+                    const float* q, const float* k, const float* v, const float* decay,
+                    const float* beta, int64_t B, int64_t H, int64_t Dk, int64_t Dv,
+                    float scale, float* out, uint16_t* out_bf16, const int* deps, int ndeps,
+                    int* op_out) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr && state && q && k && v && decay && beta && op_out && (out || out_bf16),
+             KB_ERR_NULL_POINTER, "NULL argument");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(B >= 1 && H >= 1 && Dk >= 1 && Dk <= 128 && Dv >= 1 && Dv <= 4096,
+             KB_ERR_UNSUPPORTED, "step KDA supports Dk <= 128, Dv <= 4096");
+  KB_REQUIRE(sk >= Dv && sh >= Dk * sk && sb >= H * sh, KB_ERR_BAD_SHAPE,
+             "state strides overlap rows");
+  kb::StOp op = {};
+  op.type = kb::OP_KDA;
+  op.T = pr->T;
+  int rc = kb::check_deps(pr, deps, ndeps, op);
+  if (rc) return rc;
+  op.state = state;
+  op.sb = sb;
+  op.sh = sh;
+  op.sk = sk;
+  op.q = q;
+  op.k = k;
+  op.v = v;
+  op.decay = decay;
+  op.beta = beta;
+  op.B = (int)B;
+  op.H = (int)H;
+  op.Dk = (int)Dk;
+  op.Dv = (int)Dv;
+  op.scale = scale;
+  op.kout = out;
+  op.kout_bf16 = out_bf16;
+  op.items = (int)(B * H * ((Dv + kb::ST_KDA_COLS - 1) / kb::ST_KDA_COLS));
+  op.target = op.items;
+  op.done = kb::add_sync(pr, 1);
+  *op_out = (int)pr->ops.size();
+  pr->ops.push_back(op);
+  return KB_OK;
+}
+
+int kb_step_finalize(kb_step* step) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr, KB_ERR_NULL_POINTER, "step is NULL");
+  KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
+  KB_REQUIRE(!pr->ops.empty(), KB_ERR_BAD_SHAPE, "empty program");
+  int dev = 0;
+  KB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess, KB_ERR_DEVICE, "no current CUDA device");
+  const int G = kb::num_sms(dev);
+  KB_REQUIRE(G > 0, KB_ERR_DEVICE, "cannot query the SM count");
+  const int T = pr->T;
+  // Rotations and the largest stage and activation regions.
+  int stage = 0, xbytes = 0, cum = 0;
+  for (size_t o = 0; o < pr->ops.size(); ++o) {
+    kb::StOp& op = pr->ops[o];
+    switch (op.type) {
+      case kb::OP_DENSE: {
+        op.rot = cum % G;
+        cum += op.items;
+        int xb = 0;
+        for (int i = 0; i < op.nprob; ++i) {
+          const kb::StDense& D = op.p[i];
+          const int ng = D.K >> (5 + D.gshift);
+          const int sb = (D.nchunk > 1) ? D.RBc * 16 * (D.K / (2 * D.nchunk))
+                                        : kb::item_stage_bytes(D.K, D.mats, D.RBc, ng);
+          stage = std::max(stage, sb);
+          xb = std::max(xb, (D.nchunk > 1) ? T * kb::token_stride(D.K / D.nchunk)
+                                           : D.x_off + T * kb::token_stride(D.K));
+        }
+        xbytes = std::max(xbytes, xb);
+        break;
+      }
+      case kb::OP_ROUTER:
+        op.rot = cum % G;
+        cum += op.items;
+        stage = std::max(stage, kb::ST_RT_EXPERTS * op.K * 2);
+        xbytes = std::max(xbytes, T * op.K * 2);
+        break;
+      case kb::OP_MOE_UP:
+      case kb::OP_MOE_DOWN: {
+        const int mats = op.type == kb::OP_MOE_UP ? 2 : 1;
+        stage = std::max(stage,
+                         kb::item_stage_bytes(op.K, mats, op.RBc, op.K >> (5 + op.gshift)));
+        xbytes = std::max(xbytes, T * kb::token_stride(op.K));
+        break;
+      }
+      case kb::OP_KDA:
+        op.rot = cum % G;
+        cum += op.items;
+        break;
+    }
+  }
+  stage = (stage + 127) / 128 * 128;
+  const int exit_idx = kb::add_sync(pr, 1);
+  const int abort_idx = kb::add_sync(pr, 1);
+  kb::StepParams& P = pr->params;
+  P = {};
+  P.nops = (int)pr->ops.size();
+  P.nsync = pr->nsync;
+  P.exit_idx = exit_idx;
+  P.abort_idx = abort_idx;
+  P.stage_bytes = stage;
+  P.red_off = (xbytes + 127) / 128 * 128;
+  P.scr_off = P.red_off + 2 * kb::NCW * 128 * (int)sizeof(float);
+  const int scr = (int)(sizeof(kb::StPlan) + sizeof(kb::StKda) + 127) / 128 * 128;
+  P.ring_off = P.scr_off + scr;
+  const int avail = kb::MAX_SMEM - P.ring_off - 256;
+  P.stages = std::min(16, avail / std::max(stage, 1));
+  KB_REQUIRE(P.stages >= 2, KB_ERR_UNSUPPORTED,
+             "shared memory: %d bytes of fixed regions leave room for %d stages of %d bytes",
+             P.ring_off, P.stages, stage);
+  P.bar_off = P.ring_off + P.stages * stage;
+  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2) * sizeof(uint64_t);
+  KB_REQUIRE(pr->smem <= (size_t)kb::MAX_SMEM, KB_ERR_UNSUPPORTED, "shared memory overflow");
+  P.err = kb::device_error_word(dev);
+  KB_REQUIRE(P.err, KB_ERR_DEVICE, "device error word unavailable");
+  cudaError_t e = cudaMalloc(&pr->d_ops, pr->ops.size() * sizeof(kb::StOp));
+  if (e == cudaSuccess) e = cudaMalloc(&pr->d_sync, (size_t)pr->nsync * sizeof(int));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(pr->d_ops, pr->ops.data(), pr->ops.size() * sizeof(kb::StOp),
+                   cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(pr->d_sync, 0, (size_t)pr->nsync * sizeof(int));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kb::step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kb::MAX_SMEM);
+  KB_REQUIRE(e == cudaSuccess, KB_ERR_DEVICE, "step program upload failed: %s",
+             cudaGetErrorString(e));
+  P.ops = pr->d_ops;
+  P.sync = pr->d_sync;
+  pr->grid = G;
+  pr->device = dev;
+  pr->finalized = true;
+  return KB_OK;
+}
+
+int kb_step_launch(kb_step* step, void* stream) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr, KB_ERR_NULL_POINTER, "step is NULL");
+  KB_REQUIRE(pr->finalized, KB_ERR_UNSUPPORTED, "program not finalized");
+  int dev = -1;
+  cudaGetDevice(&dev);
+  KB_REQUIRE(dev == pr->device, KB_ERR_DEVICE,
+             "program was finalized on device %d, current device is %d", pr->device, dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pr->grid);
+  cfg.blockDim = dim3(kb::NTHREADS);
+  cfg.dynamicSmemBytes = pr->smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kb::step_kernel, pr->params);
+  KB_REQUIRE(err == cudaSuccess, KB_ERR_LAUNCH, "step launch failed: %s",
+             cudaGetErrorString(err));
+  return KB_OK;
+}
+
+int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage_bytes,
+                 size_t* smem_bytes) {
+  kb::clear_error();
+  const StepProgram* pr = reinterpret_cast<const StepProgram*>(step);
+  KB_REQUIRE(pr, KB_ERR_NULL_POINTER, "step is NULL");
+  if (n_ops) *n_ops = (int)pr->ops.size();
+  if (stages) *stages = pr->params.stages;
+  if (stage_bytes) *stage_bytes = pr->params.stage_bytes;
+  if (smem_bytes) *smem_bytes = pr->smem;
+  return KB_OK;
+}
+
+}  // extern "C"

@@ -34,6 +34,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .moe import MoELayerWeights, moe_forward
+from .step import StepProgram
 
 
 @dataclass(frozen=True)
@@ -183,8 +184,9 @@ class HotPathDecoder:
                                     out_bf16=self.kda_out)
                 h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
             else:
-                _, _, h = ops.w4a16_dense_multi(
-                    [(x, *lw.q_proj), (self.mla_latent, *lw.kv_b), (self.mla_attn, *lw.o_proj)])
+                # q_proj and kv_b feed the attention, whose output feeds o_proj.
+                ops.w4a16_dense_multi([(x, *lw.q_proj), (self.mla_latent, *lw.kv_b)])
+                h = ops.w4a16_dense(self.mla_attn, *lw.o_proj)
             if lw.dense_mlp is not None:
                 (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
                 act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
@@ -196,9 +198,78 @@ class HotPathDecoder:
     def _count_launches(self) -> int:
         n = 1  # lm_head
         for lw in self.layers:
-            n += 3 if lw.kind == "kda" else 1
+            n += 3 if lw.kind == "kda" else 2
             n += 2 if lw.dense_mlp is not None else 3
         return n
+
+    # -- the same step as one executor program ------------------------------------------
+    def build_program(self, x: torch.Tensor) -> tuple[StepProgram, dict[str, object]]:
+        """The step of ``step(x)`` as a decode-step executor program.
+
+        Returns the finalized program and its buffers: ``logits`` (the
+        output), ``idx``/``weights`` (routing of every MoE layer) and the
+        intermediates.  Operations depend on the operations that produce their
+        inputs as in the model (the KDA step on the q/k/v projections, MLA's
+        o_proj on q_proj/kv_b, each layer on the previous layer's output).
+        The program's KDA states are the layers' own states, as in ``step``.
+        """
+        s = self.shape
+        B = self.batch
+        dev = self.device
+        bf = torch.bfloat16
+        proj = s.kda_heads * s.kda_head_dim
+        buf: dict[str, object] = {
+            "x_in": x,
+            "xa": torch.empty((B, s.hidden), dtype=bf, device=dev),
+            "xb": torch.empty((B, s.hidden), dtype=bf, device=dev),
+            "q": torch.empty((B, proj), dtype=bf, device=dev),
+            "k": torch.empty((B, proj), dtype=bf, device=dev),
+            "v": torch.empty((B, proj), dtype=bf, device=dev),
+            "mla_q": torch.empty((B, s.mla_heads * s.mla_q_head_dim), dtype=bf, device=dev),
+            "mla_kv": torch.empty((B, s.mla_heads * s.mla_kv_head_dim), dtype=bf, device=dev),
+            "h": torch.empty((B, s.hidden), dtype=bf, device=dev),
+            "act": torch.empty((B * (s.top_k + 1), s.moe_intermediate), dtype=bf, device=dev),
+            "routed": torch.empty((B * (s.top_k + 1), s.hidden), dtype=bf, device=dev),
+            "act0": torch.empty((B, s.dense_intermediate), dtype=bf, device=dev),
+            "logits": torch.empty((B, s.vocab_size), dtype=bf, device=dev),
+            "router_logits": [], "idx": [], "weights": [],
+        }
+        prog = StepProgram(B)
+        prev = None
+        xin = x
+        outs = [buf["xa"], buf["xb"]]
+        for li, lw in enumerate(self.layers):
+            xout = outs[li % 2]
+            if lw.kind == "kda":
+                qkv = prog.dense([(xin, *lw.qkv[0], buf["q"]), (xin, *lw.qkv[1], buf["k"]),
+                                  (xin, *lw.qkv[2], buf["v"])], deps=[prev])
+                kda = prog.kda(lw.kda_state, self.kda_q, self.kda_k, self.kda_v, self.kda_decay,
+                               self.kda_beta, s.kda_head_dim ** -0.5, out_bf16=self.kda_out,
+                               deps=[qkv])
+                oproj = prog.dense([(self.kda_out, *lw.o_proj, buf["h"])], deps=[kda])
+            else:
+                qkvb = prog.dense([(xin, *lw.q_proj, buf["mla_q"]),
+                                   (self.mla_latent, *lw.kv_b, buf["mla_kv"])], deps=[prev])
+                oproj = prog.dense([(self.mla_attn, *lw.o_proj, buf["h"])], deps=[qkvb])
+            if lw.dense_mlp is not None:
+                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+                sw = prog.swiglu(buf["h"], (w1p[0], w1s[0]), (w3p[0], w3s[0]), buf["act0"],
+                                 deps=[oproj])
+                prev = prog.dense([(buf["act0"], w2p, w2s, xout)], deps=[sw])
+            else:
+                m = lw.moe
+                lg = torch.empty((B, m.num_experts), dtype=torch.float32, device=dev)
+                idx = torch.empty((B, m.top_k + 1), dtype=torch.long, device=dev)
+                wts = torch.empty((B, m.top_k), dtype=torch.float32, device=dev)
+                buf["router_logits"].append(lg)
+                buf["idx"].append(idx)
+                buf["weights"].append(wts)
+                r = prog.router(buf["h"], m.router_weight, m.router_bias, m.top_k, m.scaling, lg,
+                                idx, wts, deps=[oproj])
+                prev = prog.moe(r, buf["h"], m, buf["act"], buf["routed"], xout, deps=[oproj])
+            xin = xout
+        prog.dense([(xin, *self.lm_head, buf["logits"])], deps=[prev])
+        return prog.finalize(), buf
 
     # -- byte accounting ----------------------------------------------------------------
     def weight_bytes(self) -> int:

@@ -69,3 +69,19 @@ def test_invalid_arguments_return_status_without_launching(library):
     assert status == 6  # KB_ERR_UNSUPPORTED (Dk > 256)
     with pytest.raises(_lib.KernelError, match="KB_ERR_BAD_GROUP"):
         _lib.check("kb_w4a16_dense", 3)
+
+
+def test_step_program_validation_without_gpu(library):
+    import ctypes
+
+    handle = ctypes.c_void_p()
+    assert library.kb_step_create(0, ctypes.byref(handle)) == 6  # KB_ERR_UNSUPPORTED
+    assert library.kb_step_create(9, ctypes.byref(handle)) == 6
+    assert library.kb_step_create(2, None) == 1  # KB_ERR_NULL_POINTER
+    assert library.kb_step_create(2, ctypes.byref(handle)) == 0 and handle.value
+    op = ctypes.c_int(-1)
+    # No problems: rejected before any CUDA call; launching an unfinalized
+    # program is refused.
+    assert library.kb_step_add_dense(handle, None, 1, None, 0, ctypes.byref(op)) == 1
+    assert library.kb_step_launch(handle, None) == 6
+    library.kb_step_destroy(handle)
