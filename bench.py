@@ -6,18 +6,22 @@
 A step is one decode step of the hot path (local_kimi_b200.decode): for all
 27 layers the INT4 attention projections, the KDA recurrent-state step, the
 MoE router/experts/combine, then the INT4 lm_head, over B tokens, with
-random-init weights of the real shapes (about 25 GB, resident in HBM).  The
-step is captured once in a CUDA graph (as the reference engine captures its
-decode step, engine/klinear/generate.py:226-276) and replayed.
+random-init weights of the real shapes (about 25 GB, resident in HBM).
+
+The step runs on the decode-step executor (local_kimi_b200.step: the whole
+program in one persistent launch, batch <= 8); the same step as registry-level
+launches captured in one CUDA graph (as the reference engine captures its
+decode step, engine/klinear/generate.py:226-276) is timed beside it and its
+logits are compared with the executor's (``parity_vs_per_op``).
 
 Printed: one JSON line.  ``value`` = tokens/s over all ranks with inputs
 resident in HBM (device-timed, max over ranks); ``e2e`` = the same metric
 with a host->device copy of the step input and a device->host copy of the
-logits inside the timed region; ``roofline`` = achieved HBM bandwidth of the
-W4A16 projection engine launches of one step, timed alone in their own graph;
-``cpu_baseline`` = the CPU oracle on a bounded sample of the same step.
-Every step reads ~1.8 GB of weights, far more than the 126 MB L2, so no L2
-flush is needed between steps.
+logits inside the timed region; ``roofline`` = algorithmic bytes of the step
+over its time, against the measured HBM copy bandwidth; ``cpu_baseline`` =
+the CPU oracle on a bounded sample of the same step.  Every step reads ~1.7 GB
+of weights, far more than the 126 MB L2, so no L2 flush is needed between
+steps.
 
 ``--impl reference`` times the reference's CPU path restated in ``oracle/``
 (the reference is pure Python/torch and does not exist on the GPU box) on all
@@ -58,7 +62,11 @@ def _args() -> argparse.Namespace:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--case", choices=("step", "lm_head", "moe", "eager"), default="step",
+    ap.add_argument("--path", choices=("executor", "per-op"), default="executor",
+                    help="executor: the whole step in one persistent launch (batch <= 8); "
+                         "per-op: the registry-level launches captured in a CUDA graph")
+    ap.add_argument("--case", choices=("step", "lm_head", "moe", "eager", "program"),
+                    default="step",
                     help="step = the benchmark; the others run one op family eagerly for "
                          "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
                          "combine of one layer; eager: uncaptured decode steps)")
@@ -321,13 +329,34 @@ def _time_graph(g, steps: int, warmup: int) -> float:
     return start.elapsed_time(end) / 1e3 / steps
 
 
+def _time_launches(fn, steps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / 1e3 / steps
+
+
+def _max_over_ranks(value: float, dist) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
     import __graft_entry__ as entry
 
     entry.build()
-    from local_kimi_b200 import _lib, ops
+    from local_kimi_b200 import _lib
     from local_kimi_b200.decode import HotPathDecoder
-    from local_kimi_b200.moe import moe_forward  # noqa: F401
+    from local_kimi_b200.step import MAX_TOKENS
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -341,50 +370,44 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
     counts = model.touched_experts(model.x0)
+    bytes_step = model.step_bytes(counts)
     static_x = model.x0.clone()
-    graph, static_out = _capture(model.step, static_x)
+    use_executor = args.path == "executor" and args.batch <= MAX_TOKENS
 
-    # Engine-only graph: the same W4A16 projection launches with routing fixed
-    # to what the step computes, for the roofline of the projection engine.
-    routes = []
+    # Per-operation path: the step's registry-level launches in one CUDA graph.
+    graph, graph_out = _capture(model.step, static_x)
+    per_op_s = _max_over_ranks(_time_graph(graph, max(10, args.steps // 2), 3), dist)
 
-    def engine_only(x):
-        i = 0
-        for lw in model.layers:
-            if lw.kind == "kda":
-                ops.w4a16_dense_multi([(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
-                h = ops.w4a16_dense(model.kda_out, *lw.o_proj)
-            else:
-                _, _, h = ops.w4a16_dense_multi([(x, *lw.q_proj), (model.mla_latent, *lw.kv_b),
-                                                (model.mla_attn, *lw.o_proj)])
-            if lw.dense_mlp is not None:
-                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
-                act = ops.w4a16_swiglu(h, model.dense_idx, w1p, w1s, w3p, w3s)
-                x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
-            else:
-                stable, wts = routes[i]
-                m = lw.moe
-                act = ops.w4a16_swiglu(h, stable, m.w1_packed, m.w1_scales, m.w3_packed,
-                                       m.w3_scales)
-                x = ops.moe_down_combine(act, stable, wts, m.w2_packed, m.w2_scales)
-                i += 1
-        return ops.w4a16_dense(x, *model.lm_head)
+    if use_executor:
+        prog, buf = model.build_program(static_x)
+        out_buf = buf["logits"]
+        # Parity of the two paths on one step from the same KDA states.
+        states = [lw.kda_state.clone() for lw in model.layers if lw.kda_state is not None]
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = graph_out.float().clone()
+        for lw, st in zip([lw for lw in model.layers if lw.kda_state is not None], states):
+            lw.kda_state.copy_(st)
+        prog.launch()
+        torch.cuda.synchronize()
+        diff = (out_buf.float() - ref).abs()
+        tol = torch.maximum(torch.full_like(ref, 1e-3), 2e-2 * ref.abs())
+        parity = float((diff <= tol).float().mean().item())
+        step_fn = prog.launch
+        launches = 1
+        path = "executor"
+    else:
+        out_buf = graph_out
+        step_fn = graph.replay
+        launches = model.launches_per_step
+        parity = None
+        path = "per-op graph"
 
-    for lw in model.layers:
-        if lw.moe is not None:
-            h = (ops.w4a16_dense(model.kda_out, *lw.o_proj) if lw.kind == "kda"
-                 else ops.w4a16_dense(model.mla_attn, *lw.o_proj))
-            routes.append(ops.moe_router(h, lw.moe.router_weight, lw.moe.router_bias,
-                                         lw.moe.top_k, routed_scaling_factor=lw.moe.scaling,
-                                         append_expert=lw.moe.num_experts))
-    eng_graph, _ = _capture(engine_only, static_x)
-
-    # Timed region: K replays of the full step.
+    # Timed region: K steps.
     if dist is not None:
         dist.barrier()
-    torch.cuda.synchronize()
     for _ in range(args.warmup):
-        graph.replay()
+        step_fn()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -393,46 +416,27 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for _ in range(args.steps):
-            graph.replay()
+            step_fn()
         end.record()
         torch.cuda.synchronize()
-    step_s = start.elapsed_time(end) / 1e3 / args.steps
+    step_s = _max_over_ranks(start.elapsed_time(end) / 1e3 / args.steps, dist)
     if dist is not None:
-        t = torch.tensor([step_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_s = float(t.item())
         dist.barrier()
 
     # End to end: pinned host input in, logits out, every step.
     host_x = torch.empty(static_x.shape, dtype=static_x.dtype, pin_memory=True)
     host_x.copy_(model.x0.cpu())
-    host_out = torch.empty(static_out.shape, dtype=static_out.dtype, pin_memory=True)
-    for _ in range(2):
-        static_x.copy_(host_x, non_blocking=True)
-        graph.replay()
-        host_out.copy_(static_out, non_blocking=True)
-    torch.cuda.synchronize()
-    e2e_steps = max(1, args.steps)
-    start.record()
-    for _ in range(e2e_steps):
-        static_x.copy_(host_x, non_blocking=True)
-        graph.replay()
-        host_out.copy_(static_out, non_blocking=True)
-    end.record()
-    torch.cuda.synchronize()
-    e2e_s = start.elapsed_time(end) / 1e3 / e2e_steps
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    host_out = torch.empty(out_buf.shape, dtype=out_buf.dtype, pin_memory=True)
 
-    # Roofline of the projection engine (its launches alone, same inputs).
-    eng_s = _time_graph(eng_graph, max(10, args.steps // 2), 3)
-    bytes_step = model.step_bytes(counts)
-    eng_bytes = (bytes_step["dense_proj"] + bytes_step["experts"] + bytes_step["lm_head"]
-                 + bytes_step["activations"])
+    def e2e_step():
+        static_x.copy_(host_x, non_blocking=True)
+        step_fn()
+        host_out.copy_(out_buf, non_blocking=True)
+
+    e2e_s = _max_over_ranks(_time_launches(e2e_step, max(1, args.steps), 2), dist)
+
     peak, peak_src = _peak_hbm()
-    achieved = eng_bytes / eng_s / 1e9
+    achieved = bytes_step["total"] / step_s / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -440,7 +444,6 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         cpu = {"value": round(args.batch / cpu_s, 4), "unit": "tok/s", "cores": cores,
                "kind": "port", "sample": sample, "seconds_per_step": round(cpu_s, 3)}
 
-    launches = model.launches_per_step
     out = {
         "metric": METRIC,
         "value": round(world * args.batch / step_s, 2),
@@ -462,32 +465,34 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
             "batch": args.batch,
             "group_size": args.group,
             "layers": model.nlayers,
+            "path": path,
             "parallelism": f"replicas{world}" if world > 1 else "single",
             "weights_gb": round(model.weight_bytes() / 1e9, 2),
             "bytes_per_step": bytes_step["total"],
-            "l2": "inputs larger than L2 (each step streams ~1.8 GB of weights)",
-            "cuda_graph": True,
-            "pdl": not args.no_pdl,
+            "l2": "inputs larger than L2 (each step streams ~1.7 GB of weights)",
         },
         "e2e": {"value": round(world * args.batch / e2e_s, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": None, "kernel": "w4a16_engine (all INT4 projections of a step)",
-                     "peak_source": peak_src,
-                     "bytes_per_step": eng_bytes, "ms_per_step": round(eng_s * 1e3, 4),
-                     "frac_of_step": round(eng_s / step_s, 3)},
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": ("step_kernel (the whole step in one launch)" if use_executor
+                                else "all launches of the step"),
+                     "peak_source": peak_src, "bytes_per_launch": bytes_step["total"]},
         "gpu_launches": launches * args.steps,
         "launches_per_step": launches,
+        "per_op_graph": {"ms_per_step": round(per_op_s * 1e3, 4),
+                         "value": round(world * args.batch / per_op_s, 2),
+                         "launches_per_step": model.launches_per_step},
         "step_bytes": bytes_step,
-        "hbm_gbs_step": round(bytes_step["total"] / step_s / 1e9, 1),
         "clocks": clocks.summary(),
     }
+    if parity is not None:
+        out["parity_vs_per_op"] = round(parity, 6)
     if cpu is not None:
         out["cpu_baseline"] = cpu
     if dist is not None:
-        del graph, eng_graph
+        del graph
         dist.destroy_process_group()
     return out if rank == 0 else None
 
@@ -558,6 +563,12 @@ def run_case(args) -> dict:
         fn = lambda: moe_forward(x, layer)  # noqa: E731
         nbytes = None
         per_step = 3
+    elif args.case == "program":
+        model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
+        prog, _ = model.build_program(model.x0.clone())
+        fn = prog.launch
+        nbytes = model.step_bytes(model.touched_experts(model.x0))["total"]
+        per_step = 1
     else:
         model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
         fn = lambda: model.step(x)  # noqa: E731

@@ -274,6 +274,12 @@ KB_API int kb_step_finalize(kb_step* step);
 KB_API int kb_step_launch(kb_step* step, void* stream);
 KB_API int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage_bytes,
                    size_t* smem_bytes);
+/* Optional timeline: with a device buffer of kb_step_trace_entries() int64   */
+/* set, every launch records %globaltimer ns per (CTA, operation): consumers  */
+/* start, inputs ready, routing built (expert blocks), end, and the time the  */
+/* producer finished issuing the operation's weights.  NULL switches it off.  */
+KB_API int kb_step_set_trace(kb_step* step, int64_t* trace, int64_t entries);
+KB_API int64_t kb_step_trace_entries(const kb_step* step);
 
 #ifdef __cplusplus
 }

@@ -127,6 +127,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
          ctypes.POINTER(c_size_t)],
     ),
+    "kb_step_set_trace": (c_int, [c_void_p, c_void_p, c_int64]),
+    "kb_step_trace_entries": (c_int64, [c_void_p]),
     "kb_kda_decode_step": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -119,7 +119,8 @@ __device__ __forceinline__ void kblock_mma(uint4 WA, uint4 WB, uint32_t sa2, uin
 // srow: scale rows of this row block (shared or global memory, generic loads).
 // D fragment: acc[p][0] = (row g, token 2t), [1] = (row g, token 2t+1),
 // [2] = (row g+8, token 2t), [3] = (row g+8, token 2t+1).
-template <int NSUB>
+// SMEM_SCALES: srow is known to point into shared memory (explicit shared loads).
+template <int NSUB, bool SMEM_SCALES = false>
 __device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
                                                  const uint16_t* srow, int ng, int rows_valid,
                                                  int K, int gshift, int kb0, int kb1,
@@ -146,12 +147,12 @@ __device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
   const uint8_t* px[NSUB];
 #pragma unroll
   for (int p = 0; p < NSUB; ++p) px[p] = xrow[p] + c * 16;
-#pragma unroll 1
+#pragma unroll 2
   for (int kb = kb0; kb < kbf; ++kb) {
     const uint4 WA = lds_v4(pa);
     const uint4 WB = lds_v4(pb);
-    const uint32_t sa = sA[c >> gshift];
-    const uint32_t sb = sB[c >> gshift];
+    const uint32_t sa = SMEM_SCALES ? lds_u16(sA + (c >> gshift)) : sA[c >> gshift];
+    const uint32_t sb = SMEM_SCALES ? lds_u16(sB + (c >> gshift)) : sB[c >> gshift];
     kblock_mma<NSUB>(WA, WB, prmt(sa, 0, 0x1010), prmt(sb, 0, 0x1010), px, NC16, nact, acc,
                      acc2);
     pa += 64;

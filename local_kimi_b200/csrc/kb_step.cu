@@ -58,6 +58,12 @@ constexpr int ST_RT_EXPERTS = 8;          // router experts per item (two warps 
 constexpr int ST_KDA_COLS = 32;
 constexpr int ST_STAGE_TARGET = 40 * 1024;  // preferred bytes per item
 constexpr long long ST_WAIT_NS = 2000000000LL;  // 2 s per wait
+// Timeline fields per (CTA, operation): consumers start, inputs ready,
+// mid-point (routing built for expert blocks), end; producer done issuing.
+constexpr int ST_TRACE_FIELDS = 5;
+constexpr int ST_THREADS = NCT + 64;  // consumers, producer warp (NCW), reducer warp (NCW+1)
+constexpr int ST_NB = 4;              // partial-sum buffers between consumers and reducer
+constexpr int EXIT_BAR = 2;           // named barrier: consumers + reducer
 
 struct StDense {
   const uint16_t* x;
@@ -132,7 +138,9 @@ struct StepParams {
   uint32_t* err;
   int stages, stage_bytes;
   int ring_off, red_off, scr_off, bar_off;
-  int tstride_max;
+  int part_bytes;  // partial-sum buffers at red_off
+  int T;
+  long long* trace;  // optional timeline [grid][nops][ST_TRACE_FIELDS] of %globaltimer ns
 };
 
 // Per-CTA routing state and plan (shared memory scratch).
@@ -148,6 +156,7 @@ struct StPlan {
   int done_tok[ST_MAX_T];
   int abort;
   int last;
+  int cur_op;  // operation the consumers are in (timeline)
 };
 
 struct StKda {
@@ -170,6 +179,11 @@ __device__ __forceinline__ long long now_ns() {
   return t;
 }
 
+__device__ __forceinline__ void trace_mark(const StepParams& P, int op, int field) {
+  if (P.trace)
+    P.trace[((size_t)blockIdx.x * P.nops + op) * ST_TRACE_FIELDS + field] = now_ns();
+}
+
 __device__ __forceinline__ void raise_abort(const StepParams& P, StPlan* pl, uint32_t bits) {
   atomicOr(P.err, bits);
   atomicExch(&P.sync[P.abort_idx], 1);
@@ -185,6 +199,7 @@ __device__ void consumers_wait(const StepParams& P, StPlan* pl, int idx, int tar
     const long long t0 = now_ns();
     int spins = 0;
     while (ld_acquire(&P.sync[idx]) < target) {
+      __nanosleep(64);
       if (((++spins) & 15) == 0) {
         if (*((volatile int*)&P.sync[P.abort_idx]) != 0) {
           pl->abort = 1;
@@ -206,19 +221,24 @@ __device__ void wait_deps(const StepParams& P, StPlan* pl, const StOp& op) {
     consumers_wait(P, pl, dop.done, dop.target);
   }
   if (op.ndeps == 0) named_barrier(CBAR, NCT);
+  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 1);
+}
+
+// Release reduction at GPU scope: the add becomes visible after every write
+// that happens before it (cumulative release).
+__device__ __forceinline__ void red_release(int* counter, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(counter), "r"(v) : "memory");
 }
 
 // Release: the writes of this warp (ordered by __syncwarp) before the add.
 __device__ __forceinline__ void warp_signal(int* counter, int v) {
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) {
-    __threadfence();
-    atomicAdd(counter, v);
-  }
+  if ((threadIdx.x & 31) == 0) red_release(counter, v);
 }
 
 // Bounded mbarrier wait that also gives up when the CTA is aborting.
 __device__ bool stage_wait(uint64_t* bar, uint32_t parity, const StPlan* pl) {
+  if (mbar_test_wait(bar, parity)) return true;
   const long long t0 = now_ns();
   int spins = 0;
   while (!mbar_try_wait(bar, parity)) {
@@ -350,16 +370,24 @@ struct Ring {
   uint64_t* full;
   uint64_t* empty;
   int stages, stage_bytes;
-  int use;
+  int use;     // stages used so far
+  int slot;    // use % stages
+  uint32_t phase;  // (use / stages) & 1
+  __device__ __forceinline__ void advance() {
+    ++use;
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
 };
 
 __device__ bool ring_acquire(Ring& R, const StPlan* pl, uint8_t** stage, uint64_t** full) {
-  const int s = R.use % R.stages;
-  const uint32_t ph = (R.use / R.stages) & 1;
-  if (!stage_wait(&R.empty[s], ph ^ 1, pl)) return false;
+  const int s = R.slot;
+  if (!stage_wait(&R.empty[s], R.phase ^ 1u, pl)) return false;
   *stage = R.base + (size_t)s * R.stage_bytes;
   *full = &R.full[s];
-  ++R.use;
+  R.advance();
   return true;
 }
 
@@ -374,6 +402,7 @@ __device__ void producer_main(const StepParams& P, StPlan* pl, Ring& R, uint64_t
     const StOp& op = P.ops[o];
     uint8_t* stage;
     uint64_t* full;
+    if (o > 0 && lane == 0) trace_mark(P, o - 1, 4);
     if (op.type == OP_DENSE) {
       const int n = op.p[op.nprob - 1].item_begin + op.p[op.nprob - 1].items;
       for (int i = first_item(op.rot); i < n && ok; i += G) {
@@ -453,20 +482,24 @@ __device__ void producer_main(const StepParams& P, StPlan* pl, Ring& R, uint64_t
 // Consumers: projection items.
 // ---------------------------------------------------------------------------
 struct Split {
-  int mat, rb, ks, rb_rows;
+  int mat, rb, ks, rb_rows;  // ks: the reduction slice this warp computes
+  int slot;                 // partial slot mat*RBc*KS + rb*KS + ks
   const uint8_t* wtile;
   const uint16_t* srow;
 };
 
-__device__ __forceinline__ Split split_of(const Item& it, const uint8_t* stage) {
+// rot rotates the reduction slices over the KS warps of a row block (KS is a
+// power of two); every consumer passes the same value for an item.
+__device__ __forceinline__ Split split_of(const Item& it, const uint8_t* stage, int rot = 0) {
   const int warp = threadIdx.x >> 5;
   Split sp;
   const int per_mat = it.RBc * it.KS;
   sp.mat = warp / per_mat;
   const int rem = warp - sp.mat * per_mat;
   sp.rb = rem / it.KS;
-  sp.ks = rem - sp.rb * it.KS;
+  sp.ks = ((rem - sp.rb * it.KS) + rot) & (it.KS - 1);
   sp.rb_rows = min(16, it.rows - sp.rb * 16);
+  sp.slot = sp.mat * per_mat + sp.rb * it.KS + sp.ks;
   sp.wtile = stage + (sp.mat * it.RBc * 16 + sp.rb * 16) * it.RS;
   sp.srow = it.scale_bulk
                 ? reinterpret_cast<const uint16_t*>(stage + stage_scale_offset(it) +
@@ -488,38 +521,86 @@ __device__ __forceinline__ void split_compute(const Item& it, const Split& sp,
                         xrow, 1, acc);
 }
 
-// Reduction of the KS slices through shared memory; the reducing warps
-// (mat 0, ks 0) get v0 (and v1 = the second matrix for gate/up) and return
-// true.  D fragment: element i is row g + 8*(i>>1), token 2t + (i&1).
-__device__ __forceinline__ bool split_reduce(const Item& it, const Split& sp, float* red,
-                                             int& rslot, const float (&acc)[1][4], float (&v0)[4],
-                                             float (&v1)[4]) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* rbuf = red + rslot * (NCW * 128);
-  rslot ^= 1;
-  *reinterpret_cast<float4*>(rbuf + (warp * 32 + lane) * 4) =
-      make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-  named_barrier(CBAR, NCT);
-  if (!(sp.mat == 0 && sp.ks == 0 && sp.rb_rows > 0)) return false;
-  const int per_mat = it.RBc * it.KS;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) v0[i] = v1[i] = 0.f;
-  for (int k2 = 0; k2 < it.KS; ++k2) {
-    const float4 pv = *reinterpret_cast<const float4*>(rbuf + ((warp + k2) * 32 + lane) * 4);
-    v0[0] += pv.x;
-    v0[1] += pv.y;
-    v0[2] += pv.z;
-    v0[3] += pv.w;
-    if (it.mats == 2) {
-      const float4 uv =
-          *reinterpret_cast<const float4*>(rbuf + ((warp + per_mat + k2) * 32 + lane) * 4);
-      v1[0] += uv.x;
-      v1[1] += uv.y;
-      v1[2] += uv.z;
-      v1[3] += uv.w;
+// Partial sums of an item's warps are handed to the reducer warp through a
+// small ring of shared-memory buffers: every consumer warp stores the partial
+// of its (matrix, row block, reduction slice) and arrives on the buffer's
+// `done` mbarrier (count NCW); the reducer waits for it, sums the slices of
+// each row block in fixed order (so results do not depend on timing), writes
+// the outputs and arrives on `free` (count 1) so the buffer can be refilled.
+struct Partials {
+  float* buf;      // [ST_NB][NCW slots][16 rows][T tokens]
+  uint64_t* done;  // [ST_NB]
+  int* taken;      // items the reducer has finished reading (release store by the reducer)
+  int T;
+  int slot;
+  uint32_t phase;
+  int count;       // items published (consumers) or taken (reducer) so far
+  __device__ __forceinline__ void advance() {
+    if (++slot == ST_NB) {
+      slot = 0;
+      phase ^= 1u;
     }
   }
-  return true;
+  __device__ __forceinline__ float* cur() const { return buf + (size_t)slot * NCW * 16 * T; }
+};
+
+// Consumer side: store this warp's partial in slot `pslot` (matrix*RBc*KS +
+// rb*KS + reduction slice) and arrive.  D fragment element e is row
+// g + 8*(e>>1), token 2t + (e&1).
+__device__ __forceinline__ int ld_acquire_cta_shared(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_cta_shared(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void partial_publish(const StepParams& P, Partials& pa, StPlan* pl,
+                                                int pslot, int ntok, const float (&acc)[1][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // The buffer is free once the reducer has taken the item published ST_NB ago.
+  if (pa.count >= ST_NB && ld_acquire_cta_shared(pa.taken) <= pa.count - ST_NB) {
+    const long long t0 = now_ns();
+    while (ld_acquire_cta_shared(pa.taken) <= pa.count - ST_NB) {
+      if (*((volatile const int*)&pl->abort) != 0 || now_ns() - t0 > ST_WAIT_NS) {
+        if (lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  ++pa.count;
+  float* base = pa.cur() + (size_t)pslot * 16 * pa.T;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int row = g + ((e >> 1) << 3), tok = 2 * t + (e & 1);
+    if (tok < ntok) base[row * pa.T + tok] = acc[0][e];
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&pa.done[pa.slot]);
+  pa.advance();
+}
+
+// Reducer side: wait for the next item's partials (false when aborting).
+__device__ __forceinline__ bool partial_take(Partials& pa, const StPlan* pl) {
+  return stage_wait(&pa.done[pa.slot], pa.phase, pl);
+}
+
+__device__ __forceinline__ void partial_release(Partials& pa) {
+  __syncwarp();
+  ++pa.count;
+  if ((threadIdx.x & 31) == 0) st_release_cta_shared(pa.taken, pa.count);
+  pa.advance();
+}
+
+// Sum of the KS slices of row block rb (matrix m) at (row, tok).
+__device__ __forceinline__ float partial_sum(const Partials& pa, int m, int RBc, int KS, int rb,
+                                             int row, int tok) {
+  const float* base = pa.cur() + ((size_t)(m * RBc * KS + rb * KS) * 16 + row) * pa.T + tok;
+  float v = 0.f;
+  for (int k2 = 0; k2 < KS; ++k2) v += base[(size_t)k2 * 16 * pa.T];
+  return v;
 }
 
 // Waits for the next ring stage.  A failed wait records the error and the
@@ -527,9 +608,9 @@ __device__ __forceinline__ bool split_reduce(const Item& it, const Split& sp, fl
 // garbage), so every warp keeps the same sequence of barriers.
 __device__ __forceinline__ const uint8_t* consume_stage(const StepParams& P, Ring& R,
                                                         StPlan* pl, int* slot) {
-  const int s = R.use % R.stages;
-  const uint32_t ph = (R.use / R.stages) & 1;
-  ++R.use;
+  const int s = R.slot;
+  const uint32_t ph = R.phase;
+  R.advance();
   *slot = s;
   if (!stage_wait(&R.full[s], ph, pl) && (threadIdx.x & 31) == 0 && !pl->abort)
     raise_abort(P, pl, ERR_TIMEOUT);
@@ -545,8 +626,8 @@ __device__ __forceinline__ void release_stage(Ring& R, int s) {
 // Consumer operations.
 // ---------------------------------------------------------------------------
 __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
-                          float* red, int& rslot) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+                          Partials& pa) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
   wait_deps(P, pl, op);
   for (int p = 0; p < op.nprob; ++p) {
@@ -560,21 +641,67 @@ __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring&
       stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
   }
   named_barrier(CBAR, NCT);
-  int* done = &P.sync[op.done];
-  for (int i = first_item(op.rot); i < op.items; i += G) {
-    Item it;
-    st_describe_dense(op, i, it);
-    const StDense& D = op.p[it.p];
-    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-    Split sp;
+  const int warp = threadIdx.x >> 5;
+  const int f = first_item(op.rot);
+  for (int p = 0; p < op.nprob; ++p) {
+    const StDense& D = op.p[p];
+    // This CTA's items of problem p: i = f (mod G) within the problem's range.
+    const int ib = D.item_begin, ie = D.item_begin + D.items;
+    int i = ib + ((f - ib) % G + G) % G;
     if (D.nchunk == 1) {
-      const uint8_t* xrow[1] = {xs + D.x_off + min(g, op.T - 1) * token_stride(D.K)};
-      int s;
-      const uint8_t* stage = consume_stage(P, R, pl, &s);
-      sp = split_of(it, stage);
-      split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
-      release_stage(R, s);
-    } else {
+      // Per-problem constants of this warp's part of an item.
+      const int K = D.K, N = D.N, RBc = D.RBc, KS = D.KS, mats = D.mats;
+      const int ng = K >> (5 + D.gshift);
+      const int RS = K >> 1;
+      const int per_mat = RBc * KS;
+      const int mat = warp / per_mat;
+      const int rem = warp - mat * per_mat;
+      const int rb = rem / KS, ks = rem - rb * KS;
+      const int KB = K >> 7;
+      int rot = 0;  // reduction slice of this warp = (ks + rot) % KS, rot advancing per item
+      const int item_rows = RBc * 16;
+      const int wt_off = (mat * item_rows + rb * 16) * RS;
+      const int sc_off = mats * item_rows * RS;
+      const int sc_stride = (item_rows * ng * 2 + 15) / 16 * 16;
+      const uint16_t* sglob = mat ? D.s3 : D.s;
+      const uint8_t* xrow[1] = {xs + D.x_off + min(g, op.T - 1) * token_stride(K)};
+      const bool base_ok = (reinterpret_cast<uintptr_t>(D.s) % 16 == 0) &&
+                           (mats == 1 || reinterpret_cast<uintptr_t>(D.s3) % 16 == 0);
+      for (; i < ie; i += G) {
+        const int r0 = (i - ib) * item_rows;
+        const int rows = min(item_rows, N - r0);
+        const int rb_rows = min(16, rows - rb * 16);
+        int st;
+        const uint8_t* stage = consume_stage(P, R, pl, &st);
+        const bool bulk = base_ok && ((rows * ng * 2) % 16 == 0);
+        const uint16_t* srow =
+            bulk ? reinterpret_cast<const uint16_t*>(stage + sc_off + mat * sc_stride) +
+                       rb * 16 * ng
+                 : sglob + (size_t)(r0 + rb * 16) * ng;
+        // Slices of unequal length rotate over the warps from item to item, so
+        // the ring's slack evens the load out.
+        const int ksr = (ks + rot) & (KS - 1);
+        rot = (rot + 1) & (KS - 1);
+        const int kb0 = KB * ksr / KS, kb1 = KB * (ksr + 1) / KS;
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        if (rb_rows > 0 && kb1 > kb0) {
+          if (bulk)
+            rowblock_compute<1, true>(stage + wt_off, RS, srow, ng, rb_rows, K, D.gshift, kb0,
+                                      kb1, xrow, 1, acc);
+          else
+            rowblock_compute<1>(stage + wt_off, RS, srow, ng, rb_rows, K, D.gshift, kb0, kb1,
+                                xrow, 1, acc);
+        }
+        release_stage(R, st);
+        partial_publish(P, pa, pl, mat * per_mat + rb * KS + ksr, op.T, acc);
+      }
+      continue;
+    }
+    for (; i < ie; i += G) {
+      Item it;
+      st_describe_dense(op, i, it);
+      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+      Split sp;
       // Reduction chunks of kc columns: each stage holds kc/2 bytes of every
       // row; the activations of the chunk are staged in a chunk-local layout
       // and the chunk is contracted as a problem of width kc.
@@ -584,38 +711,27 @@ __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring&
       Item ic = it;
       ic.K = kc;
       const uint8_t* xrow[1] = {xs + min(g, op.T - 1) * tsc};
+      const int crot = (i / G) & (D.KS - 1);
       for (int ci = 0; ci < D.nchunk; ++ci) {
         named_barrier(CBAR, NCT);
         for (int m = 0; m < op.T; ++m)
           stage_row_cg(xs + m * tsc, D.x + (size_t)m * D.xs + (size_t)ci * kc, kc, threadIdx.x,
                        NCT);
         named_barrier(CBAR, NCT);
-        int s;
-        const uint8_t* stage = consume_stage(P, R, pl, &s);
-        sp = split_of(ic, stage);
+        int st;
+        const uint8_t* stage = consume_stage(P, R, pl, &st);
+        sp = split_of(ic, stage, crot);
         sp.srow += ci * gpc;
         split_compute(ic, sp, sp.wtile, 0, (kc + 127) >> 7, xrow, acc);
-        release_stage(R, s);
+        release_stage(R, st);
       }
-    }
-    float v0[4], v1[4];
-    if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
-        const int tok = 2 * t + (e & 1);
-        if (rloc < it.rows && tok < op.T) {
-          const float val = (D.mats == 2) ? swiglu_contract(v0[e], v1[e]) : v0[e];
-          D.y[(size_t)tok * D.ys + it.r0 + rloc] = float_to_bf16_bits(val);
-        }
-      }
-      warp_signal(done, 1);
+      partial_publish(P, pa, pl, sp.slot, op.T, acc);
     }
   }
 }
 
-__device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
-                           float* red, int& rslot) {
+__device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
+                           uint8_t* xs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
   wait_deps(P, pl, op);
@@ -629,7 +745,8 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
   int* done = &P.sync[op.done];
   // Warp j < 8 computes expert i*8 + j over the whole row in the order of the
   // router kernel (lane-strided 16-byte words, a xor butterfly), so logits
-  // equal kb_router_topk's bit for bit; warps 8..15 only keep the barriers.
+  // equal kb_router_topk's bit for bit; warps 8..15 only release the stages.
+  int experts = 0;
   for (int i = first_item(op.rot); i < op.items; i += G) {
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
@@ -663,14 +780,12 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
         for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
         if (lane == 0 && m < op.T) op.logits[(size_t)m * op.E + e] = acc[m];
       }
-      release_stage(R, s);
-      warp_signal(done, 1);
-    } else {
-      release_stage(R, s);
     }
+    release_stage(R, s);
+    experts += min(ST_RT_EXPERTS, op.E - i * ST_RT_EXPERTS);
   }
-  (void)red;
-  (void)rslot;
+  named_barrier(CBAR, NCT);
+  if (threadIdx.x == 0 && experts > 0) red_release(done, experts);
 }
 
 // Top-k for every token (warp per token) and the expert plan (warp 0), in
@@ -764,13 +879,14 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
     __syncwarp();
     for (int sl = 1 + lane; sl < nslot; sl += 32) pl->slot_of[pl->slot_expert[sl]] = -1;
   }
+  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 2);
   named_barrier(CBAR, NCT);
 }
 
-// Gate/up + SwiGLU of one item; signals the slot counter per reducing warp.
+// Gate/up of one item (the reducer applies SwiGLU, writes and signals).
 __device__ void moe_up_item(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
-                            const uint8_t* xs, float* red, int& rslot, const Item& it) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+                            const uint8_t* xs, Partials& pa, const Item& it, int rot) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
   const int ts = token_stride(op.K);
   const int m = min(g, it.count - 1);
   const int a = pl->assign[it.abase + m];
@@ -778,28 +894,15 @@ __device__ void moe_up_item(const StepParams& P, const StOp& op, StPlan* pl, Rin
   float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
   int s;
   const uint8_t* stage = consume_stage(P, R, pl, &s);
-  const Split sp = split_of(it, stage);
+  const Split sp = split_of(it, stage, rot);
   split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
   release_stage(R, s);
-  float v0[4], v1[4];
-  if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
-      const int tok = 2 * t + (e & 1);
-      if (rloc < it.rows && tok < it.count) {
-        const int aa = pl->assign[it.abase + tok];
-        op.y[(size_t)aa * op.N + it.r0 + rloc] =
-            float_to_bf16_bits(swiglu_contract(v0[e], v1[e]));
-      }
-    }
-    warp_signal(&P.sync[op.slot_cnt + it.p], 1);
-  }
+  partial_publish(P, pa, pl, sp.slot, it.count, acc);
 }
 
 __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
                            uint64_t* plan_bar, uint64_t* plan_ack, uint32_t& plan_round,
-                           uint8_t* xs, float* red, int& rslot) {
+                           uint8_t* xs, Partials& pa) {
   const int G = gridDim.x;
   wait_deps(P, pl, op);
   const int ts = token_stride(op.K);
@@ -816,10 +919,12 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
   }
   named_barrier(CBAR, NCT);
   int i = first_item(op.rot);
+  int rot = 0;
   for (; i < op.items_rb; i += G) {
     Item it;
     st_describe_shared(op, i, it);
-    moe_up_item(P, op, pl, R, xs, red, rslot, it);
+    moe_up_item(P, op, pl, R, xs, pa, it, rot);
+    rot = (rot + 1) & (op.KS - 1);
   }
   // The producer must be done with the previous plan before it is replaced.
   if (plan_round > 0) {
@@ -834,23 +939,27 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
   for (; i < n; i += G) {
     Item it;
     st_describe_moe(op, pl, i, it);
-    moe_up_item(P, op, pl, R, xs, red, rslot, it);
+    moe_up_item(P, op, pl, R, xs, pa, it, rot);
+    rot = (rot + 1) & (op.KS - 1);
   }
 }
 
+// Down projection of every route (consumer side; the reducer writes the
+// per-route outputs and runs the combine).
 __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
-                             uint8_t* xs, float* red, int& rslot) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+                             uint8_t* xs, Partials& pa) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
   const int n = pl->nslots * op.items_rb;
   const int ts = token_stride(op.K);
-  const int top_k = op.R - 1;
+  int rot = 0;
   for (int i = first_item(op.rot); i < n; i += G) {
     Item it;
     st_describe_moe(op, pl, i, it);
     // Inputs: the activated rows of this slot, complete once every row block
     // of the slot's gate/up has been signalled.
     consumers_wait(P, pl, op.slot_cnt + it.p, op.up_rb);
+    if (threadIdx.x == 0 && i < G) trace_mark(P, pl->cur_op, 1);
     for (int m = 0; m < it.count; ++m)
       stage_row_cg(xs + m * ts, op.mx + (size_t)pl->assign[it.abase + m] * op.mxs, op.K,
                    threadIdx.x, NCT);
@@ -859,58 +968,15 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
-    const Split sp = split_of(it, stage);
+    const Split sp = split_of(it, stage, rot);
+    rot = (rot + 1) & (op.KS - 1);
     split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
     release_stage(R, s);
-    float v0[4], v1[4];
-    if (split_reduce(it, sp, red, rslot, acc, v0, v1)) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rloc = sp.rb * 16 + g + ((e >> 1) << 3);
-        const int tok = 2 * t + (e & 1);
-        if (rloc < it.rows && tok < it.count) {
-          const int aa = pl->assign[it.abase + tok];
-          op.wsy[(size_t)aa * op.N + it.r0 + rloc] = float_to_bf16_bits(v0[e]);
-        }
-      }
-    }
-    // Arrival per (token, row group): the CTA that brings the count to R
-    // combines the routes in route order.
+    partial_publish(P, pa, pl, sp.slot, it.count, acc);
+    // xs is restaged for the next item only after every warp is done with it.
     named_barrier(CBAR, NCT);
-    const int rbg = it.r0 / (op.RBc * 16);
-    if (threadIdx.x == 0) {
-      __threadfence();
-      for (int m = 0; m < it.count; ++m) {
-        const int tok = pl->assign[it.abase + m] / op.R;
-        const int old = atomicAdd(&P.sync[op.arrive + tok * op.items_rb + rbg], 1);
-        pl->done_tok[m] = (old == op.R - 1) ? tok : -1;
-      }
-      __threadfence();
-    }
-    named_barrier(CBAR, NCT);
-    int ndone = 0;
-    for (int m = 0; m < it.count; ++m) {
-      const int tok = pl->done_tok[m];
-      if (tok < 0) continue;
-      ++ndone;
-      for (int rl = threadIdx.x; rl < it.rows; rl += NCT) {
-        const int row = it.r0 + rl;
-        float accum = 0.f;
-        for (int r = 0; r < top_k; ++r) {
-          const uint16_t ov = __ldcg(&op.wsy[((size_t)tok * op.R + r) * op.N + row]);
-          accum += bf16_bits_to_float(ov) * pl->route_w[tok * top_k + r];
-        }
-        const uint16_t sv = __ldcg(&op.wsy[((size_t)tok * op.R + op.R - 1) * op.N + row]);
-        op.out[(size_t)tok * op.N + row] =
-            float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
-      }
-    }
-    named_barrier(CBAR, NCT);
-    if (threadIdx.x == 0 && ndone > 0) {
-      __threadfence();
-      atomicAdd(&P.sync[op.done], ndone);
-    }
   }
+  (void)lane;
 }
 
 // Warps 0..7 own rows i = r*8 + warp (r < 16) of a 32-column slice, as the
@@ -924,6 +990,7 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
   const bool worker = warp < KW;
   const int nsl = (op.Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
   bool waited = false;
+  int units = 0;
   for (int u = first_item(op.rot); u < op.items; u += G) {
     const int bh = u / nsl, sl = u - bh * nsl;
     const int b = bh / op.H, h = bh - b * op.H;
@@ -993,20 +1060,160 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
         if (op.kout) op.kout[(size_t)bh * op.Dv + col] = o;
         if (op.kout_bf16) op.kout_bf16[(size_t)bh * op.Dv + col] = float_to_bf16_bits(o);
       }
-      warp_signal(&P.sync[op.done], 1);
     }
+    ++units;
     named_barrier(CBAR, NCT);
   }
+  if (threadIdx.x == 0 && units > 0) red_release(&P.sync[op.done], units);
+}
+
+// ---------------------------------------------------------------------------
+// Reducer warp: the epilogue of every projection item, in the consumers'
+// item order (dense outputs and SwiGLU; gate/up slot signals; down
+// projection per-route outputs, arrivals and the routing-weighted combine).
+// ---------------------------------------------------------------------------
+__device__ bool reduce_up_item(const StepParams& P, const StOp& op, StPlan* pl, Partials& pa,
+                               const Item& it) {
+  const int lane = threadIdx.x & 31;
+  if (!partial_take(pa, pl)) return false;
+  const int* assign = pl->assign + it.abase;
+  const int n = it.rows * it.count;
+  for (int idx = lane; idx < n; idx += 32) {
+    const int r = idx / it.count, tok = idx - r * it.count;
+    const float g = partial_sum(pa, 0, it.RBc, it.KS, r >> 4, r & 15, tok);
+    const float u = partial_sum(pa, 1, it.RBc, it.KS, r >> 4, r & 15, tok);
+    op.y[(size_t)assign[tok] * op.N + it.r0 + r] = float_to_bf16_bits(swiglu_contract(g, u));
+  }
+  partial_release(pa);
+  if (lane == 0) red_release(&P.sync[op.slot_cnt + it.p], (it.rows + 15) >> 4);
+  return true;
+}
+
+__device__ bool reduce_down_item(const StepParams& P, const StOp& op, StPlan* pl, Partials& pa,
+                                 const Item& it) {
+  const int lane = threadIdx.x & 31;
+  if (!partial_take(pa, pl)) return false;
+  const int* assign = pl->assign + it.abase;
+  const int n = it.rows * it.count;
+  for (int idx = lane; idx < n; idx += 32) {
+    const int r = idx / it.count, tok = idx - r * it.count;
+    const float v = partial_sum(pa, 0, it.RBc, it.KS, r >> 4, r & 15, tok);
+    op.wsy[(size_t)assign[tok] * op.N + it.r0 + r] = float_to_bf16_bits(v);
+  }
+  partial_release(pa);
+  // Arrival per (token, 16-row block): the R-th arrival combines that token's
+  // routes for those rows in route order.
+  const int top_k = op.R - 1;
+  const int nrb = (op.N + 15) >> 4;
+  for (int rb = 0; rb * 16 < it.rows; ++rb) {
+    const int grb = (it.r0 >> 4) + rb;
+    const int rb_rows = min(16, it.rows - rb * 16);
+    int last = 0;
+    if (lane < it.count) {
+      const int tok = assign[lane] / op.R;
+      __threadfence();
+      const int old = atomicAdd(&P.sync[op.arrive + tok * nrb + grb], 1);
+      last = (old == op.R - 1);
+    }
+    unsigned ready = __ballot_sync(0xffffffffu, last);
+    if (ready) __threadfence();
+    while (ready) {
+      const int m = __ffs(ready) - 1;
+      ready &= ready - 1;
+      const int tok = assign[m] / op.R;
+      if (lane < rb_rows) {
+        const int row = it.r0 + rb * 16 + lane;
+        float accum = 0.f;
+        for (int r = 0; r < top_k; ++r) {
+          const uint16_t ov = __ldcg(&op.wsy[((size_t)tok * op.R + r) * op.N + row]);
+          accum += bf16_bits_to_float(ov) * pl->route_w[tok * top_k + r];
+        }
+        const uint16_t sv = __ldcg(&op.wsy[((size_t)tok * op.R + op.R - 1) * op.N + row]);
+        op.out[(size_t)tok * op.N + row] =
+            float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
+      }
+      warp_signal(&P.sync[op.done], 1);
+    }
+  }
+  return true;
+}
+
+__device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint64_t* plan_bar,
+                             uint64_t* plan_ack) {
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  uint32_t plan_phase = 0;
+  bool ok = true;
+  for (int o = 0; o < P.nops && ok; ++o) {
+    const StOp& op = P.ops[o];
+    if (op.type == OP_DENSE) {
+      const int f = first_item(op.rot);
+      int blocks = 0;
+      for (int p = 0; p < op.nprob && ok; ++p) {
+        const StDense& D = op.p[p];
+        const int ib = D.item_begin, ie = D.item_begin + D.items;
+        const int item_rows = D.RBc * 16;
+        const int T = op.T;
+        for (int i = ib + ((f - ib) % G + G) % G; i < ie; i += G) {
+          if (!partial_take(pa, pl)) {
+            ok = false;
+            break;
+          }
+          const int r0 = (i - ib) * item_rows;
+          const int rows = min(item_rows, D.N - r0);
+          blocks += (rows + 15) >> 4;
+          for (int idx = lane; idx < rows * T; idx += 32) {
+            const int r = idx / T, tok = idx - r * T;
+            const float v0 = partial_sum(pa, 0, D.RBc, D.KS, r >> 4, r & 15, tok);
+            const float val =
+                (D.mats == 2)
+                    ? swiglu_contract(v0, partial_sum(pa, 1, D.RBc, D.KS, r >> 4, r & 15, tok))
+                    : v0;
+            D.y[(size_t)tok * D.ys + r0 + r] = float_to_bf16_bits(val);
+          }
+          partial_release(pa);
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && blocks > 0) red_release(&P.sync[op.done], blocks);
+    } else if (op.type == OP_MOE_UP) {
+      int i = first_item(op.rot);
+      for (; i < op.items_rb && ok; i += G) {
+        Item it;
+        st_describe_shared(op, i, it);
+        it.abase = 0;
+        ok = reduce_up_item(P, op, pl, pa, it);
+      }
+      if (!ok) break;
+      if (!stage_wait(plan_bar, plan_phase, pl)) break;
+      const int n = pl->nslots * op.items_rb;
+      for (; i < n && ok; i += G) {
+        Item it;
+        st_describe_moe(op, pl, i, it);
+        ok = reduce_up_item(P, op, pl, pa, it);
+      }
+    } else if (op.type == OP_MOE_DOWN) {
+      const int n = pl->nslots * op.items_rb;
+      for (int i = first_item(op.rot); i < n && ok; i += G) {
+        Item it;
+        st_describe_moe(op, pl, i, it);
+        ok = reduce_down_item(P, op, pl, pa, it);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(plan_ack);
+      plan_phase ^= 1;
+    }
+  }
+  if (!ok && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant__ StepParams P) {
+__global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_constant__ StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   uint8_t* xs = smem;
-  float* red = reinterpret_cast<float*>(smem + P.red_off);
   StPlan* pl = reinterpret_cast<StPlan*>(smem + P.scr_off);
   StKda* kd = reinterpret_cast<StKda*>(smem + P.scr_off + sizeof(StPlan));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
@@ -1017,8 +1224,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant
   R.stages = P.stages;
   R.stage_bytes = P.stage_bytes;
   R.use = 0;
+  R.slot = 0;
+  R.phase = 0;
   uint64_t* plan_bar = bars + 2 * P.stages;
   uint64_t* plan_ack = plan_bar + 1;
+  Partials pa;
+  pa.buf = reinterpret_cast<float*>(smem + P.red_off);
+  pa.done = plan_ack + 1;
+  pa.taken = reinterpret_cast<int*>(pa.done + ST_NB);
+  pa.T = P.T;
+  pa.slot = 0;
+  pa.phase = 0;
+  pa.count = 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P.stages; ++s) {
@@ -1026,12 +1243,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant
       mbar_init(&R.empty[s], NCW);
     }
     mbar_init(plan_bar, 1);
-    mbar_init(plan_ack, 1);
+    mbar_init(plan_ack, 2);  // producer and reducer
+    for (int b = 0; b < ST_NB; ++b) mbar_init(&pa.done[b], NCW);
+    *pa.taken = 0;
     mbar_fence_init();
     pl->abort = 0;
     pl->nslots = 0;
   }
-  for (int e = threadIdx.x; e <= ST_MAX_E; e += NTHREADS) pl->slot_of[e] = -1;
+  for (int e = threadIdx.x; e <= ST_MAX_E; e += ST_THREADS) pl->slot_of[e] = -1;
   __syncthreads();
 
   if (warp == NCW) {
@@ -1040,25 +1259,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant
     producer_main(P, pl, R, plan_bar, plan_ack);
     return;
   }
+  if (warp == NCW + 1) {
+    reducer_main(P, pl, pa, plan_bar, plan_ack);
+    named_barrier(EXIT_BAR, NCT + 32);
+    return;
+  }
 
   // Counters are reset by the previous launch; wait for it to finish.
   pdl_wait();
-  int rslot = 0;
   uint32_t plan_round = 0;
   for (int o = 0; o < P.nops; ++o) {
     const StOp& op = P.ops[o];
+    if (threadIdx.x == 0) {
+      pl->cur_op = o;
+      trace_mark(P, o, 0);
+    }
     switch (op.type) {
       case OP_DENSE:
-        run_dense(P, op, pl, R, xs, red, rslot);
+        run_dense(P, op, pl, R, xs, pa);
         break;
       case OP_ROUTER:
-        run_router(P, op, pl, R, xs, red, rslot);
+        run_router(P, op, pl, R, xs);
         break;
       case OP_MOE_UP:
-        run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, red, rslot);
+        run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, pa);
         break;
       case OP_MOE_DOWN:
-        run_moe_down(P, op, pl, R, xs, red, rslot);
+        run_moe_down(P, op, pl, R, xs, pa);
         break;
       case OP_KDA:
         run_kda(P, op, pl, kd);
@@ -1066,10 +1293,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const __grid_constant
       default:
         break;
     }
+    if (threadIdx.x == 0) trace_mark(P, o, 3);
   }
-  // Exit: the last CTA resets every counter for the next launch (all of its
-  // consumer threads; the exit counter last).
-  named_barrier(CBAR, NCT);
+  // Exit: once the reducer is done too, the last CTA resets every counter for
+  // the next launch (all of its consumer threads; the exit counter last).
+  named_barrier(EXIT_BAR, NCT + 32);
   if (threadIdx.x == 0) {
     __threadfence();
     const int old = atomicAdd(&P.sync[P.exit_idx], 1);
@@ -1102,9 +1330,11 @@ struct StepProgram {
   int grid = 0;
 };
 
+// Counters are allocated in whole 128-byte lines, so that polls of one
+// operation's counter do not share a line with another's atomics.
 static int add_sync(StepProgram* pr, int n) {
   const int at = pr->nsync;
-  pr->nsync += n;
+  pr->nsync += (n + 31) / 32 * 32;
   return at;
 }
 
@@ -1430,8 +1660,8 @@ int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden, int64_
   dn.out = out;
   dn.rot = ((up_index + 1) * 37) % kb::current_sms();
   dn.done = kb::add_sync(pr, 1);
-  dn.arrive = kb::add_sync(pr, T * dn.items_rb);
-  dn.target = T * dn.items_rb;
+  dn.arrive = kb::add_sync(pr, T * (int)((H + 15) / 16));
+  dn.target = T * (int)((H + 15) / 16);
   *op_out = (int)pr->ops.size();
   pr->ops.push_back(dn);
   return KB_OK;
@@ -1542,17 +1772,22 @@ int kb_step_finalize(kb_step* step) {
   P.exit_idx = exit_idx;
   P.abort_idx = abort_idx;
   P.stage_bytes = stage;
+  P.T = T;
   P.red_off = (xbytes + 127) / 128 * 128;
-  P.scr_off = P.red_off + 2 * kb::NCW * 128 * (int)sizeof(float);
   const int scr = (int)(sizeof(kb::StPlan) + sizeof(kb::StKda) + 127) / 128 * 128;
+  // Ring of S stages and S+1 partial buffers (each NCW x 16 rows x T fp32,
+  // plus 16 counters): S = (room - one buffer) / (stage + one buffer).
+  P.part_bytes = kb::ST_NB * kb::NCW * 16 * T * (int)sizeof(float);
+  P.scr_off = P.red_off + (P.part_bytes + 127) / 128 * 128;
   P.ring_off = P.scr_off + scr;
-  const int avail = kb::MAX_SMEM - P.ring_off - 256;
-  P.stages = std::min(16, avail / std::max(stage, 1));
+  const int nbar = 2 + 2 * kb::ST_NB;
+  const int room = kb::MAX_SMEM - P.ring_off - (nbar + 2) * 8 - 256;
+  P.stages = std::min(16, room / std::max(stage + 16, 1));
   KB_REQUIRE(P.stages >= 2, KB_ERR_UNSUPPORTED,
              "shared memory: %d bytes of fixed regions leave room for %d stages of %d bytes",
              P.ring_off, P.stages, stage);
   P.bar_off = P.ring_off + P.stages * stage;
-  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2) * sizeof(uint64_t);
+  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2 + 2 * kb::ST_NB) * sizeof(uint64_t);
   KB_REQUIRE(pr->smem <= (size_t)kb::MAX_SMEM, KB_ERR_UNSUPPORTED, "shared memory overflow");
   P.err = kb::device_error_word(dev);
   KB_REQUIRE(P.err, KB_ERR_DEVICE, "device error word unavailable");
@@ -1586,7 +1821,7 @@ int kb_step_launch(kb_step* step, void* stream) {
              "program was finalized on device %d, current device is %d", pr->device, dev);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pr->grid);
-  cfg.blockDim = dim3(kb::NTHREADS);
+  cfg.blockDim = dim3(kb::ST_THREADS);
   cfg.dynamicSmemBytes = pr->smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
@@ -1598,6 +1833,24 @@ int kb_step_launch(kb_step* step, void* stream) {
   KB_REQUIRE(err == cudaSuccess, KB_ERR_LAUNCH, "step launch failed: %s",
              cudaGetErrorString(err));
   return KB_OK;
+}
+
+int kb_step_set_trace(kb_step* step, int64_t* trace, int64_t entries) {
+  kb::clear_error();
+  StepProgram* pr = reinterpret_cast<StepProgram*>(step);
+  KB_REQUIRE(pr, KB_ERR_NULL_POINTER, "step is NULL");
+  KB_REQUIRE(pr->finalized, KB_ERR_UNSUPPORTED, "program not finalized");
+  const int64_t need = (int64_t)pr->grid * (int64_t)pr->ops.size() * kb::ST_TRACE_FIELDS;
+  KB_REQUIRE(trace == nullptr || entries >= need, KB_ERR_WORKSPACE,
+             "trace needs %lld entries, got %lld", (long long)need, (long long)entries);
+  pr->params.trace = reinterpret_cast<long long*>(trace);
+  return KB_OK;
+}
+
+int64_t kb_step_trace_entries(const kb_step* step) {
+  const StepProgram* pr = reinterpret_cast<const StepProgram*>(step);
+  if (!pr || !pr->finalized) return 0;
+  return (int64_t)pr->grid * (int64_t)pr->ops.size() * kb::ST_TRACE_FIELDS;
 }
 
 int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage_bytes,

@@ -163,6 +163,16 @@ class StepProgram:
         self.finalized = True
         return self
 
+    def enable_trace(self) -> torch.Tensor:
+        """Record a timeline on every launch; returns the int64 buffer
+        [grid, n_ops, 5] (consumers start, inputs ready, routing built, end,
+        producer done issuing; %globaltimer ns)."""
+        n = int(_lib.lib().kb_step_trace_entries(self._h))
+        buf = torch.zeros(n, dtype=torch.int64, device="cuda")
+        _lib.call("kb_step_set_trace", self._h, _p(buf), c_int64(n))
+        self._trace = buf
+        return buf.view(-1, self.n_ops, 5)
+
     def launch(self, device: torch.device | None = None) -> None:
         """Run the whole program on the current stream."""
         dev = device or torch.device("cuda", torch.cuda.current_device())
