@@ -246,8 +246,9 @@ KB_API int kb_step_add_swiglu(kb_step* step, const uint16_t* x, int64_t x_stride
                    int64_t group, uint16_t* y, int64_t y_stride, const int* deps,
                    int ndeps, int* op_out);
 /* Router logits; the selection runs in the expert operation that uses it.   */
-/* logits fp32 [tokens, E] scratch; idx_out int64 [tokens, top_k+1] (shared  */
-/* expert id E appended), w_out fp32 [tokens, top_k].                         */
+/* logits: scratch of 2*tokens*E fp32 (the logits, then the choice keys), one */
+/* per router of the program; idx_out int64 [tokens, top_k+1] (shared expert  */
+/* id E appended), w_out fp32 [tokens, top_k].                                */
 KB_API int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride,
                    int64_t K, const uint16_t* weight, const float* bias, int64_t E,
                    int64_t top_k, int renormalize, float scaling, float* logits,
@@ -275,9 +276,10 @@ KB_API int kb_step_launch(kb_step* step, void* stream);
 KB_API int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage_bytes,
                    size_t* smem_bytes);
 /* Optional timeline: with a device buffer of kb_step_trace_entries() int64   */
-/* set, every launch records %globaltimer ns per (CTA, operation): consumers  */
-/* start, inputs ready, routing built (expert blocks), end, and the time the  */
-/* producer finished issuing the operation's weights.  NULL switches it off.  */
+/* set, every launch records %globaltimer ns per (CTA, operation) in 8 fields: */
+/* consumers start, inputs ready, routing built (expert blocks), end, producer */
+/* done issuing the weights, reducer done, shared-expert items done (expert    */
+/* gate/up), spare.  NULL switches it off.                                    */
 KB_API int kb_step_set_trace(kb_step* step, int64_t* trace, int64_t entries);
 KB_API int64_t kb_step_trace_entries(const kb_step* step);
 

@@ -59,9 +59,10 @@ constexpr int ST_KDA_COLS = 32;
 constexpr int ST_STAGE_TARGET = 40 * 1024;  // preferred bytes per item
 constexpr long long ST_WAIT_NS = 2000000000LL;  // 2 s per wait
 // Timeline fields per (CTA, operation): consumers start, inputs ready,
-// mid-point (routing built for expert blocks), end; producer done issuing.
-constexpr int ST_TRACE_FIELDS = 5;
-constexpr int ST_THREADS = NCT + 64;  // consumers, producer warp (NCW), reducer warp (NCW+1)
+// routing built (expert blocks), end; producer done issuing; reducer done;
+// shared-expert items done (expert gate/up); spare.
+constexpr int ST_TRACE_FIELDS = 8;
+constexpr int ST_THREADS = NCT + 96;  // consumers, producer (NCW), reducer (NCW+1), stager (NCW+2)
 constexpr int ST_NB = 4;              // partial-sum buffers between consumers and reducer
 constexpr int EXIT_BAR = 2;           // named barrier: consumers + reducer
 
@@ -140,6 +141,8 @@ struct StepParams {
   int ring_off, red_off, scr_off, bar_off;
   int part_bytes;  // partial-sum buffers at red_off
   int T;
+  int x_bytes, nxb;  // activation buffers at 0 (nxb of x_bytes)
+  int desc_off;      // nxb operation descriptor copies
   long long* trace;  // optional timeline [grid][nops][ST_TRACE_FIELDS] of %globaltimer ns
 };
 
@@ -625,22 +628,110 @@ __device__ __forceinline__ void release_stage(Ring& R, int s) {
 // ---------------------------------------------------------------------------
 // Consumer operations.
 // ---------------------------------------------------------------------------
+// A consumer warp waits until the stager has copied the operation's
+// descriptor, seen its dependencies complete and staged its activations.
+__device__ __forceinline__ void consumer_op_wait(const StepParams& P, StPlan* pl,
+                                                 uint64_t* xready, uint32_t xphase) {
+  if (!stage_wait(xready, xphase, pl) && (threadIdx.x & 31) == 0 && !pl->abort)
+    raise_abort(P, pl, ERR_TIMEOUT);
+  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Stager warp: runs one operation ahead of the consumers.  Per operation it
+// waits until the consumers released the activation buffer it will use,
+// copies the descriptor into shared memory, waits for the operation's
+// dependencies (acquire polls of their completion counters), stages the
+// activations and arrives on the buffer's `ready` mbarrier.
+// ---------------------------------------------------------------------------
+struct XBufs {
+  uint8_t* base;   // nxb buffers of x_bytes
+  int x_bytes, nxb;
+  StOp* desc;      // nxb descriptor copies
+  uint64_t* ready; // [nxb] count 1 (stager)
+  uint64_t* free;  // [nxb] count NCW (consumer warps)
+};
+
+__device__ bool stager_poll(const StepParams& P, StPlan* pl, int idx, int target) {
+  const int lane = threadIdx.x & 31;
+  int ok = 1;
+  if (lane == 0 && target > 0) {
+    const long long t0 = now_ns();
+    int spins = 0;
+    while (ld_acquire(&P.sync[idx]) < target) {
+      __nanosleep(32);
+      if (((++spins) & 15) == 0) {
+        if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || pl->abort) {
+          pl->abort = 1;
+          ok = 0;
+          break;
+        }
+        if (now_ns() - t0 > ST_WAIT_NS) {
+          raise_abort(P, pl, ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X) {
+  const int lane = threadIdx.x & 31;
+  int b = 0;
+  uint32_t ph = 0;
+  for (int o = 0; o < P.nops; ++o) {
+    if (o >= X.nxb && !stage_wait(&X.free[b], ph ^ 1u, pl)) break;
+    StOp* dst = X.desc + b;
+    const int* src = reinterpret_cast<const int*>(P.ops + o);
+    for (int w = lane; w < (int)(sizeof(StOp) / sizeof(int)); w += 32)
+      reinterpret_cast<int*>(dst)[w] = src[w];
+    __syncwarp();
+    const StOp& op = *dst;
+    bool ok = true;
+    for (int d = 0; d < op.ndeps && ok; ++d) {
+      const StOp& dop = P.ops[op.dep[d]];
+      ok = stager_poll(P, pl, dop.done, dop.target);
+    }
+    if (!ok) break;
+    uint8_t* xs = X.base + (size_t)b * X.x_bytes;
+    if (op.type == OP_DENSE) {
+      for (int p = 0; p < op.nprob; ++p) {
+        const StDense& D = op.p[p];
+        if (D.nchunk > 1) continue;  // staged chunk by chunk by the consumers
+        bool dup = false;
+        for (int q = 0; q < p; ++q) dup |= (op.p[q].x_off == D.x_off);
+        if (dup) continue;
+        const int ts = token_stride(D.K);
+        for (int m = 0; m < op.T; ++m)
+          stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, lane, 32);
+      }
+    } else if (op.type == OP_ROUTER) {
+      const int words = op.K >> 3;
+      for (int m = 0; m < op.T; ++m) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
+        uint4* d4 = reinterpret_cast<uint4*>(xs + (size_t)m * op.K * 2);
+        for (int w = lane; w < words; w += 32) d4[w] = __ldcg(s4 + w);
+      }
+    } else if (op.type == OP_MOE_UP) {
+      const int ts = token_stride(op.K);
+      for (int m = 0; m < op.T; ++m)
+        stage_row_cg(xs + m * ts, op.mx + (size_t)m * op.mxs, op.K, lane, 32);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&X.ready[b]);
+    if (++b == X.nxb) {
+      b = 0;
+      ph ^= 1u;
+    }
+  }
+}
+
 __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
                           Partials& pa) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
-  wait_deps(P, pl, op);
-  for (int p = 0; p < op.nprob; ++p) {
-    const StDense& D = op.p[p];
-    if (D.nchunk > 1) continue;  // staged chunk by chunk below
-    bool dup = false;
-    for (int q = 0; q < p; ++q) dup |= (op.p[q].x_off == D.x_off);
-    if (dup) continue;
-    const int ts = token_stride(D.K);
-    for (int m = 0; m < op.T; ++m)
-      stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
-  }
-  named_barrier(CBAR, NCT);
   const int warp = threadIdx.x >> 5;
   const int f = first_item(op.rot);
   for (int p = 0; p < op.nprob; ++p) {
@@ -734,14 +825,7 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
                            uint8_t* xs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
-  wait_deps(P, pl, op);
   const int K = op.K, words = K >> 3;
-  for (int m = 0; m < op.T; ++m) {
-    const uint4* src = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
-    uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)m * K * 2);
-    for (int w = threadIdx.x; w < words; w += NCT) dst[w] = __ldcg(src + w);
-  }
-  named_barrier(CBAR, NCT);
   int* done = &P.sync[op.done];
   // Warp j < 8 computes expert i*8 + j over the whole row in the order of the
   // router kernel (lane-strided 16-byte words, a xor butterfly), so logits
@@ -774,11 +858,19 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
           }
         }
       }
+      // Logit, then (lane m) the choice key of token m: choice_key(sigmoid +
+      // bias), so that the selection only compares keys.
+      const float be = op.rbias ? op.rbias[e] : 0.f;
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-        if (lane == 0 && m < op.T) op.logits[(size_t)m * op.E + e] = acc[m];
+        if (lane == m && m < op.T) {
+          const float sc = 1.0f / (1.0f + expf(-acc[m]));
+          op.logits[(size_t)m * op.E + e] = acc[m];
+          reinterpret_cast<uint32_t*>(op.logits)[(size_t)(op.T + m) * op.E + e] =
+              choice_key(sc + be);
+        }
       }
     }
     release_stage(R, s);
@@ -797,11 +889,13 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const StOp& rop = P.ops[up.router_op];
   consumers_wait(P, pl, rop.done, rop.target);
+  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 7);
   const int T = up.T, R = up.R, top_k = rop.top_k, E = rop.E;
   for (int t = warp; t < T; t += NCW) {
     int my_idx = 0;
     float my_score = 0.f, wsum = 0.f;
-    warp_topk256(rop.logits + (size_t)t * E, rop.rbias, E, top_k, lane, my_idx, my_score, wsum);
+    warp_topk256_keys(reinterpret_cast<const uint32_t*>(rop.logits) + (size_t)(T + t) * E,
+                      rop.logits + (size_t)t * E, E, top_k, lane, my_idx, my_score, wsum);
     my_idx = min(max(my_idx, 0), E - 1);
     if (lane < top_k) {
       float wv = my_score;
@@ -820,7 +914,21 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
     }
   }
   named_barrier(CBAR, NCT);
-  if (warp == 0) {
+  if (warp == 0 && T == 1) {
+    // One token: its routes are distinct experts, slot 1 + r holds route r.
+    if (lane == 0) {
+      pl->assign[0] = R - 1;
+      pl->slot_expert[0] = E;
+      pl->slot_start[0] = 0;
+      pl->nslots = 1 + top_k;
+    }
+    if (lane < top_k) {
+      pl->slot_expert[1 + lane] = pl->route_e[lane];
+      pl->slot_start[1 + lane] = 1 + lane;
+      pl->assign[1 + lane] = lane;
+    }
+    if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
+  } else if (warp == 0) {
     if (lane < T) pl->assign[lane] = lane * R + R - 1;
     if (lane == 0) {
       pl->slot_expert[0] = E;
@@ -904,10 +1012,6 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
                            uint64_t* plan_bar, uint64_t* plan_ack, uint32_t& plan_round,
                            uint8_t* xs, Partials& pa) {
   const int G = gridDim.x;
-  wait_deps(P, pl, op);
-  const int ts = token_stride(op.K);
-  for (int m = 0; m < op.T; ++m)
-    stage_row_cg(xs + m * ts, op.mx + (size_t)m * op.mxs, op.K, threadIdx.x, NCT);
   // The shared slot needs no routing: its assignments are t*R + R-1 (the
   // producer may still be reading the previous plan, which holds the same
   // values for slot 0).
@@ -926,6 +1030,7 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
     moe_up_item(P, op, pl, R, xs, pa, it, rot);
     rot = (rot + 1) & (op.KS - 1);
   }
+  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 6);
   // The producer must be done with the previous plan before it is replaced.
   if (plan_round > 0) {
     if (threadIdx.x == 0 && !stage_wait(plan_ack, (plan_round - 1) & 1, pl) && !pl->abort)
@@ -982,7 +1087,8 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
 // Warps 0..7 own rows i = r*8 + warp (r < 16) of a 32-column slice, as the
 // KDA kernel does, so the arithmetic (and its rounding) is the same; warps
 // 8..15 only keep the barriers.
-__device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* kd) {
+__device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* kd,
+                        uint64_t* xready, uint32_t xphase) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
   constexpr int KW = 8;    // computing warps
@@ -1006,7 +1112,7 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
       c[r] = (col_ok && i < op.Dk) ? base[(size_t)i * op.sk] : 0.f;
     }
     if (!waited) {
-      wait_deps(P, pl, op);
+      consumer_op_wait(P, pl, xready, xphase);
       waited = true;
     }
     const size_t vec = (size_t)bh * op.Dk;
@@ -1064,6 +1170,7 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
     ++units;
     named_barrier(CBAR, NCT);
   }
+  if (!waited) consumer_op_wait(P, pl, xready, xphase);
   if (threadIdx.x == 0 && units > 0) red_release(&P.sync[op.done], units);
 }
 
@@ -1101,28 +1208,40 @@ __device__ bool reduce_down_item(const StepParams& P, const StOp& op, StPlan* pl
     op.wsy[(size_t)assign[tok] * op.N + it.r0 + r] = float_to_bf16_bits(v);
   }
   partial_release(pa);
-  // Arrival per (token, 16-row block): the R-th arrival combines that token's
-  // routes for those rows in route order.
+  // Arrival per (token, 16-row block), all of the item's pairs in one round
+  // (lane = row block * count + token slot): the R-th arrival combines that
+  // token's routes for those rows in route order.
   const int top_k = op.R - 1;
   const int nrb = (op.N + 15) >> 4;
-  for (int rb = 0; rb * 16 < it.rows; ++rb) {
-    const int grb = (it.r0 >> 4) + rb;
-    const int rb_rows = min(16, it.rows - rb * 16);
-    int last = 0;
-    if (lane < it.count) {
-      const int tok = assign[lane] / op.R;
+  const int nrbi = (it.rows + 15) >> 4;
+  const int npairs = nrbi * it.count;
+  for (int base = 0; base < npairs; base += 32) {
+    const int pidx = base + lane;
+    int last = 0, my_tok = 0, my_rb = 0;
+    if (pidx < npairs) {
+      my_rb = pidx / it.count;
+      my_tok = assign[pidx - my_rb * it.count] / op.R;
       __threadfence();
-      const int old = atomicAdd(&P.sync[op.arrive + tok * nrb + grb], 1);
+      const int old = atomicAdd(&P.sync[op.arrive + my_tok * nrb + (it.r0 >> 4) + my_rb], 1);
       last = (old == op.R - 1);
     }
     unsigned ready = __ballot_sync(0xffffffffu, last);
     if (ready) __threadfence();
+    // Two (token, row block) pairs per pass: lanes 0-15 and 16-31.
     while (ready) {
-      const int m = __ffs(ready) - 1;
+      const int pa_lane = __ffs(ready) - 1;
       ready &= ready - 1;
-      const int tok = assign[m] / op.R;
-      if (lane < rb_rows) {
-        const int row = it.r0 + rb * 16 + lane;
+      int pb_lane = -1;
+      if (ready) {
+        pb_lane = __ffs(ready) - 1;
+        ready &= ready - 1;
+      }
+      const int src = (lane < 16) ? pa_lane : pb_lane;
+      const int tok = __shfl_sync(0xffffffffu, my_tok, src < 0 ? 0 : src);
+      const int rb = __shfl_sync(0xffffffffu, my_rb, src < 0 ? 0 : src);
+      const int rr = lane & 15;
+      if (src >= 0 && rb * 16 + rr < it.rows) {
+        const int row = it.r0 + rb * 16 + rr;
         float accum = 0.f;
         for (int r = 0; r < top_k; ++r) {
           const uint16_t ov = __ldcg(&op.wsy[((size_t)tok * op.R + r) * op.N + row]);
@@ -1132,7 +1251,7 @@ __device__ bool reduce_down_item(const StepParams& P, const StOp& op, StPlan* pl
         op.out[(size_t)tok * op.N + row] =
             float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
       }
-      warp_signal(&P.sync[op.done], 1);
+      warp_signal(&P.sync[op.done], pb_lane >= 0 ? 2 : 1);
     }
   }
   return true;
@@ -1146,6 +1265,7 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
   bool ok = true;
   for (int o = 0; o < P.nops && ok; ++o) {
     const StOp& op = P.ops[o];
+    if (o > 0 && lane == 0) trace_mark(P, o - 1, 5);
     if (op.type == OP_DENSE) {
       const int f = first_item(op.rot);
       int blocks = 0;
@@ -1213,7 +1333,6 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
 __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_constant__ StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
-  uint8_t* xs = smem;
   StPlan* pl = reinterpret_cast<StPlan*>(smem + P.scr_off);
   StKda* kd = reinterpret_cast<StKda*>(smem + P.scr_off + sizeof(StPlan));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
@@ -1236,6 +1355,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   pa.slot = 0;
   pa.phase = 0;
   pa.count = 0;
+  XBufs X;
+  X.base = smem;
+  X.x_bytes = P.x_bytes;
+  X.nxb = P.nxb;
+  X.desc = reinterpret_cast<StOp*>(smem + P.desc_off);
+  X.ready = reinterpret_cast<uint64_t*>(pa.taken + 2);
+  X.free = X.ready + 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P.stages; ++s) {
@@ -1246,6 +1372,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     mbar_init(plan_ack, 2);  // producer and reducer
     for (int b = 0; b < ST_NB; ++b) mbar_init(&pa.done[b], NCW);
     *pa.taken = 0;
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&X.ready[b], 1);
+      mbar_init(&X.free[b], NCW);
+    }
     mbar_fence_init();
     pl->abort = 0;
     pl->nslots = 0;
@@ -1264,34 +1394,54 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     named_barrier(EXIT_BAR, NCT + 32);
     return;
   }
+  if (warp == NCW + 2) {
+    pdl_wait();
+    stager_main(P, pl, X);
+    return;
+  }
 
   // Counters are reset by the previous launch; wait for it to finish.
   pdl_wait();
   uint32_t plan_round = 0;
+  int xb = 0;
+  uint32_t xph = 0;
   for (int o = 0; o < P.nops; ++o) {
-    const StOp& op = P.ops[o];
     if (threadIdx.x == 0) {
       pl->cur_op = o;
       trace_mark(P, o, 0);
     }
-    switch (op.type) {
-      case OP_DENSE:
-        run_dense(P, op, pl, R, xs, pa);
-        break;
-      case OP_ROUTER:
-        run_router(P, op, pl, R, xs);
-        break;
-      case OP_MOE_UP:
-        run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, pa);
-        break;
-      case OP_MOE_DOWN:
-        run_moe_down(P, op, pl, R, xs, pa);
-        break;
-      case OP_KDA:
-        run_kda(P, op, pl, kd);
-        break;
-      default:
-        break;
+    const int type = P.ops[o].type;
+    uint8_t* xs = X.base + (size_t)xb * X.x_bytes;
+    if (type == OP_KDA) {
+      // The KDA state does not depend on this launch: its loads are issued
+      // before the wait for the inputs (inside run_kda).
+      run_kda(P, P.ops[o], pl, kd, &X.ready[xb], xph);
+    } else {
+      consumer_op_wait(P, pl, &X.ready[xb], xph);
+      const StOp& op = X.desc[xb];
+      switch (type) {
+        case OP_DENSE:
+          run_dense(P, op, pl, R, xs, pa);
+          break;
+        case OP_ROUTER:
+          run_router(P, op, pl, R, xs);
+          break;
+        case OP_MOE_UP:
+          run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, pa);
+          break;
+        case OP_MOE_DOWN:
+          run_moe_down(P, op, pl, R, xs, pa);
+          break;
+        default:
+          break;
+      }
+    }
+    // This warp is done with the buffer and the descriptor copy.
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&X.free[xb]);
+    if (++xb == X.nxb) {
+      xb = 0;
+      xph ^= 1u;
     }
     if (threadIdx.x == 0) trace_mark(P, o, 3);
   }
@@ -1773,21 +1923,30 @@ int kb_step_finalize(kb_step* step) {
   P.abort_idx = abort_idx;
   P.stage_bytes = stage;
   P.T = T;
-  P.red_off = (xbytes + 127) / 128 * 128;
   const int scr = (int)(sizeof(kb::StPlan) + sizeof(kb::StKda) + 127) / 128 * 128;
-  // Ring of S stages and S+1 partial buffers (each NCW x 16 rows x T fp32,
-  // plus 16 counters): S = (room - one buffer) / (stage + one buffer).
+  // Layout: nxb activation buffers, nxb descriptor copies, ST_NB partial-sum
+  // buffers (NCW x 16 rows x T fp32 each), scratch, then the ring.  Two
+  // activation buffers (the stager works one operation ahead) when at least
+  // three ring stages remain, else one.
   P.part_bytes = kb::ST_NB * kb::NCW * 16 * T * (int)sizeof(float);
-  P.scr_off = P.red_off + (P.part_bytes + 127) / 128 * 128;
-  P.ring_off = P.scr_off + scr;
-  const int nbar = 2 + 2 * kb::ST_NB;
-  const int room = kb::MAX_SMEM - P.ring_off - (nbar + 2) * 8 - 256;
-  P.stages = std::min(16, room / std::max(stage + 16, 1));
+  P.x_bytes = (xbytes + 127) / 128 * 128;
+  const int desc_bytes = ((int)sizeof(kb::StOp) + 127) / 128 * 128;
+  const int nbar = 2 * 0 + 2 + kb::ST_NB + 1 + 4;
+  for (int nxb = 2; nxb >= 1; --nxb) {
+    P.nxb = nxb;
+    P.desc_off = nxb * P.x_bytes;
+    P.red_off = P.desc_off + nxb * desc_bytes;
+    P.scr_off = P.red_off + (P.part_bytes + 127) / 128 * 128;
+    P.ring_off = P.scr_off + scr;
+    const int room = kb::MAX_SMEM - P.ring_off - nbar * 8 - 256;
+    P.stages = std::min(16, room / std::max(stage + 16, 1));
+    if (P.stages >= 3) break;
+  }
   KB_REQUIRE(P.stages >= 2, KB_ERR_UNSUPPORTED,
              "shared memory: %d bytes of fixed regions leave room for %d stages of %d bytes",
              P.ring_off, P.stages, stage);
   P.bar_off = P.ring_off + P.stages * stage;
-  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2 + 2 * kb::ST_NB) * sizeof(uint64_t);
+  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2 + kb::ST_NB + 1 + 4) * sizeof(uint64_t);
   KB_REQUIRE(pr->smem <= (size_t)kb::MAX_SMEM, KB_ERR_UNSUPPORTED, "shared memory overflow");
   P.err = kb::device_error_word(dev);
   KB_REQUIRE(P.err, KB_ERR_DEVICE, "device error word unavailable");

@@ -81,13 +81,23 @@ __device__ __forceinline__ void warp_topk256(const float* lrow, const float* bia
   cswap(key, id, sc, 1, 2);
   cswap(key, id, sc, 3, 4);
   cswap(key, id, sc, 5, 6);
+  // Each pick: the best head over the lanes (one max-reduction); the lane
+  // holding it is found with a ballot, and only exact key ties fall back to
+  // the lower expert index.
   for (int sel = 0; sel < top_k; ++sel) {
     const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
-    const uint32_t cand = (key[0] == best) ? (uint32_t)id[0] : 0xffffffffu;
-    const int win = (int)__reduce_min_sync(0xffffffffu, cand);
-    float s = 0.f;
-    if (id[0] == win) {
-      s = sc[0];
+    const unsigned holders = __ballot_sync(0xffffffffu, key[0] == best);
+    int win;
+    if ((holders & (holders - 1u)) == 0u) {
+      win = __ffs(holders) - 1;
+    } else {
+      const uint32_t cand = (key[0] == best) ? (uint32_t)id[0] : 0xffffffffu;
+      const uint32_t lowest = __reduce_min_sync(0xffffffffu, cand);
+      win = __ffs(__ballot_sync(0xffffffffu, cand == lowest)) - 1;
+    }
+    const float s = __shfl_sync(0xffffffffu, sc[0], win);
+    const int wid = __shfl_sync(0xffffffffu, id[0], win);
+    if (lane == win) {
 #pragma unroll
       for (int j = 0; j < 7; ++j) {
         key[j] = key[j + 1];
@@ -98,13 +108,61 @@ __device__ __forceinline__ void warp_topk256(const float* lrow, const float* bia
       id[7] = 0x7fffffff;
       sc[7] = 0.f;
     }
-    s = __shfl_sync(0xffffffffu, s, win & 31);
     wsum += s;
     if (lane == sel) {
       my_score = s;
-      my_idx = win;
+      my_idx = wid;
     }
   }
+}
+
+// Top-k of one token from precomputed choice keys (choice_key of score +
+// bias, written by the router logits pass; NaN -> 0), E <= 256, one warp.
+// keys/logits are read with L2-only loads.  Same result and pick order as
+// warp_topk256: picks in (choice desc, index asc) order; lane r < top_k gets
+// pick r and its unbiased score sigmoid(logit); every lane gets wsum, the
+// sum of the picked scores in pick order.
+__device__ __forceinline__ void warp_topk256_keys(const uint32_t* keys, const float* lrow,
+                                                  int E, int top_k, int lane, int& my_idx,
+                                                  float& my_score, float& wsum) {
+  uint32_t key[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = (e < E) ? __ldcg(&keys[e]) : 0u;
+  }
+  // Expert ids of a lane increase with j (e = lane + 32 j), so the first j
+  // holding a key is the lowest index among this lane's ties.
+  int pick_idx = 0;
+  for (int sel = 0; sel < top_k; ++sel) {
+    uint32_t lm = key[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = max(lm, key[j]);
+    const uint32_t best = __reduce_max_sync(0xffffffffu, lm);
+    int jb = 8;
+#pragma unroll
+    for (int j = 7; j >= 0; --j)
+      if (key[j] == best) jb = j;
+    const int cand = (jb < 8) ? lane + 32 * jb : 0x7fffffff;
+    const unsigned holders = __ballot_sync(0xffffffffu, jb < 8);
+    int win;
+    if ((holders & (holders - 1u)) == 0u)
+      win = __shfl_sync(0xffffffffu, cand, __ffs(holders) - 1);
+    else
+      win = (int)__reduce_min_sync(0xffffffffu, (uint32_t)cand);
+    if ((win & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j == (win >> 5)) key[j] = 0u;
+    }
+    if (lane == sel) pick_idx = win;
+  }
+  float s = 0.f;
+  if (lane < top_k) s = 1.0f / (1.0f + expf(-__ldcg(&lrow[pick_idx])));
+  wsum = 0.f;
+  for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, s, r);
+  my_idx = pick_idx;
+  my_score = s;
 }
 
 }  // namespace kb

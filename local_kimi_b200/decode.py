@@ -258,7 +258,7 @@ class HotPathDecoder:
                 prev = prog.dense([(buf["act0"], w2p, w2s, xout)], deps=[sw])
             else:
                 m = lw.moe
-                lg = torch.empty((B, m.num_experts), dtype=torch.float32, device=dev)
+                lg = torch.empty((2, B, m.num_experts), dtype=torch.float32, device=dev)
                 idx = torch.empty((B, m.top_k + 1), dtype=torch.long, device=dev)
                 wts = torch.empty((B, m.top_k), dtype=torch.float32, device=dev)
                 buf["router_logits"].append(lg)

@@ -108,12 +108,15 @@ class StepProgram:
 
     def router(self, hidden, weight, bias, top_k, scaling, logits, idx_out, w_out,
                renormalize=True, deps=None) -> int:
-        """Router logits into ``logits`` (one buffer per router of the program);
-        the selection runs in the expert block that uses this router and
-        writes idx_out int64 [T, top_k+1] (shared id appended) and w_out."""
+        """Router logits into ``logits`` (fp32 scratch of 2*T*E: the logits, then
+        the choice keys; one buffer per router of the program); the selection
+        runs in the expert block that uses this router and writes idx_out
+        int64 [T, top_k+1] (shared id appended) and w_out."""
         _require(hidden, torch.bfloat16, "hidden states")
         _require(weight, torch.bfloat16, "router weight")
         _require(logits, torch.float32, "logits")
+        if logits.numel() < 2 * hidden.shape[0] * weight.shape[0] or not logits.is_contiguous():
+            raise ValueError("logits scratch must be contiguous with 2 * tokens * experts floats")
         b = None
         if bias is not None:
             b = bias.to(torch.float32).contiguous()
@@ -165,13 +168,14 @@ class StepProgram:
 
     def enable_trace(self) -> torch.Tensor:
         """Record a timeline on every launch; returns the int64 buffer
-        [grid, n_ops, 5] (consumers start, inputs ready, routing built, end,
-        producer done issuing; %globaltimer ns)."""
+        [grid, n_ops, 8] (consumers start, inputs ready, routing built, end,
+        producer done issuing, reducer done, shared-expert items done, spare;
+        %globaltimer ns)."""
         n = int(_lib.lib().kb_step_trace_entries(self._h))
         buf = torch.zeros(n, dtype=torch.int64, device="cuda")
         _lib.call("kb_step_set_trace", self._h, _p(buf), c_int64(n))
         self._trace = buf
-        return buf.view(-1, self.n_ops, 5)
+        return buf.view(-1, self.n_ops, 8)
 
     def launch(self, device: torch.device | None = None) -> None:
         """Run the whole program on the current stream."""
