@@ -62,9 +62,11 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
   }
   __syncthreads();
   if (expert < E) {
-    float acc[RT_TOK];
+    float acc[RT_TOK][4];
 #pragma unroll
-    for (int m = 0; m < RT_TOK; ++m) acc[m] = 0.f;
+    for (int m = 0; m < RT_TOK; ++m)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
     for (int w0 = 0; w0 < words; w0 += 32 * 8) {
       if (w0 > 0) {
 #pragma unroll
@@ -77,21 +79,11 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
       for (int u = 0; u < 8; ++u) {
         const int w = w0 + u * 32 + lane;
         if (w < words) {
-          const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
 #pragma unroll
           for (int m = 0; m < RT_TOK; ++m) {
             if (m < nt) {
               const uint4 hv = reinterpret_cast<const uint4*>(hsm + (size_t)m * K)[w];
-              const uint32_t hr[4] = {hv.x, hv.y, hv.z, hv.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float w_lo = __uint_as_float(wr[j] << 16);
-                const float w_hi = __uint_as_float(wr[j] & 0xFFFF0000u);
-                const float h_lo = __uint_as_float(hr[j] << 16);
-                const float h_hi = __uint_as_float(hr[j] & 0xFFFF0000u);
-                acc[m] = __fmaf_rn(h_lo, w_lo, acc[m]);
-                acc[m] = __fmaf_rn(h_hi, w_hi, acc[m]);
-              }
+              router_word_fma(wv[u], hv, acc[m]);
             }
           }
         }
@@ -99,9 +91,10 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
     }
 #pragma unroll
     for (int m = 0; m < RT_TOK; ++m) {
+      float v = router_lane_sum(acc[m]);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-      if (lane == 0 && m < nt) logits[(size_t)(t0 + m) * E + expert] = acc[m];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && m < nt) logits[(size_t)(t0 + m) * E + expert] = v;
     }
   }
 

@@ -825,56 +825,80 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
                            uint8_t* xs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
-  const int K = op.K, words = K >> 3;
+  // Descriptor fields in registers: the loops below must not re-read them.
+  const int K = op.K, words = K >> 3, T = op.T, E = op.E, items = op.items;
+  const float* rbias = op.rbias;
+  float* logits = op.logits;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(op.logits) + (size_t)T * E;
   int* done = &P.sync[op.done];
+  const uint32_t xs_s = smem_addr(xs);
   // Warp j < 8 computes expert i*8 + j over the whole row in the order of the
-  // router kernel (lane-strided 16-byte words, a xor butterfly), so logits
-  // equal kb_router_topk's bit for bit; warps 8..15 only release the stages.
+  // router kernel (lane-strided 16-byte words, router_word_fma, a xor
+  // butterfly), so logits equal kb_router_topk's bit for bit; warps 8..15
+  // only release the stages.
   int experts = 0;
-  for (int i = first_item(op.rot); i < op.items; i += G) {
+  for (int i = first_item(op.rot); i < items; i += G) {
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
     const int e = i * ST_RT_EXPERTS + warp;
-    if (warp < ST_RT_EXPERTS && e < op.E) {
-      float acc[ST_MAX_T];
+    if (warp < ST_RT_EXPERTS && e < E) {
+      float acc[ST_MAX_T][4];
 #pragma unroll
-      for (int m = 0; m < ST_MAX_T; ++m) acc[m] = 0.f;
-      const uint8_t* wr = stage + (size_t)warp * K * 2;
-      for (int w = lane; w < words; w += 32) {
-        const uint4 wv = lds_v4(wr + (size_t)w * 16);
-        const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+      for (int m = 0; m < ST_MAX_T; ++m)
 #pragma unroll
-        for (int m = 0; m < ST_MAX_T; ++m) {
-          if (m < op.T) {
-            const uint4 hv = lds_v4(xs + (size_t)m * K * 2 + (size_t)w * 16);
-            const uint32_t hq[4] = {hv.x, hv.y, hv.z, hv.w};
+        for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
+      uint32_t wa = smem_addr(stage) + (uint32_t)(warp * K * 2 + lane * 16);
+      uint32_t ha = xs_s + (uint32_t)(lane * 16);
+      if (T == 1) {
+        // One token: a branch-free loop (the per-token conditions of the
+        // general loop below keep the compiler from overlapping iterations).
+        for (int w = lane; w < words; w += 32, wa += 512, ha += 512) {
+          uint4 wv, hv;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
+                       : "r"(wa));
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
+                       : "r"(ha));
+          router_word_fma(wv, hv, acc[0]);
+        }
+      } else {
+        for (int w = lane; w < words; w += 32, wa += 512, ha += 512) {
+          uint4 wv;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
+                       : "r"(wa));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              acc[m] = __fmaf_rn(__uint_as_float(hq[q] << 16), __uint_as_float(wq[q] << 16),
-                                 acc[m]);
-              acc[m] = __fmaf_rn(__uint_as_float(hq[q] & 0xFFFF0000u),
-                                 __uint_as_float(wq[q] & 0xFFFF0000u), acc[m]);
+          for (int m = 0; m < ST_MAX_T; ++m) {
+            if (m < T) {
+              uint4 hv;
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
+                           : "r"(ha + (uint32_t)(m * K * 2)));
+              router_word_fma(wv, hv, acc[m]);
             }
           }
         }
       }
       // Logit, then (lane m) the choice key of token m: choice_key(sigmoid +
       // bias), so that the selection only compares keys.
-      const float be = op.rbias ? op.rbias[e] : 0.f;
+      const float be = rbias ? __ldg(rbias + e) : 0.f;
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m) {
+        if (m < T) {
+          float v = router_lane_sum(acc[m]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-        if (lane == m && m < op.T) {
-          const float sc = 1.0f / (1.0f + expf(-acc[m]));
-          op.logits[(size_t)m * op.E + e] = acc[m];
-          reinterpret_cast<uint32_t*>(op.logits)[(size_t)(op.T + m) * op.E + e] =
-              choice_key(sc + be);
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == m) {
+            const float sc = 1.0f / (1.0f + expf(-v));
+            logits[(size_t)m * E + e] = v;
+            keys[(size_t)m * E + e] = choice_key(sc + be);
+          }
         }
       }
     }
     release_stage(R, s);
-    experts += min(ST_RT_EXPERTS, op.E - i * ST_RT_EXPERTS);
+    experts += min(ST_RT_EXPERTS, E - i * ST_RT_EXPERTS);
   }
   named_barrier(CBAR, NCT);
   if (threadIdx.x == 0 && experts > 0) red_release(done, experts);
@@ -1094,43 +1118,58 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
   constexpr int KW = 8;    // computing warps
   constexpr int RPW = 16;  // rows per computing warp (Dk <= 128)
   const bool worker = warp < KW;
-  const int nsl = (op.Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
+  // Descriptor fields in registers: the loops below store to global memory
+  // and must not re-read them.
+  const int Dk = op.Dk, Dv = op.Dv, H = op.H, items = op.items;
+  const int64_t sb = op.sb, sh = op.sh, sk = op.sk;
+  float* const state = op.state;
+  const float* const qp = op.q;
+  const float* const kp = op.k;
+  const float* const vp = op.v;
+  const float* const dp = op.decay;
+  const float* const bp = op.beta;
+  const float scale = op.scale;
+  float* const kout = op.kout;
+  uint16_t* const kout16 = op.kout_bf16;
+  int* const done = &P.sync[op.done];
+  const int nsl = (Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
   bool waited = false;
   int units = 0;
-  for (int u = first_item(op.rot); u < op.items; u += G) {
+  for (int u = first_item(op.rot); u < items; u += G) {
     const int bh = u / nsl, sl = u - bh * nsl;
-    const int b = bh / op.H, h = bh - b * op.H;
+    const int b = bh / H, h = bh - b * H;
     const int col = sl * ST_KDA_COLS + lane;
-    const bool col_ok = worker && col < op.Dv;
-    float* base = op.state + (size_t)b * op.sb + (size_t)h * op.sh + col;
+    const bool col_ok = worker && col < Dv;
+    float* base = state + (size_t)b * sb + (size_t)h * sh + col;
     // The state depends on no operation of this launch: read it before the
     // wait for the inputs.
     float c[RPW];
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
       const int i = r * KW + warp;
-      c[r] = (col_ok && i < op.Dk) ? base[(size_t)i * op.sk] : 0.f;
+      c[r] = (col_ok && i < Dk) ? base[(size_t)i * sk] : 0.f;
     }
     if (!waited) {
       consumer_op_wait(P, pl, xready, xphase);
       waited = true;
     }
-    const size_t vec = (size_t)bh * op.Dk;
-    const float bt = __ldcg(&op.beta[bh]);
-    for (int i = threadIdx.x; i < op.Dk; i += NCT) {
-      const float kv = __ldcg(&op.k[vec + i]);
-      kd->ed[i] = expf(__ldcg(&op.decay[vec + i]));
+    const size_t vec = (size_t)bh * Dk;
+    const float bt = __ldcg(&bp[bh]);
+    const float vcol = col_ok ? __ldcg(&vp[(size_t)bh * Dv + col]) : 0.f;
+    for (int i = threadIdx.x; i < Dk; i += NCT) {
+      const float kv = __ldcg(&kp[vec + i]);
+      kd->ed[i] = expf(__ldcg(&dp[vec + i]));
       kd->k[i] = kv;
       kd->bk[i] = __fmul_rn(bt, kv);
-      kd->q[i] = __fmul_rn(__ldcg(&op.q[vec + i]), op.scale);
+      kd->q[i] = __fmul_rn(__ldcg(&qp[vec + i]), scale);
     }
     named_barrier(CBAR, NCT);
-    float part = 0.f;
     if (worker) {
+      float part = 0.f;
 #pragma unroll
       for (int r = 0; r < RPW; ++r) {
         const int i = r * KW + warp;
-        if (i < op.Dk) {
+        if (i < Dk) {
           c[r] = __fmul_rn(c[r], kd->ed[i]);
           part = __fadd_rn(part, __fmul_rn(c[r], kd->k[i]));
         }
@@ -1141,37 +1180,40 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
     float pred = 0.f;
 #pragma unroll
     for (int w = 0; w < KW; ++w) pred = __fadd_rn(pred, kd->red[w][lane]);
-    const float delta = col_ok ? __fsub_rn(__ldcg(&op.v[(size_t)bh * op.Dv + col]), pred) : 0.f;
+    const float delta = col_ok ? __fsub_rn(vcol, pred) : 0.f;
     named_barrier(CBAR, NCT);
     if (worker) {
       float opart = 0.f;
 #pragma unroll
       for (int r = 0; r < RPW; ++r) {
         const int i = r * KW + warp;
-        if (i < op.Dk) {
+        if (i < Dk) {
           c[r] = __fadd_rn(c[r], __fmul_rn(kd->bk[i], delta));
           opart = __fadd_rn(opart, __fmul_rn(c[r], kd->q[i]));
-          if (col_ok) base[(size_t)i * op.sk] = c[r];
         }
       }
       kd->red[warp][lane] = opart;
+      if (col_ok) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          const int i = r * KW + warp;
+          if (i < Dk) base[(size_t)i * sk] = c[r];
+        }
+      }
     }
     named_barrier(CBAR, NCT);
-    if (warp == 0) {
-      const bool ok_col = sl * ST_KDA_COLS + lane < op.Dv;
-      if (ok_col) {
-        float o = 0.f;
+    if (warp == 0 && sl * ST_KDA_COLS + lane < Dv) {
+      float o = 0.f;
 #pragma unroll
-        for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
-        if (op.kout) op.kout[(size_t)bh * op.Dv + col] = o;
-        if (op.kout_bf16) op.kout_bf16[(size_t)bh * op.Dv + col] = float_to_bf16_bits(o);
-      }
+      for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
+      if (kout) kout[(size_t)bh * Dv + col] = o;
+      if (kout16) kout16[(size_t)bh * Dv + col] = float_to_bf16_bits(o);
     }
     ++units;
     named_barrier(CBAR, NCT);
   }
   if (!waited) consumer_op_wait(P, pl, xready, xphase);
-  if (threadIdx.x == 0 && units > 0) red_release(&P.sync[op.done], units);
+  if (threadIdx.x == 0 && units > 0) red_release(done, units);
 }
 
 // ---------------------------------------------------------------------------
@@ -1179,51 +1221,84 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
 // item order (dense outputs and SwiGLU; gate/up slot signals; down
 // projection per-route outputs, arrivals and the routing-weighted combine).
 // ---------------------------------------------------------------------------
-__device__ bool reduce_up_item(const StepParams& P, const StOp& op, StPlan* pl, Partials& pa,
-                               const Item& it) {
+// Expert-block fields the reducer needs, read once per operation (the
+// epilogues store to global memory, so fields read through the descriptor
+// would be re-read after every store).
+struct MoeEpi {
+  uint16_t* y;     // gate/up: activated rows
+  uint16_t* wsy;   // down: per-route outputs
+  uint16_t* out;   // down: combined rows
+  int* slot_cnt;   // gate/up: per-slot counters
+  int* arrive;     // down: (token, row block) counters
+  int* done;       // down: combined blocks
+  int N, R, KS, RBc;
+};
+
+__device__ __forceinline__ MoeEpi moe_epi(const StepParams& P, const StOp& op) {
+  MoeEpi m;
+  m.y = op.y;
+  m.wsy = op.wsy;
+  m.out = op.out;
+  m.slot_cnt = &P.sync[op.slot_cnt];
+  m.arrive = &P.sync[op.arrive];
+  m.done = &P.sync[op.done];
+  m.N = op.N;
+  m.R = op.R;
+  m.KS = op.KS;
+  m.RBc = op.RBc;
+  return m;
+}
+
+__device__ bool reduce_up_item(const MoeEpi& m, StPlan* pl, Partials& pa, const Item& it) {
   const int lane = threadIdx.x & 31;
   if (!partial_take(pa, pl)) return false;
   const int* assign = pl->assign + it.abase;
-  const int n = it.rows * it.count;
+  const int cnt = it.count, rows = it.rows, r0 = it.r0;
+  const int n = rows * cnt;
+  uint16_t* const y = m.y;
+  const int N = m.N;
   for (int idx = lane; idx < n; idx += 32) {
-    const int r = idx / it.count, tok = idx - r * it.count;
-    const float g = partial_sum(pa, 0, it.RBc, it.KS, r >> 4, r & 15, tok);
-    const float u = partial_sum(pa, 1, it.RBc, it.KS, r >> 4, r & 15, tok);
-    op.y[(size_t)assign[tok] * op.N + it.r0 + r] = float_to_bf16_bits(swiglu_contract(g, u));
+    const int r = idx / cnt, tok = idx - r * cnt;
+    const float g = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
+    const float u = partial_sum(pa, 1, m.RBc, m.KS, r >> 4, r & 15, tok);
+    y[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(swiglu_contract(g, u));
   }
   partial_release(pa);
-  if (lane == 0) red_release(&P.sync[op.slot_cnt + it.p], (it.rows + 15) >> 4);
+  if (lane == 0) red_release(m.slot_cnt + it.p, (rows + 15) >> 4);
   return true;
 }
 
-__device__ bool reduce_down_item(const StepParams& P, const StOp& op, StPlan* pl, Partials& pa,
-                                 const Item& it) {
+__device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, const Item& it) {
   const int lane = threadIdx.x & 31;
   if (!partial_take(pa, pl)) return false;
   const int* assign = pl->assign + it.abase;
-  const int n = it.rows * it.count;
+  const int cnt = it.count, rows = it.rows, r0 = it.r0;
+  const int n = rows * cnt;
+  const int N = m.N, R = m.R;
+  uint16_t* const wsy = m.wsy;
+  uint16_t* const out = m.out;
   for (int idx = lane; idx < n; idx += 32) {
-    const int r = idx / it.count, tok = idx - r * it.count;
-    const float v = partial_sum(pa, 0, it.RBc, it.KS, r >> 4, r & 15, tok);
-    op.wsy[(size_t)assign[tok] * op.N + it.r0 + r] = float_to_bf16_bits(v);
+    const int r = idx / cnt, tok = idx - r * cnt;
+    const float v = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
+    wsy[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(v);
   }
   partial_release(pa);
   // Arrival per (token, 16-row block), all of the item's pairs in one round
   // (lane = row block * count + token slot): the R-th arrival combines that
   // token's routes for those rows in route order.
-  const int top_k = op.R - 1;
-  const int nrb = (op.N + 15) >> 4;
-  const int nrbi = (it.rows + 15) >> 4;
-  const int npairs = nrbi * it.count;
+  const int top_k = R - 1;
+  const int nrb = (N + 15) >> 4;
+  const int nrbi = (rows + 15) >> 4;
+  const int npairs = nrbi * cnt;
   for (int base = 0; base < npairs; base += 32) {
     const int pidx = base + lane;
     int last = 0, my_tok = 0, my_rb = 0;
     if (pidx < npairs) {
-      my_rb = pidx / it.count;
-      my_tok = assign[pidx - my_rb * it.count] / op.R;
+      my_rb = pidx / cnt;
+      my_tok = assign[pidx - my_rb * cnt] / R;
       __threadfence();
-      const int old = atomicAdd(&P.sync[op.arrive + my_tok * nrb + (it.r0 >> 4) + my_rb], 1);
-      last = (old == op.R - 1);
+      const int old = atomicAdd(m.arrive + my_tok * nrb + (r0 >> 4) + my_rb, 1);
+      last = (old == R - 1);
     }
     unsigned ready = __ballot_sync(0xffffffffu, last);
     if (ready) __threadfence();
@@ -1240,18 +1315,17 @@ __device__ bool reduce_down_item(const StepParams& P, const StOp& op, StPlan* pl
       const int tok = __shfl_sync(0xffffffffu, my_tok, src < 0 ? 0 : src);
       const int rb = __shfl_sync(0xffffffffu, my_rb, src < 0 ? 0 : src);
       const int rr = lane & 15;
-      if (src >= 0 && rb * 16 + rr < it.rows) {
-        const int row = it.r0 + rb * 16 + rr;
+      if (src >= 0 && rb * 16 + rr < rows) {
+        const int row = r0 + rb * 16 + rr;
+        const uint16_t* ws = wsy + (size_t)tok * R * N + row;
+        const float* rw = pl->route_w + tok * top_k;
         float accum = 0.f;
-        for (int r = 0; r < top_k; ++r) {
-          const uint16_t ov = __ldcg(&op.wsy[((size_t)tok * op.R + r) * op.N + row]);
-          accum += bf16_bits_to_float(ov) * pl->route_w[tok * top_k + r];
-        }
-        const uint16_t sv = __ldcg(&op.wsy[((size_t)tok * op.R + op.R - 1) * op.N + row]);
-        op.out[(size_t)tok * op.N + row] =
-            float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
+        for (int r = 0; r < top_k; ++r)
+          accum += bf16_bits_to_float(__ldcg(ws + (size_t)r * N)) * rw[r];
+        const uint16_t sv = __ldcg(ws + (size_t)(R - 1) * N);
+        out[(size_t)tok * N + row] = float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
       }
-      warp_signal(&P.sync[op.done], pb_lane >= 0 ? 2 : 1);
+      warp_signal(m.done, pb_lane >= 0 ? 2 : 1);
     }
   }
   return true;
@@ -1268,28 +1342,30 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
     if (o > 0 && lane == 0) trace_mark(P, o - 1, 5);
     if (op.type == OP_DENSE) {
       const int f = first_item(op.rot);
+      const int T = op.T, nprob = op.nprob;
       int blocks = 0;
-      for (int p = 0; p < op.nprob && ok; ++p) {
-        const StDense& D = op.p[p];
-        const int ib = D.item_begin, ie = D.item_begin + D.items;
-        const int item_rows = D.RBc * 16;
-        const int T = op.T;
+      for (int p = 0; p < nprob && ok; ++p) {
+        const StDense& Dg = op.p[p];
+        const int ib = Dg.item_begin, ie = Dg.item_begin + Dg.items;
+        const int RBc = Dg.RBc, KS = Dg.KS, N = Dg.N;
+        const bool pair = Dg.mats == 2;
+        uint16_t* const y = Dg.y;
+        const int64_t ys = Dg.ys;
+        const int item_rows = RBc * 16;
         for (int i = ib + ((f - ib) % G + G) % G; i < ie; i += G) {
           if (!partial_take(pa, pl)) {
             ok = false;
             break;
           }
           const int r0 = (i - ib) * item_rows;
-          const int rows = min(item_rows, D.N - r0);
+          const int rows = min(item_rows, N - r0);
           blocks += (rows + 15) >> 4;
           for (int idx = lane; idx < rows * T; idx += 32) {
             const int r = idx / T, tok = idx - r * T;
-            const float v0 = partial_sum(pa, 0, D.RBc, D.KS, r >> 4, r & 15, tok);
+            const float v0 = partial_sum(pa, 0, RBc, KS, r >> 4, r & 15, tok);
             const float val =
-                (D.mats == 2)
-                    ? swiglu_contract(v0, partial_sum(pa, 1, D.RBc, D.KS, r >> 4, r & 15, tok))
-                    : v0;
-            D.y[(size_t)tok * D.ys + r0 + r] = float_to_bf16_bits(val);
+                pair ? swiglu_contract(v0, partial_sum(pa, 1, RBc, KS, r >> 4, r & 15, tok)) : v0;
+            y[(size_t)tok * ys + r0 + r] = float_to_bf16_bits(val);
           }
           partial_release(pa);
         }
@@ -1297,12 +1373,13 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       __syncwarp();
       if (lane == 0 && blocks > 0) red_release(&P.sync[op.done], blocks);
     } else if (op.type == OP_MOE_UP) {
+      const MoeEpi m = moe_epi(P, op);
       int i = first_item(op.rot);
       for (; i < op.items_rb && ok; i += G) {
         Item it;
         st_describe_shared(op, i, it);
         it.abase = 0;
-        ok = reduce_up_item(P, op, pl, pa, it);
+        ok = reduce_up_item(m, pl, pa, it);
       }
       if (!ok) break;
       if (!stage_wait(plan_bar, plan_phase, pl)) break;
@@ -1310,14 +1387,15 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       for (; i < n && ok; i += G) {
         Item it;
         st_describe_moe(op, pl, i, it);
-        ok = reduce_up_item(P, op, pl, pa, it);
+        ok = reduce_up_item(m, pl, pa, it);
       }
     } else if (op.type == OP_MOE_DOWN) {
+      const MoeEpi m = moe_epi(P, op);
       const int n = pl->nslots * op.items_rb;
       for (int i = first_item(op.rot); i < n && ok; i += G) {
         Item it;
         st_describe_moe(op, pl, i, it);
-        ok = reduce_down_item(P, op, pl, pa, it);
+        ok = reduce_down_item(m, pl, pa, it);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(plan_ack);

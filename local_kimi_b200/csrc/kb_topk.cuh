@@ -35,6 +35,26 @@ __device__ __forceinline__ void cswap(uint32_t (&k)[N], int (&id)[N], float (&sc
   }
 }
 
+// Router dot products: one lane accumulates its 16-byte words of bf16
+// weights times bf16 activations (fp32 products, fused adds) into four
+// partial sums, one per element pair j of the word; router_lane_sum joins
+// them as (a0 + a1) + (a2 + a3) before the warp's xor butterfly.  Both router
+// implementations use this order, so their logits agree bit for bit.
+__device__ __forceinline__ void router_word_fma(uint4 wv, uint4 hv, float (&a)[4]) {
+  const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+  const uint32_t hr[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    a[j] = __fmaf_rn(__uint_as_float(hr[j] << 16), __uint_as_float(wr[j] << 16), a[j]);
+    a[j] = __fmaf_rn(__uint_as_float(hr[j] & 0xFFFF0000u), __uint_as_float(wr[j] & 0xFFFF0000u),
+                     a[j]);
+  }
+}
+
+__device__ __forceinline__ float router_lane_sum(const float (&a)[4]) {
+  return __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+}
+
 // Top-k of one token over E <= 256 experts, one warp.  lrow holds the fp32
 // logits (read with L2-only loads: another CTA may have written them in the
 // same kernel).  scores = sigmoid(logit); choice = score + bias; the k picks
