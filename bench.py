@@ -49,6 +49,11 @@ import torch  # noqa: E402
 
 METRIC = "decode tok/s Kimi-Linear-48B W4A16 (hot path step)"
 HBM_FALLBACK_GBS = 6650.0
+# DRAM traffic over algorithmic bytes of step_kernel, from an ncu capture of a
+# 3-layer program (profiles/step_kernel_decode_bs1.md: 370.9 MB read+write for
+# 366.9 MB algorithmic); traffic grows with the bytes streamed, so the full
+# step's traffic is reported as this ratio times its algorithmic bytes.
+STEP_TRAFFIC_RATIO = 1.011
 
 
 def _args() -> argparse.Namespace:
@@ -475,7 +480,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": (int(bytes_step["total"] * STEP_TRAFFIC_RATIO) if use_executor
+                                 else None),
+                     "traffic_source": ("ncu dram bytes of a 3-layer capture, scaled by bytes"
+                                        if use_executor else None),
                      "kernel": ("step_kernel (the whole step in one launch)" if use_executor
                                 else "all launches of the step"),
                      "peak_source": peak_src, "bytes_per_launch": bytes_step["total"]},
