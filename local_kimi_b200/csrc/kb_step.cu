@@ -64,6 +64,7 @@ constexpr long long ST_WAIT_NS = 2000000000LL;  // 2 s per wait
 constexpr int ST_TRACE_FIELDS = 8;
 constexpr int ST_THREADS = NCT + 96;  // consumers, producer (NCW), reducer (NCW+1), stager (NCW+2)
 constexpr int ST_NB = 4;              // partial-sum buffers between consumers and reducer
+constexpr int ST_DNB = 4;             // down-projection input buffers (stager to consumers)
 constexpr int EXIT_BAR = 2;           // named barrier: consumers + reducer
 
 struct StDense {
@@ -98,13 +99,13 @@ struct StOp {
   const float* rbias;
   int E, K, top_k, renorm;
   float scaling;
-  float* logits;
+  unsigned long long* rwords;  // router words [2 parities][T][E]
   int64_t* idx_out;
   float* w_out;
   // experts (up and down)
   int router_op;
-  int slot_cnt;  // sync index of the up op's per-slot counters
-  int arrive;    // down: sync index of the (token, row group) arrival counters
+  int slot_cnt;    // sync index of the up op's per-slot counters
+  int items_done;  // down: sync index of the count of finished down items
   const uint16_t* mx;
   int64_t mxs;
   const uint8_t* w0;
@@ -136,12 +137,14 @@ struct StepParams {
   int* sync;
   int nsync;
   int exit_idx, abort_idx;
+  int parity_idx;    // launch parity (selects the router words of this launch)
   uint32_t* err;
   int stages, stage_bytes;
   int ring_off, red_off, scr_off, bar_off;
   int part_bytes;  // partial-sum buffers at red_off
   int T;
   int x_bytes, nxb;  // activation buffers at 0 (nxb of x_bytes)
+  int dnb, drow_bytes;  // down inputs: dnb buffers of drow_bytes inside the op's activation buffer
   int desc_off;      // nxb operation descriptor copies
   long long* trace;  // optional timeline [grid][nops][ST_TRACE_FIELDS] of %globaltimer ns
 };
@@ -159,6 +162,7 @@ struct StPlan {
   int done_tok[ST_MAX_T];
   int abort;
   int last;
+  int parity;  // launch parity
   int cur_op;  // operation the consumers are in (timeline)
 };
 
@@ -259,15 +263,27 @@ __device__ __forceinline__ int first_item(int rot) {
 }
 
 // Activation row into the B-fragment layout, read with L2-only loads (the row
-// may have been written by another CTA of this launch).
+// may have been written by another CTA of this launch); B loads per thread in
+// flight before the stores.
+template <int B = 1>
 __device__ __forceinline__ void stage_row_cg(uint8_t* xs_row, const uint16_t* src, int K,
                                              int first, int step) {
   const int NC = K >> 5;
   const int words = K >> 3;
-  for (int w = first; w < words; w += step) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + w);
-    const int c = w >> 2, j = w & 3;
-    *reinterpret_cast<uint4*>(xs_row + (j * NC + c) * 16) = permute_pairs(v);
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  for (int w0 = first; w0 < words; w0 += B * step) {
+    uint4 v[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int w = w0 + b * step;
+      if (w < words) v[b] = __ldcg(s4 + w);
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int w = w0 + b * step;
+      if (w < words)
+        *reinterpret_cast<uint4*>(xs_row + ((w & 3) * NC + (w >> 2)) * 16) = permute_pairs(v[b]);
+    }
   }
 }
 
@@ -519,9 +535,14 @@ __device__ __forceinline__ void split_compute(const Item& it, const Split& sp,
                                               const uint8_t* (&xrow)[1], float (&acc)[1][4]) {
   const int n = kb_hi - kb_lo;
   const int kb0 = kb_lo + n * sp.ks / it.KS, kb1 = kb_lo + n * (sp.ks + 1) / it.KS;
-  if (sp.rb_rows > 0 && kb1 > kb0)
-    rowblock_compute<1>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0, kb1,
-                        xrow, 1, acc);
+  if (sp.rb_rows > 0 && kb1 > kb0) {
+    if (it.scale_bulk)  // scales staged with the weights: explicit shared loads
+      rowblock_compute<1, true>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0,
+                                kb1, xrow, 1, acc);
+    else
+      rowblock_compute<1>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0, kb1,
+                          xrow, 1, acc);
+  }
 }
 
 // Partial sums of an item's warps are handed to the reducer warp through a
@@ -650,6 +671,17 @@ struct XBufs {
   StOp* desc;      // nxb descriptor copies
   uint64_t* ready; // [nxb] count 1 (stager)
   uint64_t* free;  // [nxb] count NCW (consumer warps)
+  uint64_t* dready;  // [ST_DNB] down inputs staged, count 1 (stager)
+  uint64_t* dfree;   // [ST_DNB] down inputs consumed, count NCW
+  int dnb, drow_bytes;
+};
+
+// Down-projection input buffer use u (the same sequence on the stager and the
+// consumers): buffer u % dnb, phase (u / dnb) & 1.
+struct DUse {
+  int u = 0;
+  __device__ __forceinline__ int buf(int dnb) const { return u % dnb; }
+  __device__ __forceinline__ uint32_t phase(int dnb) const { return (uint32_t)(u / dnb) & 1u; }
 };
 
 __device__ bool stager_poll(const StepParams& P, StPlan* pl, int idx, int target) {
@@ -677,11 +709,15 @@ __device__ bool stager_poll(const StepParams& P, StPlan* pl, int idx, int target
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X) {
+__device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uint64_t* plan_bar) {
   const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
   int b = 0;
   uint32_t ph = 0;
-  for (int o = 0; o < P.nops; ++o) {
+  uint32_t plan_phase = 0;
+  DUse du;
+  int o = 0;
+  for (; o < P.nops; ++o) {
     if (o >= X.nxb && !stage_wait(&X.free[b], ph ^ 1u, pl)) break;
     StOp* dst = X.desc + b;
     const int* src = reinterpret_cast<const int*>(P.ops + o);
@@ -705,27 +741,65 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X) {
         if (dup) continue;
         const int ts = token_stride(D.K);
         for (int m = 0; m < op.T; ++m)
-          stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, lane, 32);
+          stage_row_cg<1>(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, lane, 32);
       }
     } else if (op.type == OP_ROUTER) {
       const int words = op.K >> 3;
       for (int m = 0; m < op.T; ++m) {
         const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
         uint4* d4 = reinterpret_cast<uint4*>(xs + (size_t)m * op.K * 2);
-        for (int w = lane; w < words; w += 32) d4[w] = __ldcg(s4 + w);
+        for (int w0 = lane; w0 < words; w0 += 8 * 32) {
+          uint4 v[8];
+#pragma unroll
+          for (int b = 0; b < 8; ++b)
+            if (w0 + 32 * b < words) v[b] = __ldcg(s4 + w0 + 32 * b);
+#pragma unroll
+          for (int b = 0; b < 8; ++b)
+            if (w0 + 32 * b < words) d4[w0 + 32 * b] = v[b];
+        }
       }
     } else if (op.type == OP_MOE_UP) {
       const int ts = token_stride(op.K);
       for (int m = 0; m < op.T; ++m)
-        stage_row_cg(xs + m * ts, op.mx + (size_t)m * op.mxs, op.K, lane, 32);
+        stage_row_cg<1>(xs + m * ts, op.mx + (size_t)m * op.mxs, op.K, lane, 32);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&X.ready[b]);
+    if (op.type == OP_MOE_DOWN) {
+      // Inputs of each down item of this CTA, in item order, as soon as the
+      // gate/up of its slot is complete: the activated rows of the slot's
+      // assignments, into the next of dnb buffers inside this operation's
+      // activation buffer.
+      if (!stage_wait(plan_bar, plan_phase, pl)) break;
+      plan_phase ^= 1u;
+      const int n = pl->nslots * op.items_rb;
+      const int ts = token_stride(op.K);
+      for (int i = first_item(op.rot); i < n && ok; i += G, ++du.u) {
+        const int j = du.buf(X.dnb);
+        if (du.u >= X.dnb && !stage_wait(&X.dfree[j], du.phase(X.dnb) ^ 1u, pl)) {
+          ok = false;
+          break;
+        }
+        const int slot = i / op.items_rb;
+        ok = stager_poll(P, pl, op.slot_cnt + slot, op.up_rb);
+        if (!ok) break;
+        const int a0 = pl->slot_start[slot], cnt = pl->slot_start[slot + 1] - a0;
+        uint8_t* dst = xs + (size_t)j * X.drow_bytes;
+        for (int m = 0; m < cnt; ++m)
+          stage_row_cg<1>(dst + m * ts, op.mx + (size_t)pl->assign[a0 + m] * op.mxs, op.K, lane,
+                          32);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&X.dready[j]);
+      }
+      if (!ok) break;
+    }
     if (++b == X.nxb) {
       b = 0;
       ph ^= 1u;
     }
   }
+  // A wait that gave up ends the launch (the consumers' waits are bounded too).
+  if (o < P.nops && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
 }
 
 __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
@@ -828,8 +902,9 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
   // Descriptor fields in registers: the loops below must not re-read them.
   const int K = op.K, words = K >> 3, T = op.T, E = op.E, items = op.items;
   const float* rbias = op.rbias;
-  float* logits = op.logits;
-  uint32_t* keys = reinterpret_cast<uint32_t*>(op.logits) + (size_t)T * E;
+  // Router words of this launch and of the next (cleared here for it).
+  unsigned long long* rwords = op.rwords + (size_t)pl->parity * T * E;
+  unsigned long long* next_rwords = op.rwords + (size_t)(pl->parity ^ 1) * T * E;
   int* done = &P.sync[op.done];
   const uint32_t xs_s = smem_addr(xs);
   // Warp j < 8 computes expert i*8 + j over the whole row in the order of the
@@ -880,8 +955,8 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
           }
         }
       }
-      // Logit, then (lane m) the choice key of token m: choice_key(sigmoid +
-      // bias), so that the selection only compares keys.
+      // Lane m publishes token m's word: the choice key of sigmoid + bias
+      // (plus one, so that zero means "not written") and the logit.
       const float be = rbias ? __ldg(rbias + e) : 0.f;
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m) {
@@ -891,8 +966,8 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
           for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
           if (lane == m) {
             const float sc = 1.0f / (1.0f + expf(-v));
-            logits[(size_t)m * E + e] = v;
-            keys[(size_t)m * E + e] = choice_key(sc + be);
+            st_relaxed_u64(rwords + (size_t)m * E + e, router_word(choice_key(sc + be), v));
+            next_rwords[(size_t)m * E + e] = 0ull;
           }
         }
       }
@@ -904,22 +979,71 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
   if (threadIdx.x == 0 && experts > 0) red_release(done, experts);
 }
 
+// Polls the router words of token row `row` until every one of its E <= 256
+// experts is written (bounded), keeping key[j], lg[j] of expert lane + 32 j.
+// Returns false when the wait ended without them.
+__device__ bool poll_router_words(const StepParams& P, StPlan* pl,
+                                  const unsigned long long* row, int E, uint32_t (&key)[8],
+                                  float (&lg)[8]) {
+  const int lane = threadIdx.x & 31;
+  unsigned need = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    key[j] = 0u;
+    lg[j] = 0.f;
+    if (lane + 32 * j < E) need |= 1u << j;
+  }
+  unsigned have = 0;
+  const long long t0 = now_ns();
+  for (int spins = 0;; ++spins) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((need & ~have) & (1u << j)) {
+        const unsigned long long w = ld_relaxed_u64(row + lane + 32 * j);
+        if ((w >> 32) != 0ull) {
+          key[j] = (uint32_t)(w >> 32) - 1u;
+          lg[j] = __uint_as_float((uint32_t)w);
+          have |= 1u << j;
+        }
+      }
+    }
+    if (__all_sync(0xffffffffu, have == need)) return true;
+    __nanosleep(32);
+    if ((spins & 15) == 15) {
+      int stop = 0;
+      if (lane == 0) {
+        if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
+          pl->abort = 1;
+          stop = 1;
+        } else if (now_ns() - t0 > ST_WAIT_NS) {
+          raise_abort(P, pl, ERR_TIMEOUT);
+          stop = 1;
+        }
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+  }
+}
+
 // Top-k for every token (warp per token) and the expert plan (warp 0), in
-// every CTA from the same logits, so every CTA holds the same plan.  Slot 0
-// is the shared expert (bank slot E, every token, route R-1); routed experts
-// follow in order of first use (token-major, then route order).  Indices are
-// always in [0, E), whatever the logits hold.
+// every CTA from the same router words, so every CTA holds the same plan.
+// The words are read as soon as the router has written them (no completion
+// counter between).  Slot 0 is the shared expert (bank slot E, every token,
+// route R-1); routed experts follow in order of first use (token-major, then
+// route order).  Indices are always in [0, E), whatever the words hold.
 __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const StOp& rop = P.ops[up.router_op];
-  consumers_wait(P, pl, rop.done, rop.target);
-  if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 7);
   const int T = up.T, R = up.R, top_k = rop.top_k, E = rop.E;
+  const unsigned long long* words = rop.rwords + (size_t)pl->parity * T * E;
   for (int t = warp; t < T; t += NCW) {
+    uint32_t key[8];
+    float lg[8];
+    poll_router_words(P, pl, words + (size_t)t * E, E, key, lg);
+    if (t == 0 && lane == 0) trace_mark(P, pl->cur_op, 7);
     int my_idx = 0;
     float my_score = 0.f, wsum = 0.f;
-    warp_topk256_keys(reinterpret_cast<const uint32_t*>(rop.logits) + (size_t)(T + t) * E,
-                      rop.logits + (size_t)t * E, E, top_k, lane, my_idx, my_score, wsum);
+    warp_topk256_regs(key, lg, top_k, lane, my_idx, my_score, wsum);
     my_idx = min(max(my_idx, 0), E - 1);
     if (lane < top_k) {
       float wv = my_score;
@@ -1073,27 +1197,25 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
   }
 }
 
-// Down projection of every route (consumer side; the reducer writes the
-// per-route outputs and runs the combine).
+// Down projection of every route (consumer side).  The stager stages each
+// item's inputs (the activated rows of its slot) into one of dnb buffers once
+// the slot's gate/up is complete; the reducer writes the per-route outputs,
+// and the combine follows once every item of the operation is done.
 __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
-                             uint8_t* xs, Partials& pa) {
+                             const XBufs& X, uint8_t* xs, Partials& pa, DUse& du) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
   const int n = pl->nslots * op.items_rb;
   const int ts = token_stride(op.K);
   int rot = 0;
-  for (int i = first_item(op.rot); i < n; i += G) {
+  for (int i = first_item(op.rot); i < n; i += G, ++du.u) {
     Item it;
     st_describe_moe(op, pl, i, it);
-    // Inputs: the activated rows of this slot, complete once every row block
-    // of the slot's gate/up has been signalled.
-    consumers_wait(P, pl, op.slot_cnt + it.p, op.up_rb);
+    const int j = du.buf(X.dnb);
+    if (!stage_wait(&X.dready[j], du.phase(X.dnb), pl) && lane == 0 && !pl->abort)
+      raise_abort(P, pl, ERR_TIMEOUT);
     if (threadIdx.x == 0 && i < G) trace_mark(P, pl->cur_op, 1);
-    for (int m = 0; m < it.count; ++m)
-      stage_row_cg(xs + m * ts, op.mx + (size_t)pl->assign[it.abase + m] * op.mxs, op.K,
-                   threadIdx.x, NCT);
-    named_barrier(CBAR, NCT);
-    const uint8_t* xrow[1] = {xs + min(g, it.count - 1) * ts};
+    const uint8_t* xrow[1] = {xs + (size_t)j * X.drow_bytes + min(g, it.count - 1) * ts};
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
@@ -1101,11 +1223,10 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
     rot = (rot + 1) & (op.KS - 1);
     split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
     release_stage(R, s);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&X.dfree[j]);
     partial_publish(P, pa, pl, sp.slot, it.count, acc);
-    // xs is restaged for the next item only after every warp is done with it.
-    named_barrier(CBAR, NCT);
   }
-  (void)lane;
 }
 
 // Warps 0..7 own rows i = r*8 + warp (r < 16) of a 32-column slice, as the
@@ -1228,9 +1349,9 @@ struct MoeEpi {
   uint16_t* y;     // gate/up: activated rows
   uint16_t* wsy;   // down: per-route outputs
   uint16_t* out;   // down: combined rows
-  int* slot_cnt;   // gate/up: per-slot counters
-  int* arrive;     // down: (token, row block) counters
-  int* done;       // down: combined blocks
+  int* slot_cnt;    // gate/up: per-slot counters
+  int* items_done;  // down: finished items
+  int* done;        // down: combined blocks
   int N, R, KS, RBc;
 };
 
@@ -1240,7 +1361,7 @@ __device__ __forceinline__ MoeEpi moe_epi(const StepParams& P, const StOp& op) {
   m.wsy = op.wsy;
   m.out = op.out;
   m.slot_cnt = &P.sync[op.slot_cnt];
-  m.arrive = &P.sync[op.arrive];
+  m.items_done = &P.sync[op.items_done];
   m.done = &P.sync[op.done];
   m.N = op.N;
   m.R = op.R;
@@ -1274,60 +1395,57 @@ __device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, cons
   const int* assign = pl->assign + it.abase;
   const int cnt = it.count, rows = it.rows, r0 = it.r0;
   const int n = rows * cnt;
-  const int N = m.N, R = m.R;
+  const int N = m.N;
   uint16_t* const wsy = m.wsy;
-  uint16_t* const out = m.out;
   for (int idx = lane; idx < n; idx += 32) {
     const int r = idx / cnt, tok = idx - r * cnt;
     const float v = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
     wsy[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(v);
   }
   partial_release(pa);
-  // Arrival per (token, 16-row block), all of the item's pairs in one round
-  // (lane = row block * count + token slot): the R-th arrival combines that
-  // token's routes for those rows in route order.
-  const int top_k = R - 1;
+  return true;
+}
+
+// Combine of the (token, 16-row block) pairs p = first_item(rot) + k*grid
+// once every down item of the operation is done: out = bf16(sum_r
+// routed_r * w_r in route order) + shared, two pairs per pass (lanes 0-15 and
+// 16-31, one row each).  Returns false when the wait gave up.
+__device__ bool combine_pairs(const StepParams& P, const MoeEpi& m, StPlan* pl, int T, int rot,
+                              int total_items) {
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int N = m.N, R = m.R, top_k = R - 1;
   const int nrb = (N + 15) >> 4;
-  const int nrbi = (rows + 15) >> 4;
-  const int npairs = nrbi * cnt;
-  for (int base = 0; base < npairs; base += 32) {
-    const int pidx = base + lane;
-    int last = 0, my_tok = 0, my_rb = 0;
-    if (pidx < npairs) {
-      my_rb = pidx / cnt;
-      my_tok = assign[pidx - my_rb * cnt] / R;
-      __threadfence();
-      const int old = atomicAdd(m.arrive + my_tok * nrb + (r0 >> 4) + my_rb, 1);
-      last = (old == R - 1);
-    }
-    unsigned ready = __ballot_sync(0xffffffffu, last);
-    if (ready) __threadfence();
-    // Two (token, row block) pairs per pass: lanes 0-15 and 16-31.
-    while (ready) {
-      const int pa_lane = __ffs(ready) - 1;
-      ready &= ready - 1;
-      int pb_lane = -1;
-      if (ready) {
-        pb_lane = __ffs(ready) - 1;
-        ready &= ready - 1;
-      }
-      const int src = (lane < 16) ? pa_lane : pb_lane;
-      const int tok = __shfl_sync(0xffffffffu, my_tok, src < 0 ? 0 : src);
-      const int rb = __shfl_sync(0xffffffffu, my_rb, src < 0 ? 0 : src);
-      const int rr = lane & 15;
-      if (src >= 0 && rb * 16 + rr < rows) {
-        const int row = r0 + rb * 16 + rr;
+  const int npairs = T * nrb;
+  const int p0 = first_item(rot);
+  if (p0 >= npairs) return true;
+  if (!stager_poll(P, pl, (int)(m.items_done - P.sync), total_items)) return false;
+  const uint16_t* const wsy = m.wsy;
+  uint16_t* const out = m.out;
+  int combined = 0;
+  for (int p = p0; p < npairs; p += 2 * G) {
+    const int mine = (lane < 16) ? p : p + G;
+    if (mine < npairs) {
+      const int tok = mine / nrb, rb = mine - tok * nrb;
+      const int row = rb * 16 + (lane & 15);
+      if (row < N) {
         const uint16_t* ws = wsy + (size_t)tok * R * N + row;
         const float* rw = pl->route_w + tok * top_k;
-        float accum = 0.f;
-        for (int r = 0; r < top_k; ++r)
-          accum += bf16_bits_to_float(__ldcg(ws + (size_t)r * N)) * rw[r];
+        // Every route's value in flight at once, then the sum in route order.
+        uint16_t rv[ST_MAX_TOPK];
+#pragma unroll
+        for (int r = 0; r < ST_MAX_TOPK; ++r) rv[r] = r < top_k ? __ldcg(ws + (size_t)r * N) : 0;
         const uint16_t sv = __ldcg(ws + (size_t)(R - 1) * N);
+        float accum = 0.f;
+#pragma unroll
+        for (int r = 0; r < ST_MAX_TOPK; ++r)
+          if (r < top_k) accum += bf16_bits_to_float(rv[r]) * rw[r];
         out[(size_t)tok * N + row] = float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
       }
-      warp_signal(m.done, pb_lane >= 0 ? 2 : 1);
     }
+    combined += (p + G < npairs) ? 2 : 1;
   }
+  warp_signal(m.done, combined);
   return true;
 }
 
@@ -1392,11 +1510,17 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
     } else if (op.type == OP_MOE_DOWN) {
       const MoeEpi m = moe_epi(P, op);
       const int n = pl->nslots * op.items_rb;
-      for (int i = first_item(op.rot); i < n && ok; i += G) {
+      int items = 0;
+      for (int i = first_item(op.rot); i < n && ok; i += G, ++items) {
         Item it;
         st_describe_moe(op, pl, i, it);
         ok = reduce_down_item(m, pl, pa, it);
       }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0 && items > 0) red_release(m.items_done, items);
+      ok = combine_pairs(P, m, pl, op.T, op.rot, n);
+      if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(plan_ack);
       plan_phase ^= 1;
@@ -1440,6 +1564,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   X.desc = reinterpret_cast<StOp*>(smem + P.desc_off);
   X.ready = reinterpret_cast<uint64_t*>(pa.taken + 2);
   X.free = X.ready + 2;
+  X.dready = X.free + 2;
+  X.dfree = X.dready + ST_DNB;
+  X.dnb = P.dnb;
+  X.drow_bytes = P.drow_bytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P.stages; ++s) {
@@ -1453,6 +1581,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     for (int b = 0; b < 2; ++b) {
       mbar_init(&X.ready[b], 1);
       mbar_init(&X.free[b], NCW);
+    }
+    for (int b = 0; b < ST_DNB; ++b) {
+      mbar_init(&X.dready[b], 1);
+      mbar_init(&X.dfree[b], NCW);
     }
     mbar_fence_init();
     pl->abort = 0;
@@ -1474,13 +1606,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   }
   if (warp == NCW + 2) {
     pdl_wait();
-    stager_main(P, pl, X);
+    stager_main(P, pl, X, plan_bar);
     return;
   }
 
   // Counters are reset by the previous launch; wait for it to finish.
   pdl_wait();
+  if (threadIdx.x == 0) pl->parity = *((volatile int*)&P.sync[P.parity_idx]) & 1;
+  named_barrier(CBAR, NCT);
   uint32_t plan_round = 0;
+  DUse du;
   int xb = 0;
   uint32_t xph = 0;
   for (int o = 0; o < P.nops; ++o) {
@@ -1508,7 +1643,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
           run_moe_up(P, op, pl, R, plan_bar, plan_ack, plan_round, xs, pa);
           break;
         case OP_MOE_DOWN:
-          run_moe_down(P, op, pl, R, xs, pa);
+          run_moe_down(P, op, pl, R, X, xs, pa, du);
           break;
         default:
           break;
@@ -1535,7 +1670,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   named_barrier(CBAR, NCT);
   if (pl->last) {
     for (int i = threadIdx.x; i < P.nsync; i += NCT)
-      if (i != P.exit_idx) P.sync[i] = 0;
+      if (i != P.exit_idx && i != P.parity_idx) P.sync[i] = 0;
+    if (threadIdx.x == 0) P.sync[P.parity_idx] = pl->parity ^ 1;
     __threadfence();
     named_barrier(CBAR, NCT);
     if (threadIdx.x == 0) P.sync[P.exit_idx] = 0;
@@ -1764,19 +1900,20 @@ int kb_step_add_swiglu(kb_step* step, const uint16_t* x, int64_t x_stride, int64
 
 int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride, int64_t K,
                        const uint16_t* weight, const float* bias, int64_t E, int64_t top_k,
-                       int renormalize, float scaling, float* logits, int64_t* idx_out,
+                       int renormalize, float scaling, void* scratch, int64_t* idx_out,
                        float* w_out, const int* deps, int ndeps, int* op_out) {
   kb::clear_error();
   StepProgram* pr = reinterpret_cast<StepProgram*>(step);
-  KB_REQUIRE(pr && hidden && weight && logits && idx_out && w_out && op_out,
+  KB_REQUIRE(pr && hidden && weight && scratch && idx_out && w_out && op_out,
              KB_ERR_NULL_POINTER, "NULL argument");
   KB_REQUIRE(!pr->finalized, KB_ERR_UNSUPPORTED, "program already finalized");
   KB_REQUIRE(E >= 1 && E <= kb::ST_MAX_E && top_k >= 1 && top_k <= kb::ST_MAX_TOPK &&
                  top_k <= E && K > 0 && K % 8 == 0 && K <= 8192,
              KB_ERR_UNSUPPORTED, "step router supports E <= %d, top_k <= %d, K %% 8 == 0",
              kb::ST_MAX_E, kb::ST_MAX_TOPK);
-  KB_REQUIRE(kb::aligned(hidden, 16) && h_stride % 8 == 0 && kb::aligned(weight, 16),
-             KB_ERR_ALIGNMENT, "hidden/weight must be 16-byte aligned");
+  KB_REQUIRE(kb::aligned(hidden, 16) && h_stride % 8 == 0 && kb::aligned(weight, 16) &&
+                 kb::aligned(scratch, 8),
+             KB_ERR_ALIGNMENT, "hidden/weight must be 16-byte aligned, scratch 8-byte aligned");
   kb::StOp op = {};
   op.type = kb::OP_ROUTER;
   op.T = pr->T;
@@ -1791,7 +1928,7 @@ int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride, 
   op.top_k = (int)top_k;
   op.renorm = renormalize;
   op.scaling = scaling;
-  op.logits = logits;
+  op.rwords = static_cast<unsigned long long*>(scratch);
   op.idx_out = idx_out;
   op.w_out = w_out;
   op.items = (int)((E + kb::ST_RT_EXPERTS - 1) / kb::ST_RT_EXPERTS);
@@ -1888,7 +2025,7 @@ int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden, int64_
   dn.out = out;
   dn.rot = ((up_index + 1) * 37) % kb::current_sms();
   dn.done = kb::add_sync(pr, 1);
-  dn.arrive = kb::add_sync(pr, T * (int)((H + 15) / 16));
+  dn.items_done = kb::add_sync(pr, 1);
   dn.target = T * (int)((H + 15) / 16);
   *op_out = (int)pr->ops.size();
   pr->ops.push_back(dn);
@@ -1950,7 +2087,7 @@ int kb_step_finalize(kb_step* step) {
   KB_REQUIRE(G > 0, KB_ERR_DEVICE, "cannot query the SM count");
   const int T = pr->T;
   // Rotations and the largest stage and activation regions.
-  int stage = 0, xbytes = 0, cum = 0;
+  int stage = 0, xbytes = 0, cum = 0, drow = 0;
   for (size_t o = 0; o < pr->ops.size(); ++o) {
     kb::StOp& op = pr->ops[o];
     switch (op.type) {
@@ -1982,6 +2119,7 @@ int kb_step_finalize(kb_step* step) {
         stage = std::max(stage,
                          kb::item_stage_bytes(op.K, mats, op.RBc, op.K >> (5 + op.gshift)));
         xbytes = std::max(xbytes, T * kb::token_stride(op.K));
+        if (op.type == kb::OP_MOE_DOWN) drow = std::max(drow, T * kb::token_stride(op.K));
         break;
       }
       case kb::OP_KDA:
@@ -1993,12 +2131,14 @@ int kb_step_finalize(kb_step* step) {
   stage = (stage + 127) / 128 * 128;
   const int exit_idx = kb::add_sync(pr, 1);
   const int abort_idx = kb::add_sync(pr, 1);
+  const int parity_idx = kb::add_sync(pr, 1);
   kb::StepParams& P = pr->params;
   P = {};
   P.nops = (int)pr->ops.size();
   P.nsync = pr->nsync;
   P.exit_idx = exit_idx;
   P.abort_idx = abort_idx;
+  P.parity_idx = parity_idx;
   P.stage_bytes = stage;
   P.T = T;
   const int scr = (int)(sizeof(kb::StPlan) + sizeof(kb::StKda) + 127) / 128 * 128;
@@ -2008,8 +2148,11 @@ int kb_step_finalize(kb_step* step) {
   // three ring stages remain, else one.
   P.part_bytes = kb::ST_NB * kb::NCW * 16 * T * (int)sizeof(float);
   P.x_bytes = (xbytes + 127) / 128 * 128;
+  // Down inputs: as many item buffers as fit in one activation buffer.
+  P.drow_bytes = std::max(128, (drow + 127) / 128 * 128);
+  P.dnb = std::max(1, std::min(kb::ST_DNB, P.x_bytes / P.drow_bytes));
   const int desc_bytes = ((int)sizeof(kb::StOp) + 127) / 128 * 128;
-  const int nbar = 2 * 0 + 2 + kb::ST_NB + 1 + 4;
+  const int nbar = 2 + kb::ST_NB + 1 + 4 + 2 * kb::ST_DNB;
   for (int nxb = 2; nxb >= 1; --nxb) {
     P.nxb = nxb;
     P.desc_off = nxb * P.x_bytes;
@@ -2024,7 +2167,7 @@ int kb_step_finalize(kb_step* step) {
              "shared memory: %d bytes of fixed regions leave room for %d stages of %d bytes",
              P.ring_off, P.stages, stage);
   P.bar_off = P.ring_off + P.stages * stage;
-  pr->smem = (size_t)P.bar_off + (2 * P.stages + 2 + kb::ST_NB + 1 + 4) * sizeof(uint64_t);
+  pr->smem = (size_t)P.bar_off + (2 * P.stages + nbar) * sizeof(uint64_t);
   KB_REQUIRE(pr->smem <= (size_t)kb::MAX_SMEM, KB_ERR_UNSUPPORTED, "shared memory overflow");
   P.err = kb::device_error_word(dev);
   KB_REQUIRE(P.err, KB_ERR_DEVICE, "device error word unavailable");
@@ -2034,6 +2177,11 @@ int kb_step_finalize(kb_step* step) {
     e = cudaMemcpy(pr->d_ops, pr->ops.data(), pr->ops.size() * sizeof(kb::StOp),
                    cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(pr->d_sync, 0, (size_t)pr->nsync * sizeof(int));
+  // Router words: zero means "not written"; each launch clears the other
+  // launch parity's words for the next.
+  for (size_t o = 0; o < pr->ops.size() && e == cudaSuccess; ++o)
+    if (pr->ops[o].type == kb::OP_ROUTER)
+      e = cudaMemset(pr->ops[o].rwords, 0, (size_t)2 * T * pr->ops[o].E * sizeof(uint64_t));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(kb::step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kb::MAX_SMEM);

@@ -136,24 +136,35 @@ __device__ __forceinline__ void warp_topk256(const float* lrow, const float* bia
   }
 }
 
-// Top-k of one token from precomputed choice keys (choice_key of score +
-// bias, written by the router logits pass; NaN -> 0), E <= 256, one warp.
-// keys/logits are read with L2-only loads.  Same result and pick order as
-// warp_topk256: picks in (choice desc, index asc) order; lane r < top_k gets
-// pick r and its unbiased score sigmoid(logit); every lane gets wsum, the
-// sum of the picked scores in pick order.
-__device__ __forceinline__ void warp_topk256_keys(const uint32_t* keys, const float* lrow,
-                                                  int E, int top_k, int lane, int& my_idx,
+// Router word of one (token, expert): choice key + 1 in the high half (zero
+// means "not yet written"; keys stay below 0xff800001, so the sum does not
+// wrap) and the fp32 logit in the low half, published with one 64-bit store
+// so that a reader sees both or neither.
+__device__ __forceinline__ unsigned long long router_word(uint32_t key, float logit) {
+  return ((unsigned long long)(key + 1u) << 32) | __float_as_uint(logit);
+}
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Top-k of one token from the keys and logits of its E <= 256 experts held
+// in registers (expert lane + 32 j in key[j], lg[j]); one warp.  Same
+// selection as warp_topk256 (largest key, lowest index among equal keys):
+// per pick, a warp max-reduction of the lane maxima, then the lowest index
+// among the holders.  Lane r < top_k receives the r-th pick, its sigmoid
+// score and the sum of the picked scores in pick order.  Keys are consumed.
+__device__ __forceinline__ void warp_topk256_regs(uint32_t (&key)[8], const float (&lg)[8],
+                                                  int top_k, int lane, int& my_idx,
                                                   float& my_score, float& wsum) {
-  uint32_t key[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int e = lane + 32 * j;
-    key[j] = (e < E) ? __ldcg(&keys[e]) : 0u;
-  }
-  // Expert ids of a lane increase with j (e = lane + 32 j), so the first j
-  // holding a key is the lowest index among this lane's ties.
   int pick_idx = 0;
+  float pick_logit = 0.f;
   for (int sel = 0; sel < top_k; ++sel) {
     uint32_t lm = key[0];
 #pragma unroll
@@ -170,15 +181,23 @@ __device__ __forceinline__ void warp_topk256_keys(const uint32_t* keys, const fl
       win = __shfl_sync(0xffffffffu, cand, __ffs(holders) - 1);
     else
       win = (int)__reduce_min_sync(0xffffffffu, (uint32_t)cand);
+    float wl = 0.f;
     if ((win & 31) == lane) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (j == (win >> 5)) key[j] = 0u;
+        if (j == (win >> 5)) {
+          key[j] = 0u;
+          wl = lg[j];
+        }
     }
-    if (lane == sel) pick_idx = win;
+    const float l = __shfl_sync(0xffffffffu, wl, win & 31);
+    if (lane == sel) {
+      pick_idx = win;
+      pick_logit = l;
+    }
   }
   float s = 0.f;
-  if (lane < top_k) s = 1.0f / (1.0f + expf(-__ldcg(&lrow[pick_idx])));
+  if (lane < top_k) s = 1.0f / (1.0f + expf(-pick_logit));
   wsum = 0.f;
   for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, s, r);
   my_idx = pick_idx;

@@ -232,7 +232,7 @@ class HotPathDecoder:
             "routed": torch.empty((B * (s.top_k + 1), s.hidden), dtype=bf, device=dev),
             "act0": torch.empty((B, s.dense_intermediate), dtype=bf, device=dev),
             "logits": torch.empty((B, s.vocab_size), dtype=bf, device=dev),
-            "router_logits": [], "idx": [], "weights": [],
+            "router_scratch": [], "idx": [], "weights": [],
         }
         prog = StepProgram(B)
         prev = None
@@ -258,10 +258,10 @@ class HotPathDecoder:
                 prev = prog.dense([(buf["act0"], w2p, w2s, xout)], deps=[sw])
             else:
                 m = lw.moe
-                lg = torch.empty((2, B, m.num_experts), dtype=torch.float32, device=dev)
+                lg = StepProgram.router_scratch(B, m.num_experts, dev)
                 idx = torch.empty((B, m.top_k + 1), dtype=torch.long, device=dev)
                 wts = torch.empty((B, m.top_k), dtype=torch.float32, device=dev)
-                buf["router_logits"].append(lg)
+                buf["router_scratch"].append(lg)
                 buf["idx"].append(idx)
                 buf["weights"].append(wts)
                 r = prog.router(buf["h"], m.router_weight, m.router_bias, m.top_k, m.scaling, lg,

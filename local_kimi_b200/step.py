@@ -106,17 +106,22 @@ class StepProgram:
                   c_int64(_group(w1p, w1s)), _p(y), c_int64(y.stride(0)), d, nd, ref)
         return o.value
 
-    def router(self, hidden, weight, bias, top_k, scaling, logits, idx_out, w_out,
+    def router(self, hidden, weight, bias, top_k, scaling, scratch, idx_out, w_out,
                renormalize=True, deps=None) -> int:
-        """Router logits into ``logits`` (fp32 scratch of 2*T*E: the logits, then
-        the choice keys; one buffer per router of the program); the selection
-        runs in the expert block that uses this router and writes idx_out
-        int64 [T, top_k+1] (shared id appended) and w_out."""
+        """Router logits into ``scratch`` (16 * T * E bytes, contiguous, owned by
+        the program: per launch parity and (token, expert) a 64-bit word with
+        the choice key and the logit; one buffer per router, see
+        ``router_scratch``); the selection runs in the expert block that uses
+        this router and writes idx_out int64 [T, top_k+1] (shared id appended)
+        and w_out."""
         _require(hidden, torch.bfloat16, "hidden states")
         _require(weight, torch.bfloat16, "router weight")
-        _require(logits, torch.float32, "logits")
-        if logits.numel() < 2 * hidden.shape[0] * weight.shape[0] or not logits.is_contiguous():
-            raise ValueError("logits scratch must be contiguous with 2 * tokens * experts floats")
+        if scratch.device.type != "cuda" or not scratch.is_contiguous():
+            raise ValueError("router scratch must be a contiguous CUDA tensor")
+        need = 16 * hidden.shape[0] * weight.shape[0]
+        if scratch.numel() * scratch.element_size() < need:
+            raise ValueError(f"router scratch needs {need} bytes")
+        logits = scratch
         b = None
         if bias is not None:
             b = bias.to(torch.float32).contiguous()
@@ -128,6 +133,11 @@ class StepProgram:
                   c_int64(top_k), 1 if renormalize else 0, c_float(float(scaling)), _p(logits),
                   _p(idx_out), _p(w_out), d, nd, ref)
         return o.value
+
+    @staticmethod
+    def router_scratch(tokens: int, experts: int, device=None) -> torch.Tensor:
+        """A router scratch buffer for ``router``: [2, tokens, experts] int64."""
+        return torch.empty((2, tokens, experts), dtype=torch.int64, device=device or "cuda")
 
     def moe(self, router_op, hidden, layer, activated, routed_out, out, deps=None) -> int:
         """Expert block of one MoE layer (MoELayerWeights); returns the index of

@@ -86,7 +86,7 @@ def test_step_moe_layer_matches_oracle_and_per_op(cuda, tokens):
     gen = cuda_gen(20 + tokens)
     layer = _moe_layer(128, gen)
     h = rand_act((tokens, 2304), gen)
-    lg = torch.empty((2, tokens, 256), dtype=torch.float32, device=cuda)
+    lg = StepProgram.router_scratch(tokens, 256, cuda)
     idx = torch.empty((tokens, 9), dtype=torch.long, device=cuda)
     wts = torch.empty((tokens, 8), dtype=torch.float32, device=cuda)
     act = torch.empty((tokens * 9, 1024), dtype=torch.bfloat16, device=cuda)
