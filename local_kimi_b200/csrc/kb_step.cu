@@ -114,6 +114,7 @@ struct StOp {
   const uint16_t* s1;
   int64_t wse, sse;
   int N, gshift, KS, RBc, items_rb, R, up_rb;
+  int sbulk;  // expert scale banks 16-byte aligned per expert: items stage their scales
   uint16_t* y;
   uint16_t* out;
   uint16_t* wsy;
@@ -316,6 +317,13 @@ __device__ __forceinline__ void st_describe_dense(const StOp& op, int item, Item
   it.count = op.T;
 }
 
+// Scales of an expert item are staged with its weights when every expert's
+// scale rows start 16-byte aligned (host-checked) and the item's scale block
+// is a whole number of 16-byte units (row offsets are multiples of 16 rows).
+__device__ __forceinline__ bool expert_scale_bulk(const StOp& op, int rows) {
+  return op.sbulk && ((rows * (op.K >> (5 + op.gshift)) * 2) & 15) == 0;
+}
+
 // Slot s of the plan: expert slot_expert[s], assignments assign[start..end).
 __device__ __forceinline__ void st_describe_moe(const StOp& op, const StPlan* pl, int item,
                                                 Item& it) {
@@ -336,8 +344,7 @@ __device__ __forceinline__ void st_describe_moe(const StOp& op, const StPlan* pl
   it.rows = min(op.RBc * 16, op.N - it.r0);
   it.RS = row_stride_bytes(op.K);
   it.ng = op.K >> (5 + op.gshift);
-  it.scale_bulk = scale_bulk_ok(it.s[0], it.r0, it.rows, it.ng) &&
-                  (it.mats == 1 || scale_bulk_ok(it.s[1], it.r0, it.rows, it.ng));
+  it.scale_bulk = expert_scale_bulk(op, it.rows);
   it.p = slot;
   it.abase = pl->slot_start[slot];
   it.count = pl->slot_start[slot + 1] - it.abase;
@@ -361,8 +368,7 @@ __device__ __forceinline__ void st_describe_shared(const StOp& op, int item, Ite
   it.rows = min(op.RBc * 16, op.N - it.r0);
   it.RS = row_stride_bytes(op.K);
   it.ng = op.K >> (5 + op.gshift);
-  it.scale_bulk = scale_bulk_ok(it.s[0], it.r0, it.rows, it.ng) &&
-                  (it.mats == 1 || scale_bulk_ok(it.s[1], it.r0, it.rows, it.ng));
+  it.scale_bulk = expert_scale_bulk(op, it.rows);
   it.p = 0;
   it.abase = 0;
   it.count = op.T;
@@ -1139,45 +1145,125 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
   named_barrier(CBAR, NCT);
 }
 
-// Gate/up of one item (the reducer applies SwiGLU, writes and signals).
-__device__ void moe_up_item(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
-                            const uint8_t* xs, Partials& pa, const Item& it, int rot) {
-  const int lane = threadIdx.x & 31, g = lane >> 2;
-  const int ts = token_stride(op.K);
-  const int m = min(g, it.count - 1);
-  const int a = pl->assign[it.abase + m];
-  const uint8_t* xrow[1] = {xs + (a / op.R) * ts};
-  float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-  int s;
-  const uint8_t* stage = consume_stage(P, R, pl, &s);
-  const Split sp = split_of(it, stage, rot);
-  split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
-  release_stage(R, s);
-  partial_publish(P, pa, pl, sp.slot, it.count, acc);
+// Item-invariant part of an expert operation's items for one consumer warp
+// (read once per operation; per item only the slot, row group and token rows
+// change).  KS and RBc are powers of two.
+struct ExpertWarp {
+  int K, N, gshift, ng, KB, KS, kslog, item_rows, items_rb;
+  int pslot_base;      // partial slot of this warp's (matrix, row block), + slice
+  int rb;              // row block within the item
+  int ks;              // reduction slice before rotation
+  int wt_off, sc_off;  // stage offsets of this warp's weight tile and scale rows
+  int64_t sse;         // scale elements per expert
+  const uint16_t* s;   // scales of this warp's matrix, expert 0
+  int sbulk;
+};
+
+__device__ __forceinline__ ExpertWarp expert_warp(const StOp& op) {
+  const int warp = threadIdx.x >> 5;
+  ExpertWarp w;
+  w.K = op.K;
+  w.N = op.N;
+  w.gshift = op.gshift;
+  w.ng = op.K >> (5 + op.gshift);
+  w.KB = (op.K + 127) >> 7;
+  w.KS = op.KS;
+  w.kslog = __ffs(op.KS) - 1;
+  w.item_rows = op.RBc * 16;
+  w.items_rb = op.items_rb;
+  const int per_mat = op.RBc * op.KS;
+  const int mat = warp / per_mat;
+  const int rem = warp - mat * per_mat;
+  w.rb = rem >> w.kslog;
+  w.ks = rem & (op.KS - 1);
+  w.pslot_base = mat * per_mat + w.rb * op.KS;
+  const int RS = op.K >> 1;
+  const int mats = (op.type == OP_MOE_UP) ? 2 : 1;
+  w.wt_off = (mat * w.item_rows + w.rb * 16) * RS;
+  w.sc_off = mats * w.item_rows * RS + mat * ((w.item_rows * w.ng * 2 + 15) / 16 * 16) +
+             w.rb * 16 * w.ng * 2;
+  w.sse = op.sse;
+  w.s = mat ? op.s1 : op.s0;
+  w.sbulk = op.sbulk;
+  return w;
 }
 
+// Item i = slot * items_rb + row group, advanced by the grid without divisions.
+struct ExpertIter {
+  int i, slot, rbg;
+  __device__ __forceinline__ void start(int first, int items_rb) {
+    i = first;
+    slot = first / items_rb;
+    rbg = first - slot * items_rb;
+  }
+  __device__ __forceinline__ void next(int G, int items_rb) {
+    i += G;
+    rbg += G;
+    while (rbg >= items_rb) {
+      rbg -= items_rb;
+      ++slot;
+    }
+  }
+};
+
+// One expert item (row group rbg of expert e, cnt token rows; xrow0: this
+// lane's activation row): the warp's row block over its rotated reduction
+// slice, partial to the reducer.
+__device__ __forceinline__ void expert_item(const StepParams& P, const ExpertWarp& w, StPlan* pl,
+                                            Ring& R, Partials& pa, int e, int rbg, int cnt,
+                                            const uint8_t* xrow0, int& rot) {
+  const int r0 = rbg * w.item_rows;
+  const int rows = min(w.item_rows, w.N - r0);
+  const int rb_rows = min(16, rows - w.rb * 16);
+  const bool bulk = w.sbulk && ((rows * w.ng * 2) & 15) == 0;
+  const int ksr = (w.ks + rot) & (w.KS - 1);
+  rot = (rot + 1) & (w.KS - 1);
+  const int kb0 = (w.KB * ksr) >> w.kslog, kb1 = (w.KB * (ksr + 1)) >> w.kslog;
+  const uint8_t* xrow[1] = {xrow0};
+  float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+  int st;
+  const uint8_t* stage = consume_stage(P, R, pl, &st);
+  if (rb_rows > 0 && kb1 > kb0) {
+    if (bulk)
+      rowblock_compute<1, true>(stage + w.wt_off, w.K >> 1,
+                                reinterpret_cast<const uint16_t*>(stage + w.sc_off), w.ng,
+                                rb_rows, w.K, w.gshift, kb0, kb1, xrow, 1, acc);
+    else
+      rowblock_compute<1>(stage + w.wt_off, w.K >> 1,
+                          w.s + (size_t)e * w.sse + (size_t)(r0 + w.rb * 16) * w.ng, w.ng,
+                          rb_rows, w.K, w.gshift, kb0, kb1, xrow, 1, acc);
+  }
+  release_stage(R, st);
+  partial_publish(P, pa, pl, w.pslot_base + ksr, cnt, acc);
+}
+
+// Gate/up + SwiGLU of the shared expert, then (after the routing) of every
+// routed expert; the reducer applies SwiGLU, writes and signals per slot.
 __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
                            uint64_t* plan_bar, uint64_t* plan_ack, uint32_t& plan_round,
                            uint8_t* xs, Partials& pa) {
-  const int G = gridDim.x;
+  const int G = gridDim.x, g = (threadIdx.x & 31) >> 2;
+  const ExpertWarp w = expert_warp(op);
+  const int T = op.T, Rr = op.R, E = op.E;
+  const int ts = token_stride(op.K);
+  // Token of assignment a = t*R + r without a division (a < 2^16 / R).
+  const uint32_t rinv = (65536u + (uint32_t)Rr - 1u) / (uint32_t)Rr;
   // The shared slot needs no routing: its assignments are t*R + R-1 (the
   // producer may still be reading the previous plan, which holds the same
   // values for slot 0).
-  if (threadIdx.x < op.T) pl->assign[threadIdx.x] = threadIdx.x * op.R + op.R - 1;
+  if (threadIdx.x < T) pl->assign[threadIdx.x] = threadIdx.x * Rr + Rr - 1;
   if (threadIdx.x == 0) {
     pl->slot_start[0] = 0;
-    pl->slot_start[1] = op.T;
-    pl->slot_expert[0] = op.E;
+    pl->slot_start[1] = T;
+    pl->slot_expert[0] = E;
   }
   named_barrier(CBAR, NCT);
-  int i = first_item(op.rot);
+  ExpertIter it;
+  it.start(first_item(op.rot), w.items_rb);
   int rot = 0;
-  for (; i < op.items_rb; i += G) {
-    Item it;
-    st_describe_shared(op, i, it);
-    moe_up_item(P, op, pl, R, xs, pa, it, rot);
-    rot = (rot + 1) & (op.KS - 1);
-  }
+  const uint8_t* xshared = xs + min(g, T - 1) * ts;
+  for (; it.i < w.items_rb; it.next(G, w.items_rb))
+    expert_item(P, w, pl, R, pa, E, it.rbg, T, xshared, rot);
   if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 6);
   // The producer must be done with the previous plan before it is replaced.
   if (plan_round > 0) {
@@ -1188,12 +1274,13 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
   build_routing(P, op, pl);
   if (threadIdx.x == 0) mbar_arrive(plan_bar);
   ++plan_round;
-  const int n = pl->nslots * op.items_rb;
-  for (; i < n; i += G) {
-    Item it;
-    st_describe_moe(op, pl, i, it);
-    moe_up_item(P, op, pl, R, xs, pa, it, rot);
-    rot = (rot + 1) & (op.KS - 1);
+  const int n = pl->nslots * w.items_rb;
+  for (; it.i < n; it.next(G, w.items_rb)) {
+    const int abase = pl->slot_start[it.slot];
+    const int cnt = pl->slot_start[it.slot + 1] - abase;
+    const int a = pl->assign[abase + min(g, cnt - 1)];
+    const int tok = (int)(((uint32_t)a * rinv) >> 16);
+    expert_item(P, w, pl, R, pa, pl->slot_expert[it.slot], it.rbg, cnt, xs + tok * ts, rot);
   }
 }
 
@@ -1205,27 +1292,24 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
                              const XBufs& X, uint8_t* xs, Partials& pa, DUse& du) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
-  const int n = pl->nslots * op.items_rb;
+  const ExpertWarp w = expert_warp(op);
+  const int n = pl->nslots * w.items_rb;
   const int ts = token_stride(op.K);
+  const int dnb = X.dnb, drow = X.drow_bytes;
   int rot = 0;
-  for (int i = first_item(op.rot); i < n; i += G, ++du.u) {
-    Item it;
-    st_describe_moe(op, pl, i, it);
-    const int j = du.buf(X.dnb);
-    if (!stage_wait(&X.dready[j], du.phase(X.dnb), pl) && lane == 0 && !pl->abort)
+  ExpertIter it;
+  for (it.start(first_item(op.rot), w.items_rb); it.i < n; it.next(G, w.items_rb), ++du.u) {
+    const int abase = pl->slot_start[it.slot];
+    const int cnt = pl->slot_start[it.slot + 1] - abase;
+    const int j = du.buf(dnb);
+    if (!stage_wait(&X.dready[j], du.phase(dnb), pl) && lane == 0 && !pl->abort)
       raise_abort(P, pl, ERR_TIMEOUT);
-    if (threadIdx.x == 0 && i < G) trace_mark(P, pl->cur_op, 1);
-    const uint8_t* xrow[1] = {xs + (size_t)j * X.drow_bytes + min(g, it.count - 1) * ts};
-    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-    int s;
-    const uint8_t* stage = consume_stage(P, R, pl, &s);
-    const Split sp = split_of(it, stage, rot);
-    rot = (rot + 1) & (op.KS - 1);
-    split_compute(it, sp, sp.wtile, 0, (it.K + 127) >> 7, xrow, acc);
-    release_stage(R, s);
-    __syncwarp();
+    if (threadIdx.x == 0 && it.i < G) trace_mark(P, pl->cur_op, 1);
+    // The input buffer is freed once every warp has published its part (the
+    // publish synchronizes the warp after its last read of the buffer).
+    expert_item(P, w, pl, R, pa, pl->slot_expert[it.slot], it.rbg, cnt,
+                xs + (size_t)j * drow + min(g, cnt - 1) * ts, rot);
     if (lane == 0) mbar_arrive(&X.dfree[j]);
-    partial_publish(P, pa, pl, sp.slot, it.count, acc);
   }
 }
 
@@ -1352,7 +1436,7 @@ struct MoeEpi {
   int* slot_cnt;    // gate/up: per-slot counters
   int* items_done;  // down: finished items
   int* done;        // down: combined blocks
-  int N, R, KS, RBc;
+  int N, R, KS, RBc, items_rb, item_rows;
 };
 
 __device__ __forceinline__ MoeEpi moe_epi(const StepParams& P, const StOp& op) {
@@ -1367,40 +1451,65 @@ __device__ __forceinline__ MoeEpi moe_epi(const StepParams& P, const StOp& op) {
   m.R = op.R;
   m.KS = op.KS;
   m.RBc = op.RBc;
+  m.items_rb = op.items_rb;
+  m.item_rows = op.RBc * 16;
   return m;
 }
 
-__device__ bool reduce_up_item(const MoeEpi& m, StPlan* pl, Partials& pa, const Item& it) {
+// Epilogue of one gate/up item (slot ei.slot, row group ei.rbg; assignments
+// assign[abase .. abase+cnt)): SwiGLU of the summed slices into the activated
+// rows, then the slot's counter.
+__device__ bool reduce_up_item(const MoeEpi& m, StPlan* pl, Partials& pa, int abase, int cnt,
+                               const ExpertIter& ei) {
   const int lane = threadIdx.x & 31;
   if (!partial_take(pa, pl)) return false;
-  const int* assign = pl->assign + it.abase;
-  const int cnt = it.count, rows = it.rows, r0 = it.r0;
-  const int n = rows * cnt;
+  const int* assign = pl->assign + abase;
+  const int r0 = ei.rbg * m.item_rows;
+  const int rows = min(m.item_rows, m.N - r0);
   uint16_t* const y = m.y;
   const int N = m.N;
-  for (int idx = lane; idx < n; idx += 32) {
-    const int r = idx / cnt, tok = idx - r * cnt;
-    const float g = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
-    const float u = partial_sum(pa, 1, m.RBc, m.KS, r >> 4, r & 15, tok);
-    y[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(swiglu_contract(g, u));
+  if (cnt == 1) {
+    uint16_t* const yrow = y + (size_t)assign[0] * N + r0;
+    for (int r = lane; r < rows; r += 32) {
+      const float gv = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, 0);
+      const float uv = partial_sum(pa, 1, m.RBc, m.KS, r >> 4, r & 15, 0);
+      yrow[r] = float_to_bf16_bits(swiglu_contract(gv, uv));
+    }
+  } else {
+    const int n = rows * cnt;
+    for (int idx = lane; idx < n; idx += 32) {
+      const int r = idx / cnt, tok = idx - r * cnt;
+      const float gv = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
+      const float uv = partial_sum(pa, 1, m.RBc, m.KS, r >> 4, r & 15, tok);
+      y[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(swiglu_contract(gv, uv));
+    }
   }
   partial_release(pa);
-  if (lane == 0) red_release(m.slot_cnt + it.p, (rows + 15) >> 4);
+  if (lane == 0) red_release(m.slot_cnt + ei.slot, (rows + 15) >> 4);
   return true;
 }
 
-__device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, const Item& it) {
+// Epilogue of one down item: the per-route outputs.
+__device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, int abase, int cnt,
+                                 const ExpertIter& ei) {
   const int lane = threadIdx.x & 31;
   if (!partial_take(pa, pl)) return false;
-  const int* assign = pl->assign + it.abase;
-  const int cnt = it.count, rows = it.rows, r0 = it.r0;
-  const int n = rows * cnt;
+  const int* assign = pl->assign + abase;
+  const int r0 = ei.rbg * m.item_rows;
+  const int rows = min(m.item_rows, m.N - r0);
   const int N = m.N;
   uint16_t* const wsy = m.wsy;
-  for (int idx = lane; idx < n; idx += 32) {
-    const int r = idx / cnt, tok = idx - r * cnt;
-    const float v = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
-    wsy[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(v);
+  if (cnt == 1) {
+    uint16_t* const yrow = wsy + (size_t)assign[0] * N + r0;
+    for (int r = lane; r < rows; r += 32)
+      yrow[r] = float_to_bf16_bits(partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, 0));
+  } else {
+    const int n = rows * cnt;
+    for (int idx = lane; idx < n; idx += 32) {
+      const int r = idx / cnt, tok = idx - r * cnt;
+      const float v = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
+      wsy[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(v);
+    }
   }
   partial_release(pa);
   return true;
@@ -1492,29 +1601,25 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       if (lane == 0 && blocks > 0) red_release(&P.sync[op.done], blocks);
     } else if (op.type == OP_MOE_UP) {
       const MoeEpi m = moe_epi(P, op);
-      int i = first_item(op.rot);
-      for (; i < op.items_rb && ok; i += G) {
-        Item it;
-        st_describe_shared(op, i, it);
-        it.abase = 0;
-        ok = reduce_up_item(m, pl, pa, it);
-      }
+      ExpertIter ei;
+      ei.start(first_item(op.rot), m.items_rb);
+      for (; ei.i < m.items_rb && ok; ei.next(G, m.items_rb))
+        ok = reduce_up_item(m, pl, pa, 0, op.T, ei);
       if (!ok) break;
       if (!stage_wait(plan_bar, plan_phase, pl)) break;
-      const int n = pl->nslots * op.items_rb;
-      for (; i < n && ok; i += G) {
-        Item it;
-        st_describe_moe(op, pl, i, it);
-        ok = reduce_up_item(m, pl, pa, it);
+      const int n = pl->nslots * m.items_rb;
+      for (; ei.i < n && ok; ei.next(G, m.items_rb)) {
+        const int abase = pl->slot_start[ei.slot];
+        ok = reduce_up_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei);
       }
     } else if (op.type == OP_MOE_DOWN) {
       const MoeEpi m = moe_epi(P, op);
-      const int n = pl->nslots * op.items_rb;
+      const int n = pl->nslots * m.items_rb;
       int items = 0;
-      for (int i = first_item(op.rot); i < n && ok; i += G, ++items) {
-        Item it;
-        st_describe_moe(op, pl, i, it);
-        ok = reduce_down_item(m, pl, pa, it);
+      ExpertIter ei;
+      for (ei.start(first_item(op.rot), m.items_rb); ei.i < n && ok; ei.next(G, m.items_rb), ++items) {
+        const int abase = pl->slot_start[ei.slot];
+        ok = reduce_down_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei);
       }
       if (!ok) break;
       __syncwarp();
@@ -1993,6 +2098,7 @@ int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden, int64_
                  &up.KS, &up.RBc, &nchunk);
   up.items_rb = (int)((I + 16 * up.RBc - 1) / (16 * up.RBc));
   up.y = activated;
+  up.sbulk = kb::aligned(w1_scales, 16) && kb::aligned(w3_scales, 16) && (up.sse * 2) % 16 == 0;
   up.rot = ((int)pr->ops.size() * 37) % kb::current_sms();
   up.done = kb::add_sync(pr, 1);
   up.slot_cnt = kb::add_sync(pr, kb::ST_MAX_SLOTS);
@@ -2023,6 +2129,7 @@ int kb_step_add_moe(kb_step* step, int router_op, const uint16_t* hidden, int64_
   dn.slot_cnt = pr->ops[up_index].slot_cnt;
   dn.wsy = routed_out;
   dn.out = out;
+  dn.sbulk = kb::aligned(w2_scales, 16) && (dn.sse * 2) % 16 == 0;
   dn.rot = ((up_index + 1) * 37) % kb::current_sms();
   dn.done = kb::add_sync(pr, 1);
   dn.items_done = kb::add_sync(pr, 1);
