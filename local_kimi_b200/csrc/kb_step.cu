@@ -808,96 +808,123 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
   if (o < P.nops && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
 }
 
+// A dense operation of one problem whose rows are split into reduction
+// chunks (one stage each): the consumers stage the activations chunk by chunk.
+__device__ void run_dense_chunked(const StepParams& P, const StOp& op, StPlan* pl, Ring& R,
+                                  uint8_t* xs, Partials& pa) {
+  const int g = (threadIdx.x & 31) >> 2;
+  const int G = gridDim.x;
+  const StDense& D = op.p[0];
+  const int n = D.items;
+  for (int i = first_item(op.rot); i < n; i += G) {
+    Item it;
+    st_describe_dense(op, i, it);
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    Split sp;
+    // Reduction chunks of kc columns: each stage holds kc/2 bytes of every
+    // row; the activations of the chunk are staged in a chunk-local layout
+    // and the chunk is contracted as a problem of width kc.
+    const int kc = D.K / D.nchunk;
+    const int tsc = token_stride(kc);
+    const int gpc = kc >> (5 + D.gshift);  // scale groups per chunk
+    Item ic = it;
+    ic.K = kc;
+    const uint8_t* xrow[1] = {xs + min(g, op.T - 1) * tsc};
+    const int crot = (i / G) & (D.KS - 1);
+    for (int ci = 0; ci < D.nchunk; ++ci) {
+      named_barrier(CBAR, NCT);
+      for (int m = 0; m < op.T; ++m)
+        stage_row_cg(xs + m * tsc, D.x + (size_t)m * D.xs + (size_t)ci * kc, kc, threadIdx.x,
+                     NCT);
+      named_barrier(CBAR, NCT);
+      int st;
+      const uint8_t* stage = consume_stage(P, R, pl, &st);
+      sp = split_of(ic, stage, crot);
+      sp.srow += ci * gpc;
+      split_compute(ic, sp, sp.wtile, 0, (kc + 127) >> 7, xrow, acc);
+      release_stage(R, st);
+    }
+    partial_publish(P, pa, pl, sp.slot, op.T, acc);
+  }
+}
+
 __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
                           Partials& pa) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
   const int warp = threadIdx.x >> 5;
-  const int f = first_item(op.rot);
-  for (int p = 0; p < op.nprob; ++p) {
-    const StDense& D = op.p[p];
-    // This CTA's items of problem p: i = f (mod G) within the problem's range.
-    const int ib = D.item_begin, ie = D.item_begin + D.items;
-    int i = ib + ((f - ib) % G + G) % G;
-    if (D.nchunk == 1) {
-      // Per-problem constants of this warp's part of an item.
-      const int K = D.K, N = D.N, RBc = D.RBc, KS = D.KS, mats = D.mats;
-      const int ng = K >> (5 + D.gshift);
+  const int nprob = op.nprob;
+  const int n = op.p[nprob - 1].item_begin + op.p[nprob - 1].items;
+  if (op.p[0].nchunk > 1) {
+    run_dense_chunked(P, op, pl, R, xs, pa);
+    return;
+  }
+  // This warp's part of an item of the current problem (reloaded when the
+  // item sequence i = first, first + G, ... enters another problem).  KS and
+  // RBc are powers of two.
+  int p = -1, pend = 0, ib = 0;
+  int K = 0, N = 0, gshift = 0, ng = 0, KB = 0, KS = 1, kslog = 0, item_rows = 0;
+  int rb = 0, ks = 0, pslot_base = 0, wt_off = 0, sc_off = 0;
+  bool base_ok = false;
+  const uint16_t* sglob = nullptr;
+  const uint8_t* xrow0 = xs;
+  int rot = 0;  // reduction slice of this warp = (ks + rot) % KS, rot advancing per item
+  for (int i = first_item(op.rot); i < n; i += G) {
+    if (i >= pend) {
+      do {
+        ++p;
+        pend = op.p[p].item_begin + op.p[p].items;
+      } while (i >= pend);
+      const StDense& D = op.p[p];
+      ib = D.item_begin;
+      K = D.K;
+      N = D.N;
+      gshift = D.gshift;
+      ng = K >> (5 + gshift);
+      KB = K >> 7;
+      KS = D.KS;
+      kslog = __ffs(KS) - 1;
+      item_rows = D.RBc * 16;
+      const int mats = D.mats;
+      const int pmlog = kslog + __ffs(D.RBc) - 1;  // log2(RBc * KS)
+      const int mat = warp >> pmlog;
+      const int rem = warp - (mat << pmlog);
+      rb = rem >> kslog;
+      ks = rem & (KS - 1);
+      pslot_base = (mat << pmlog) + (rb << kslog);
       const int RS = K >> 1;
-      const int per_mat = RBc * KS;
-      const int mat = warp / per_mat;
-      const int rem = warp - mat * per_mat;
-      const int rb = rem / KS, ks = rem - rb * KS;
-      const int KB = K >> 7;
-      int rot = 0;  // reduction slice of this warp = (ks + rot) % KS, rot advancing per item
-      const int item_rows = RBc * 16;
-      const int wt_off = (mat * item_rows + rb * 16) * RS;
-      const int sc_off = mats * item_rows * RS;
-      const int sc_stride = (item_rows * ng * 2 + 15) / 16 * 16;
-      const uint16_t* sglob = mat ? D.s3 : D.s;
-      const uint8_t* xrow[1] = {xs + D.x_off + min(g, op.T - 1) * token_stride(K)};
-      const bool base_ok = (reinterpret_cast<uintptr_t>(D.s) % 16 == 0) &&
-                           (mats == 1 || reinterpret_cast<uintptr_t>(D.s3) % 16 == 0);
-      for (; i < ie; i += G) {
-        const int r0 = (i - ib) * item_rows;
-        const int rows = min(item_rows, N - r0);
-        const int rb_rows = min(16, rows - rb * 16);
-        int st;
-        const uint8_t* stage = consume_stage(P, R, pl, &st);
-        const bool bulk = base_ok && ((rows * ng * 2) % 16 == 0);
-        const uint16_t* srow =
-            bulk ? reinterpret_cast<const uint16_t*>(stage + sc_off + mat * sc_stride) +
-                       rb * 16 * ng
-                 : sglob + (size_t)(r0 + rb * 16) * ng;
-        // Slices of unequal length rotate over the warps from item to item, so
-        // the ring's slack evens the load out.
-        const int ksr = (ks + rot) & (KS - 1);
-        rot = (rot + 1) & (KS - 1);
-        const int kb0 = KB * ksr / KS, kb1 = KB * (ksr + 1) / KS;
-        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        if (rb_rows > 0 && kb1 > kb0) {
-          if (bulk)
-            rowblock_compute<1, true>(stage + wt_off, RS, srow, ng, rb_rows, K, D.gshift, kb0,
-                                      kb1, xrow, 1, acc);
-          else
-            rowblock_compute<1>(stage + wt_off, RS, srow, ng, rb_rows, K, D.gshift, kb0, kb1,
-                                xrow, 1, acc);
-        }
-        release_stage(R, st);
-        partial_publish(P, pa, pl, mat * per_mat + rb * KS + ksr, op.T, acc);
-      }
-      continue;
+      wt_off = (mat * item_rows + rb * 16) * RS;
+      sc_off = mats * item_rows * RS + mat * ((item_rows * ng * 2 + 15) / 16 * 16) +
+               rb * 16 * ng * 2;
+      sglob = mat ? D.s3 : D.s;
+      xrow0 = xs + D.x_off + min(g, op.T - 1) * token_stride(K);
+      base_ok = (reinterpret_cast<uintptr_t>(D.s) % 16 == 0) &&
+                (mats == 1 || reinterpret_cast<uintptr_t>(D.s3) % 16 == 0);
     }
-    for (; i < ie; i += G) {
-      Item it;
-      st_describe_dense(op, i, it);
-      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-      Split sp;
-      // Reduction chunks of kc columns: each stage holds kc/2 bytes of every
-      // row; the activations of the chunk are staged in a chunk-local layout
-      // and the chunk is contracted as a problem of width kc.
-      const int kc = D.K / D.nchunk;
-      const int tsc = token_stride(kc);
-      const int gpc = kc >> (5 + D.gshift);  // scale groups per chunk
-      Item ic = it;
-      ic.K = kc;
-      const uint8_t* xrow[1] = {xs + min(g, op.T - 1) * tsc};
-      const int crot = (i / G) & (D.KS - 1);
-      for (int ci = 0; ci < D.nchunk; ++ci) {
-        named_barrier(CBAR, NCT);
-        for (int m = 0; m < op.T; ++m)
-          stage_row_cg(xs + m * tsc, D.x + (size_t)m * D.xs + (size_t)ci * kc, kc, threadIdx.x,
-                       NCT);
-        named_barrier(CBAR, NCT);
-        int st;
-        const uint8_t* stage = consume_stage(P, R, pl, &st);
-        sp = split_of(ic, stage, crot);
-        sp.srow += ci * gpc;
-        split_compute(ic, sp, sp.wtile, 0, (kc + 127) >> 7, xrow, acc);
-        release_stage(R, st);
-      }
-      partial_publish(P, pa, pl, sp.slot, op.T, acc);
+    const int r0 = (i - ib) * item_rows;
+    const int rows = min(item_rows, N - r0);
+    const int rb_rows = min(16, rows - rb * 16);
+    const bool bulk = base_ok && ((rows * ng * 2) % 16 == 0);
+    // Slices of unequal length rotate over the warps from item to item, so
+    // the ring's slack evens the load out.
+    const int ksr = (ks + rot) & (KS - 1);
+    rot = (rot + 1) & (KS - 1);
+    const int kb0 = (KB * ksr) >> kslog, kb1 = (KB * (ksr + 1)) >> kslog;
+    const uint8_t* xrow[1] = {xrow0};
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    int st;
+    const uint8_t* stage = consume_stage(P, R, pl, &st);
+    if (rb_rows > 0 && kb1 > kb0) {
+      if (bulk)
+        rowblock_compute<1, true>(stage + wt_off, K >> 1,
+                                  reinterpret_cast<const uint16_t*>(stage + sc_off), ng,
+                                  rb_rows, K, gshift, kb0, kb1, xrow, 1, acc);
+      else
+        rowblock_compute<1>(stage + wt_off, K >> 1, sglob + (size_t)(r0 + rb * 16) * ng, ng,
+                            rb_rows, K, gshift, kb0, kb1, xrow, 1, acc);
     }
+    release_stage(R, st);
+    partial_publish(P, pa, pl, pslot_base + ksr, op.T, acc);
   }
 }
 
@@ -1568,25 +1595,44 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
     const StOp& op = P.ops[o];
     if (o > 0 && lane == 0) trace_mark(P, o - 1, 5);
     if (op.type == OP_DENSE) {
-      const int f = first_item(op.rot);
       const int T = op.T, nprob = op.nprob;
+      const int n = op.p[nprob - 1].item_begin + op.p[nprob - 1].items;
       int blocks = 0;
-      for (int p = 0; p < nprob && ok; ++p) {
-        const StDense& Dg = op.p[p];
-        const int ib = Dg.item_begin, ie = Dg.item_begin + Dg.items;
-        const int RBc = Dg.RBc, KS = Dg.KS, N = Dg.N;
-        const bool pair = Dg.mats == 2;
-        uint16_t* const y = Dg.y;
-        const int64_t ys = Dg.ys;
-        const int item_rows = RBc * 16;
-        for (int i = ib + ((f - ib) % G + G) % G; i < ie; i += G) {
-          if (!partial_take(pa, pl)) {
-            ok = false;
-            break;
+      int p = -1, pend = 0, ib = 0, RBc = 1, KS = 1, N = 0, item_rows = 0;
+      bool pair = false;
+      uint16_t* y = nullptr;
+      int64_t ys = 0;
+      for (int i = first_item(op.rot); i < n && ok; i += G) {
+        if (i >= pend) {
+          do {
+            ++p;
+            pend = op.p[p].item_begin + op.p[p].items;
+          } while (i >= pend);
+          const StDense& Dg = op.p[p];
+          ib = Dg.item_begin;
+          RBc = Dg.RBc;
+          KS = Dg.KS;
+          N = Dg.N;
+          item_rows = RBc * 16;
+          pair = Dg.mats == 2;
+          y = Dg.y;
+          ys = Dg.ys;
+        }
+        if (!partial_take(pa, pl)) {
+          ok = false;
+          break;
+        }
+        const int r0 = (i - ib) * item_rows;
+        const int rows = min(item_rows, N - r0);
+        blocks += (rows + 15) >> 4;
+        if (T == 1) {
+          for (int r = lane; r < rows; r += 32) {
+            const float v0 = partial_sum(pa, 0, RBc, KS, r >> 4, r & 15, 0);
+            const float val =
+                pair ? swiglu_contract(v0, partial_sum(pa, 1, RBc, KS, r >> 4, r & 15, 0)) : v0;
+            y[r0 + r] = float_to_bf16_bits(val);
           }
-          const int r0 = (i - ib) * item_rows;
-          const int rows = min(item_rows, N - r0);
-          blocks += (rows + 15) >> 4;
+        } else {
           for (int idx = lane; idx < rows * T; idx += 32) {
             const int r = idx / T, tok = idx - r * T;
             const float v0 = partial_sum(pa, 0, RBc, KS, r >> 4, r & 15, tok);
@@ -1594,8 +1640,8 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
                 pair ? swiglu_contract(v0, partial_sum(pa, 1, RBc, KS, r >> 4, r & 15, tok)) : v0;
             y[(size_t)tok * ys + r0 + r] = float_to_bf16_bits(val);
           }
-          partial_release(pa);
         }
+        partial_release(pa);
       }
       __syncwarp();
       if (lane == 0 && blocks > 0) red_release(&P.sync[op.done], blocks);
