@@ -89,6 +89,7 @@ struct StOp {
   int rot;     // item i runs on CTA (i + rot) % grid
   int T;
   int items;   // static items (dense, router, KDA)
+  int cstage;  // dense/router: the consumers stage the activations (input of the previous operation)
   // dense
   int nprob;
   StDense p[ST_MAX_PROB];
@@ -738,7 +739,9 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
     }
     if (!ok) break;
     uint8_t* xs = X.base + (size_t)b * X.x_bytes;
-    if (op.type == OP_DENSE) {
+    if (op.cstage) {
+      // Staged by the consumers, which are waiting for this input anyway.
+    } else if (op.type == OP_DENSE) {
       for (int p = 0; p < op.nprob; ++p) {
         const StDense& D = op.p[p];
         if (D.nchunk > 1) continue;  // staged chunk by chunk by the consumers
@@ -754,15 +757,7 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
       for (int m = 0; m < op.T; ++m) {
         const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
         uint4* d4 = reinterpret_cast<uint4*>(xs + (size_t)m * op.K * 2);
-        for (int w0 = lane; w0 < words; w0 += 8 * 32) {
-          uint4 v[8];
-#pragma unroll
-          for (int b = 0; b < 8; ++b)
-            if (w0 + 32 * b < words) v[b] = __ldcg(s4 + w0 + 32 * b);
-#pragma unroll
-          for (int b = 0; b < 8; ++b)
-            if (w0 + 32 * b < words) d4[w0 + 32 * b] = v[b];
-        }
+        for (int w = lane; w < words; w += 32) d4[w] = __ldcg(s4 + w);
       }
     } else if (op.type == OP_MOE_UP) {
       const int ts = token_stride(op.K);
@@ -806,6 +801,32 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
   }
   // A wait that gave up ends the launch (the consumers' waits are bounded too).
   if (o < P.nops && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
+}
+
+// Activations of a dense or router operation whose input comes from the
+// operation just before it: staged by all consumer threads (one L2 round
+// trip) once the stager has seen the input complete.
+__device__ void consumer_stage(const StOp& op, uint8_t* xs) {
+  if (op.type == OP_DENSE) {
+    for (int p = 0; p < op.nprob; ++p) {
+      const StDense& D = op.p[p];
+      if (D.nchunk > 1) continue;  // staged chunk by chunk
+      bool dup = false;
+      for (int q = 0; q < p; ++q) dup |= (op.p[q].x_off == D.x_off);
+      if (dup) continue;
+      const int ts = token_stride(D.K);
+      for (int m = 0; m < op.T; ++m)
+        stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+    }
+  } else {
+    const int words = op.K >> 3;
+    for (int m = 0; m < op.T; ++m) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
+      uint4* d4 = reinterpret_cast<uint4*>(xs + (size_t)m * op.K * 2);
+      for (int w = threadIdx.x; w < words; w += NCT) d4[w] = __ldcg(s4 + w);
+    }
+  }
+  named_barrier(CBAR, NCT);
 }
 
 // A dense operation of one problem whose rows are split into reduction
@@ -1783,6 +1804,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     } else {
       consumer_op_wait(P, pl, &X.ready[xb], xph);
       const StOp& op = X.desc[xb];
+      if (op.cstage) consumer_stage(op, xs);
       switch (type) {
         case OP_DENSE:
           run_dense(P, op, pl, R, xs, pa);
@@ -2243,6 +2265,12 @@ int kb_step_finalize(kb_step* step) {
   int stage = 0, xbytes = 0, cum = 0, drow = 0;
   for (size_t o = 0; o < pr->ops.size(); ++o) {
     kb::StOp& op = pr->ops[o];
+    // Inputs produced by the operation just before are staged by the
+    // consumers (they wait for them in any case); others by the stager,
+    // ahead of the consumers.
+    op.cstage = 0;
+    if (op.type == kb::OP_DENSE || op.type == kb::OP_ROUTER)
+      for (int d = 0; d < op.ndeps; ++d) op.cstage |= (op.dep[d] == (int)o - 1);
     switch (op.type) {
       case kb::OP_DENSE: {
         op.rot = cum % G;
