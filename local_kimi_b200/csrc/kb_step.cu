@@ -78,6 +78,7 @@ struct StDense {
   int64_t ys;
   int K, N, gshift, KS, RBc, nchunk, mats;
   int items, item_begin, x_off;
+  int xcomb;  // x is the output of the down operation just before: staged as its combine
 };
 
 struct StOp {
@@ -90,6 +91,7 @@ struct StOp {
   int T;
   int items;   // static items (dense, router, KDA)
   int cstage;  // dense/router: the consumers stage the activations (input of the previous operation)
+  int comb_src;  // dense: down operation whose combine the consumers compute while staging, or -1
   // dense
   int nprob;
   StDense p[ST_MAX_PROB];
@@ -287,6 +289,17 @@ __device__ __forceinline__ void stage_row_cg(uint8_t* xs_row, const uint16_t* sr
         *reinterpret_cast<uint4*>(xs_row + ((w & 3) * NC + (w >> 2)) * 16) = permute_pairs(v[b]);
     }
   }
+}
+
+// One combined value: bf16(sum_r routed_r * w_r, fp32 in route order) +
+// shared (engine/kernels/moe_combine.py:209-261).
+__device__ __forceinline__ uint16_t combine_value(const uint16_t (&rv)[ST_MAX_TOPK],
+                                                  const float* rw, int top_k, uint16_t sv) {
+  float accum = 0.f;
+#pragma unroll
+  for (int r = 0; r < ST_MAX_TOPK; ++r)
+    if (r < top_k) accum = fmaf(bf16_bits_to_float(rv[r]), rw[r], accum);
+  return float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
 }
 
 // ---------------------------------------------------------------------------
@@ -734,6 +747,7 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
     const StOp& op = *dst;
     bool ok = true;
     for (int d = 0; d < op.ndeps && ok; ++d) {
+      if (op.dep[d] == op.comb_src) continue;  // the consumers wait for its items
       const StOp& dop = P.ops[op.dep[d]];
       ok = stager_poll(P, pl, dop.done, dop.target);
     }
@@ -803,20 +817,84 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
   if (o < P.nops && lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
 }
 
+// Row of the combined output of a down operation (routes of one token at
+// wrows + r*N, r < R; weights rw) computed from the per-route outputs and
+// staged in the B-fragment layout: what staging the combine's output row
+// would give, without waiting for the combine.  Each lane combines one
+// 8-byte half of a 16-byte word (few registers: this runs inside the
+// consumer loop) and trades a pair of values with its neighbour lane, which
+// holds the other half.  first/step: a warp-aligned thread index and stride.
+__device__ __forceinline__ void stage_combined(uint8_t* xs_row, const uint16_t* wrows,
+                                               const float* rw, int top_k, int R, int N,
+                                               int first, int step) {
+  const int NC = N >> 5;
+  const int halves = N >> 2;
+  for (int h = first; h - (first & 31) < halves; h += step) {
+    const bool valid = h < halves;
+    const int part = h & 1, w = h >> 1;
+    uint2 v[ST_MAX_TOPK];
+#pragma unroll
+    for (int r = 0; r < ST_MAX_TOPK; ++r)
+      v[r] = (valid && r < top_k) ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)r * N) + h)
+                                  : make_uint2(0u, 0u);
+    const uint2 sv = valid ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)(R - 1) * N) + h)
+                           : make_uint2(0u, 0u);
+    uint32_t c[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint16_t lo[ST_MAX_TOPK], hi[ST_MAX_TOPK];
+#pragma unroll
+      for (int r = 0; r < ST_MAX_TOPK; ++r) {
+        const uint32_t x = q ? v[r].y : v[r].x;
+        lo[r] = (uint16_t)(x & 0xffffu);
+        hi[r] = (uint16_t)(x >> 16);
+      }
+      const uint32_t sx = q ? sv.y : sv.x;
+      c[q] = (uint32_t)combine_value(lo, rw, top_k, (uint16_t)(sx & 0xffffu)) |
+             ((uint32_t)combine_value(hi, rw, top_k, (uint16_t)(sx >> 16)) << 16);
+    }
+    // Half 0 holds elements 0-3 of the word, half 1 elements 4-7; the pair
+    // order (0,4),(1,5) | (2,6),(3,7) needs one value of the other half.
+    const uint32_t got = __shfl_xor_sync(0xffffffffu, part ? c[0] : c[1], 1);
+    if (valid) {
+      const uint32_t a = part ? got : c[0], b2 = part ? c[1] : got;
+      *reinterpret_cast<uint2*>(xs_row + ((w & 3) * NC + (w >> 2)) * 16 + part * 8) =
+          make_uint2(prmt(a, b2, 0x5410), prmt(a, b2, 0x7632));
+    }
+  }
+}
+
 // Activations of a dense or router operation whose input comes from the
 // operation just before it: staged by all consumer threads (one L2 round
 // trip) once the stager has seen the input complete.
-__device__ void consumer_stage(const StOp& op, uint8_t* xs) {
+__device__ void consumer_stage(const StepParams& P, StPlan* pl, const StOp& op, uint8_t* xs) {
   if (op.type == OP_DENSE) {
+    int comb_off = -1, comb_k = 0;
     for (int p = 0; p < op.nprob; ++p) {
       const StDense& D = op.p[p];
       if (D.nchunk > 1) continue;  // staged chunk by chunk
       bool dup = false;
       for (int q = 0; q < p; ++q) dup |= (op.p[q].x_off == D.x_off);
       if (dup) continue;
+      if (D.xcomb) {
+        comb_off = D.x_off;
+        comb_k = D.K;
+        continue;
+      }
       const int ts = token_stride(D.K);
       for (int m = 0; m < op.T; ++m)
         stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+    }
+    if (comb_off >= 0) {
+      // The down operation's per-route outputs are complete once all of its
+      // items are (the plan in shared memory is still this layer's).
+      const StOp& dop = P.ops[op.comb_src];
+      const int R = dop.R, N = dop.N;
+      consumers_wait(P, pl, dop.items_done, pl->nslots * dop.items_rb);
+      const int ts = token_stride(comb_k);
+      for (int m = 0; m < op.T; ++m)
+        stage_combined(xs + comb_off + m * ts, dop.wsy + (size_t)m * R * N,
+                       pl->route_w + m * (R - 1), R - 1, R, N, threadIdx.x, NCT);
     }
   } else {
     const int words = op.K >> 3;
@@ -1593,11 +1671,7 @@ __device__ bool combine_pairs(const StepParams& P, const MoeEpi& m, StPlan* pl, 
 #pragma unroll
         for (int r = 0; r < ST_MAX_TOPK; ++r) rv[r] = r < top_k ? __ldcg(ws + (size_t)r * N) : 0;
         const uint16_t sv = __ldcg(ws + (size_t)(R - 1) * N);
-        float accum = 0.f;
-#pragma unroll
-        for (int r = 0; r < ST_MAX_TOPK; ++r)
-          if (r < top_k) accum += bf16_bits_to_float(rv[r]) * rw[r];
-        out[(size_t)tok * N + row] = float_to_bf16_bits(round_bf16(accum) + bf16_bits_to_float(sv));
+        out[(size_t)tok * N + row] = combine_value(rv, rw, top_k, sv);
       }
     }
     combined += (p + G < npairs) ? 2 : 1;
@@ -1804,7 +1878,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     } else {
       consumer_op_wait(P, pl, &X.ready[xb], xph);
       const StOp& op = X.desc[xb];
-      if (op.cstage) consumer_stage(op, xs);
+      if (op.cstage) consumer_stage(P, pl, op, xs);
       switch (type) {
         case OP_DENSE:
           run_dense(P, op, pl, R, xs, pa);
@@ -2269,8 +2343,21 @@ int kb_step_finalize(kb_step* step) {
     // consumers (they wait for them in any case); others by the stager,
     // ahead of the consumers.
     op.cstage = 0;
+    op.comb_src = -1;
     if (op.type == kb::OP_DENSE || op.type == kb::OP_ROUTER)
       for (int d = 0; d < op.ndeps; ++d) op.cstage |= (op.dep[d] == (int)o - 1);
+    // An activation row that is the combine output of the down operation just
+    // before is computed from its per-route outputs by the consumers.
+    if (op.type == kb::OP_DENSE && op.cstage && o > 0 &&
+        pr->ops[o - 1].type == kb::OP_MOE_DOWN) {
+      const kb::StOp& dop = pr->ops[o - 1];
+      for (int i = 0; i < op.nprob; ++i) {
+        kb::StDense& D = op.p[i];
+        D.xcomb = D.nchunk == 1 && D.x == dop.out && D.xs == dop.N && D.K == dop.N &&
+                  dop.R - 1 <= kb::ST_MAX_TOPK;
+        if (D.xcomb) op.comb_src = (int)o - 1;
+      }
+    }
     switch (op.type) {
       case kb::OP_DENSE: {
         op.rot = cum % G;
