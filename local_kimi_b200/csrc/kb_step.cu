@@ -1465,7 +1465,6 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
   int* const done = &P.sync[op.done];
   const int nsl = (Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
   bool waited = false;
-  int units = 0;
   for (int u = first_item(op.rot); u < items; u += G) {
     const int bh = u / nsl, sl = u - bh * nsl;
     const int b = bh / H, h = bh - b * H;
@@ -1524,27 +1523,31 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
         }
       }
       kd->red[warp][lane] = opart;
-      if (col_ok) {
+    }
+    named_barrier(CBAR, NCT);
+    if (warp == 0) {
+      if (sl * ST_KDA_COLS + lane < Dv) {
+        float o = 0.f;
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          const int i = r * KW + warp;
-          if (i < Dk) base[(size_t)i * sk] = c[r];
-        }
+        for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
+        if (kout) kout[(size_t)bh * Dv + col] = o;
+        if (kout16) kout16[(size_t)bh * Dv + col] = float_to_bf16_bits(o);
+      }
+      // The outputs are published before the state is written back: only
+      // the next launch reads the state, so its stores need not complete
+      // before the signal.
+      warp_signal(done, 1);
+    }
+    if (worker && col_ok) {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = r * KW + warp;
+        if (i < Dk) base[(size_t)i * sk] = c[r];
       }
     }
     named_barrier(CBAR, NCT);
-    if (warp == 0 && sl * ST_KDA_COLS + lane < Dv) {
-      float o = 0.f;
-#pragma unroll
-      for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
-      if (kout) kout[(size_t)bh * Dv + col] = o;
-      if (kout16) kout16[(size_t)bh * Dv + col] = float_to_bf16_bits(o);
-    }
-    ++units;
-    named_barrier(CBAR, NCT);
   }
   if (!waited) consumer_op_wait(P, pl, xready, xphase);
-  if (threadIdx.x == 0 && units > 0) red_release(done, units);
 }
 
 // ---------------------------------------------------------------------------
