@@ -163,6 +163,13 @@ struct StPlan {
   int slot_id[ST_MAX_T * ST_MAX_TOPK];
   int slot_of[ST_MAX_E + 1];
   int nslots;
+  // Selection scratch, two tokens at a time: 8 candidates per warp of 32
+  // experts (choice key, expert, logit), then the picks in choice order.
+  uint32_t cand_k[2][64];
+  int cand_e[2][64];
+  float cand_l[2][64];
+  int pick_e[2][ST_MAX_TOPK];
+  float pick_l[2][ST_MAX_TOPK];
   int done_tok[ST_MAX_T];
   int abort;
   int last;
@@ -1111,86 +1118,125 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
   if (threadIdx.x == 0 && experts > 0) red_release(done, experts);
 }
 
-// Polls the router words of token row `row` until every one of its E <= 256
-// experts is written (bounded), keeping key[j], lg[j] of expert lane + 32 j.
-// Returns false when the wait ended without them.
-__device__ bool poll_router_words(const StepParams& P, StPlan* pl,
-                                  const unsigned long long* row, int E, uint32_t (&key)[8],
-                                  float (&lg)[8]) {
-  const int lane = threadIdx.x & 31;
-  unsigned need = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    key[j] = 0u;
-    lg[j] = 0.f;
-    if (lane + 32 * j < E) need |= 1u << j;
-  }
-  unsigned have = 0;
+// Waits (bounded) until a router word is written and returns it; zero when
+// the wait gave up (then the launch is aborting).
+__device__ unsigned long long poll_router_word(const StepParams& P, StPlan* pl,
+                                               const unsigned long long* word) {
+  unsigned long long w = ld_relaxed_u64(word);
+  if ((w >> 32) != 0ull) return w;
   const long long t0 = now_ns();
-  for (int spins = 0;; ++spins) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if ((need & ~have) & (1u << j)) {
-        const unsigned long long w = ld_relaxed_u64(row + lane + 32 * j);
-        if ((w >> 32) != 0ull) {
-          key[j] = (uint32_t)(w >> 32) - 1u;
-          lg[j] = __uint_as_float((uint32_t)w);
-          have |= 1u << j;
-        }
-      }
-    }
-    if (__all_sync(0xffffffffu, have == need)) return true;
+  for (int spins = 1;; ++spins) {
     __nanosleep(32);
-    if ((spins & 15) == 15) {
-      int stop = 0;
-      if (lane == 0) {
-        if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
-          pl->abort = 1;
-          stop = 1;
-        } else if (now_ns() - t0 > ST_WAIT_NS) {
-          raise_abort(P, pl, ERR_TIMEOUT);
-          stop = 1;
-        }
+    w = ld_relaxed_u64(word);
+    if ((w >> 32) != 0ull) return w;
+    if ((spins & 15) == 0) {
+      if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
+        pl->abort = 1;
+        return 0ull;
       }
-      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+      if (now_ns() - t0 > ST_WAIT_NS) {
+        raise_abort(P, pl, ERR_TIMEOUT);
+        return 0ull;
+      }
     }
   }
 }
 
-// Top-k for every token (warp per token) and the expert plan (warp 0), in
-// every CTA from the same router words, so every CTA holds the same plan.
-// The words are read as soon as the router has written them (no completion
-// counter between).  Slot 0 is the shared expert (bank slot E, every token,
-// route R-1); routed experts follow in order of first use (token-major, then
-// route order).  Indices are always in [0, E), whatever the words hold.
+// (key, expert) a precedes (key, expert) b in choice order: larger key, then
+// lower expert index.
+__device__ __forceinline__ bool choice_before(uint32_t ka, int ea, uint32_t kb, int eb) {
+  return ka > kb || (ka == kb && ea < eb);
+}
+
+// Top-k of every token and the expert plan (warp 0), in every CTA from the
+// same router words, so every CTA holds the same plan.  The words are read as
+// soon as the router has written them (no completion counter between).  Two
+// tokens at a time, 256 consumer threads per token, one expert each: every
+// warp ranks its 32 experts with shuffles and keeps its best 8 (a superset
+// of the token's top-k among them), then 64 threads rank those 64
+// candidates.  The picks come out in choice order (largest choice key, ties
+// to the lower index), the order of the per-operation router.  Slot 0 is the
+// shared expert (bank slot E, every token, route R-1); routed experts follow
+// in order of first use (token-major, then route order).  Indices are always
+// in [0, E), whatever the words hold.
 __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const StOp& rop = P.ops[up.router_op];
   const int T = up.T, R = up.R, top_k = rop.top_k, E = rop.E;
   const unsigned long long* words = rop.rwords + (size_t)pl->parity * T * E;
-  for (int t = warp; t < T; t += NCW) {
-    uint32_t key[8];
-    float lg[8];
-    poll_router_words(P, pl, words + (size_t)t * E, E, key, lg);
-    if (t == 0 && lane == 0) trace_mark(P, pl->cur_op, 7);
-    int my_idx = 0;
-    float my_score = 0.f, wsum = 0.f;
-    warp_topk256_regs(key, lg, top_k, lane, my_idx, my_score, wsum);
-    my_idx = min(max(my_idx, 0), E - 1);
-    if (lane < top_k) {
-      float wv = my_score;
-      if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
-      wv *= rop.scaling;
-      pl->route_e[t * R + lane] = my_idx;
-      pl->route_w[t * top_k + lane] = wv;
-      if (blockIdx.x == 0) {
-        rop.idx_out[(size_t)t * (top_k + 1) + lane] = my_idx;
-        rop.w_out[(size_t)t * top_k + lane] = wv;
+  const int half = threadIdx.x >> 8;        // token t0 + half
+  const int e = threadIdx.x & 255;          // expert of this thread
+  const int w8 = warp & 7;                  // warp within the token's eight
+  for (int t0 = 0; t0 < T; t0 += 2) {
+    const int t = t0 + half;
+    const bool valid = t < T && e < E;
+    uint32_t key = 0u;
+    float lg = 0.f;
+    if (valid) {
+      const unsigned long long w = poll_router_word(P, pl, words + (size_t)t * E + e);
+      key = (uint32_t)(w >> 32) - 1u;
+      lg = __uint_as_float((uint32_t)w);
+    }
+    if (t0 == 0 && threadIdx.x == 0) trace_mark(P, pl->cur_op, 7);
+    // Rank among the warp's valid experts (lane order = index order).
+    int rank = 0;
+#pragma unroll
+    for (int sl = 0; sl < 32; ++sl) {
+      const uint32_t ks = __shfl_sync(0xffffffffu, key, sl);
+      const bool vs = __shfl_sync(0xffffffffu, valid, sl);
+      rank += (vs && (ks > key || (ks == key && sl < lane))) ? 1 : 0;
+    }
+    if (lane < 8) pl->cand_e[half][w8 * 8 + lane] = 0x7fffffff;  // empty candidate slot
+    __syncwarp();
+    if (valid && rank < 8) {
+      pl->cand_k[half][w8 * 8 + rank] = key;
+      pl->cand_e[half][w8 * 8 + rank] = e;
+      pl->cand_l[half][w8 * 8 + rank] = lg;
+    }
+    named_barrier(CBAR, NCT);
+    if (e < 64 && t < T) {
+      const int ec = pl->cand_e[half][e];
+      if (ec < E) {
+        const uint32_t kc = pl->cand_k[half][e];
+        int r2 = 0;
+        for (int j = 0; j < 64; ++j) {
+          const int ej = pl->cand_e[half][j];
+          r2 += (ej < E && choice_before(pl->cand_k[half][j], ej, kc, ec)) ? 1 : 0;
+        }
+        if (r2 < top_k) {
+          pl->pick_e[half][r2] = ec;
+          pl->pick_l[half][r2] = pl->cand_l[half][e];
+        }
       }
     }
-    if (lane == 0) {
-      pl->route_e[t * R + R - 1] = E;
-      if (blockIdx.x == 0) rop.idx_out[(size_t)t * (top_k + 1) + top_k] = E;
+    named_barrier(CBAR, NCT);
+    // Weights of token t0 + warp (warps 0 and 1): unbiased sigmoid scores,
+    // renormalised in pick order, scaled.
+    if (warp < 2 && t0 + warp < T) {
+      const int tt = t0 + warp;
+      float sc = 0.f;
+      int my_idx = 0;
+      if (lane < top_k) {
+        my_idx = min(max(pl->pick_e[warp][lane], 0), E - 1);
+        sc = 1.0f / (1.0f + expf(-pl->pick_l[warp][lane]));
+      }
+      float wsum = 0.f;
+      for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, sc, r);
+      if (lane < top_k) {
+        float wv = sc;
+        if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
+        wv *= rop.scaling;
+        pl->route_e[tt * R + lane] = my_idx;
+        pl->route_w[tt * top_k + lane] = wv;
+        if (blockIdx.x == 0) {
+          rop.idx_out[(size_t)tt * (top_k + 1) + lane] = my_idx;
+          rop.w_out[(size_t)tt * top_k + lane] = wv;
+        }
+      }
+      if (lane == 0) {
+        pl->route_e[tt * R + R - 1] = E;
+        if (blockIdx.x == 0) rop.idx_out[(size_t)tt * (top_k + 1) + top_k] = E;
+      }
     }
   }
   named_barrier(CBAR, NCT);

@@ -154,54 +154,4 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   return v;
 }
 
-// Top-k of one token from the keys and logits of its E <= 256 experts held
-// in registers (expert lane + 32 j in key[j], lg[j]); one warp.  Same
-// selection as warp_topk256 (largest key, lowest index among equal keys):
-// per pick, a warp max-reduction of the lane maxima, then the lowest index
-// among the holders.  Lane r < top_k receives the r-th pick, its sigmoid
-// score and the sum of the picked scores in pick order.  Keys are consumed.
-__device__ __forceinline__ void warp_topk256_regs(uint32_t (&key)[8], const float (&lg)[8],
-                                                  int top_k, int lane, int& my_idx,
-                                                  float& my_score, float& wsum) {
-  int pick_idx = 0;
-  float pick_logit = 0.f;
-  for (int sel = 0; sel < top_k; ++sel) {
-    uint32_t lm = key[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) lm = max(lm, key[j]);
-    const uint32_t best = __reduce_max_sync(0xffffffffu, lm);
-    int jb = 8;
-#pragma unroll
-    for (int j = 7; j >= 0; --j)
-      if (key[j] == best) jb = j;
-    const int cand = (jb < 8) ? lane + 32 * jb : 0x7fffffff;
-    const unsigned holders = __ballot_sync(0xffffffffu, jb < 8);
-    int win;
-    if ((holders & (holders - 1u)) == 0u)
-      win = __shfl_sync(0xffffffffu, cand, __ffs(holders) - 1);
-    else
-      win = (int)__reduce_min_sync(0xffffffffu, (uint32_t)cand);
-    float wl = 0.f;
-    if ((win & 31) == lane) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j == (win >> 5)) {
-          key[j] = 0u;
-          wl = lg[j];
-        }
-    }
-    const float l = __shfl_sync(0xffffffffu, wl, win & 31);
-    if (lane == sel) {
-      pick_idx = win;
-      pick_logit = l;
-    }
-  }
-  float s = 0.f;
-  if (lane < top_k) s = 1.0f / (1.0f + expf(-pick_logit));
-  wsum = 0.f;
-  for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, s, r);
-  my_idx = pick_idx;
-  my_score = s;
-}
-
 }  // namespace kb
