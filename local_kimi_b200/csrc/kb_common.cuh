@@ -89,12 +89,7 @@ __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) {
 }
 
 __device__ __forceinline__ uint4 lds_v4(const void* p) {
-  uint4 v;
-  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(a));
-  return v;
+  return *reinterpret_cast<const uint4*>(p);
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -254,9 +249,7 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 }
 
 __device__ __forceinline__ uint16_t lds_u16(const void* p) {
-  uint16_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(smem_addr(p)));
-  return v;
+  return *reinterpret_cast<const uint16_t*>(p);
 }
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {

@@ -1052,9 +1052,12 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
   // only release the stages.
   int experts = 0;
   for (int i = first_item(op.rot); i < items; i += G) {
+    const int e = i * ST_RT_EXPERTS + warp;
+    // The bias is read from memory; its load goes out before the stage wait
+    // and the dot product, which hide its latency.
+    const float be = (rbias && warp < ST_RT_EXPERTS && e < E) ? __ldg(rbias + e) : 0.f;
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
-    const int e = i * ST_RT_EXPERTS + warp;
     if (warp < ST_RT_EXPERTS && e < E) {
       float acc[ST_MAX_T][4];
 #pragma unroll
@@ -1066,16 +1069,11 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
       if (T == 1) {
         // One token: a branch-free loop (the per-token conditions of the
         // general loop below keep the compiler from overlapping iterations).
-        for (int w = lane; w < words; w += 32, wa += 512, ha += 512) {
-          uint4 wv, hv;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
-                       : "r"(wa));
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
-                       : "r"(ha));
-          router_word_fma(wv, hv, acc[0]);
-        }
+        const uint4* wp = reinterpret_cast<const uint4*>(stage + warp * K * 2) + lane;
+        const uint4* hp = reinterpret_cast<const uint4*>(xs) + lane;
+#pragma unroll 3
+        for (int w = lane; w < words; w += 32, wp += 32, hp += 32)
+          router_word_fma(*wp, *hp, acc[0]);
       } else {
         for (int w = lane; w < words; w += 32, wa += 512, ha += 512) {
           uint4 wv;
@@ -1096,7 +1094,6 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
       }
       // Lane m publishes token m's word: the choice key of sigmoid + bias
       // (plus one, so that zero means "not written") and the logit.
-      const float be = rbias ? __ldg(rbias + e) : 0.f;
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m) {
         if (m < T) {
