@@ -120,7 +120,10 @@ __device__ __forceinline__ void kblock_mma(uint4 WA, uint4 WB, uint32_t sa2, uin
 // D fragment: acc[p][0] = (row g, token 2t), [1] = (row g, token 2t+1),
 // [2] = (row g+8, token 2t), [3] = (row g+8, token 2t+1).
 // SMEM_SCALES: srow is known to point into shared memory (explicit shared loads).
-template <int NSUB, bool SMEM_SCALES = false>
+// COMPACT: the reduction width is a multiple of 128 (no partial block) and the
+// loop is not unrolled -- the decode-step executor runs many operations in one
+// kernel, where instruction-cache footprint costs more than the unrolling gains.
+template <int NSUB, bool SMEM_SCALES = false, bool COMPACT = false>
 __device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
                                                  const uint16_t* srow, int ng, int rows_valid,
                                                  int K, int gshift, int kb0, int kb1,
@@ -147,7 +150,7 @@ __device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
   const uint8_t* px[NSUB];
 #pragma unroll
   for (int p = 0; p < NSUB; ++p) px[p] = xrow[p] + c * 16;
-#pragma unroll 2
+#pragma unroll(COMPACT ? 1 : 2)
   for (int kb = kb0; kb < kbf; ++kb) {
     const uint4 WA = lds_v4(pa);
     const uint4 WB = lds_v4(pb);
@@ -161,7 +164,7 @@ __device__ __forceinline__ void rowblock_compute(const uint8_t* wtile, int RS,
 #pragma unroll
     for (int p = 0; p < NSUB; ++p) px[p] += 64;
   }
-  if (kbf < kb1) {
+  if (!COMPACT && kbf < kb1) {
     // Partial block: chunks at or past NC contribute zero weights.
     const bool valid = c < NC;
     const int cc = valid ? c : NC - 1;

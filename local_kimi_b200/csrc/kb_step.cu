@@ -564,10 +564,10 @@ __device__ __forceinline__ void split_compute(const Item& it, const Split& sp,
   const int kb0 = kb_lo + n * sp.ks / it.KS, kb1 = kb_lo + n * (sp.ks + 1) / it.KS;
   if (sp.rb_rows > 0 && kb1 > kb0) {
     if (it.scale_bulk)  // scales staged with the weights: explicit shared loads
-      rowblock_compute<1, true>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0,
+      rowblock_compute<1, true, true>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0,
                                 kb1, xrow, 1, acc);
     else
-      rowblock_compute<1>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0, kb1,
+      rowblock_compute<1, false, true>(wtile, it.RS, sp.srow, it.ng, sp.rb_rows, it.K, it.gshift, kb0, kb1,
                           xrow, 1, acc);
   }
 }
@@ -1022,11 +1022,11 @@ __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring&
     const uint8_t* stage = consume_stage(P, R, pl, &st);
     if (rb_rows > 0 && kb1 > kb0) {
       if (bulk)
-        rowblock_compute<1, true>(stage + wt_off, K >> 1,
+        rowblock_compute<1, true, true>(stage + wt_off, K >> 1,
                                   reinterpret_cast<const uint16_t*>(stage + sc_off), ng,
                                   rb_rows, K, gshift, kb0, kb1, xrow, 1, acc);
       else
-        rowblock_compute<1>(stage + wt_off, K >> 1, sglob + (size_t)(r0 + rb * 16) * ng, ng,
+        rowblock_compute<1, false, true>(stage + wt_off, K >> 1, sglob + (size_t)(r0 + rb * 16) * ng, ng,
                             rb_rows, K, gshift, kb0, kb1, xrow, 1, acc);
     }
     release_stage(R, st);
@@ -1394,11 +1394,11 @@ __device__ __forceinline__ void expert_item(const StepParams& P, const ExpertWar
   const uint8_t* stage = consume_stage(P, R, pl, &st);
   if (rb_rows > 0 && kb1 > kb0) {
     if (bulk)
-      rowblock_compute<1, true>(stage + w.wt_off, w.K >> 1,
+      rowblock_compute<1, true, true>(stage + w.wt_off, w.K >> 1,
                                 reinterpret_cast<const uint16_t*>(stage + w.sc_off), w.ng,
                                 rb_rows, w.K, w.gshift, kb0, kb1, xrow, 1, acc);
     else
-      rowblock_compute<1>(stage + w.wt_off, w.K >> 1,
+      rowblock_compute<1, false, true>(stage + w.wt_off, w.K >> 1,
                           w.s + (size_t)e * w.sse + (size_t)(r0 + w.rb * 16) * w.ng, w.ng,
                           rb_rows, w.K, w.gshift, kb0, kb1, xrow, 1, acc);
   }
