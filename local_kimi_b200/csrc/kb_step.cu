@@ -62,10 +62,12 @@ constexpr long long ST_WAIT_NS = 2000000000LL;  // 2 s per wait
 // routing built (expert blocks), end; producer done issuing; reducer done;
 // shared-expert items done (expert gate/up); spare.
 constexpr int ST_TRACE_FIELDS = 8;
-constexpr int ST_THREADS = NCT + 96;  // consumers, producer (NCW), reducer (NCW+1), stager (NCW+2)
+constexpr int ST_REDUCERS = 2;        // reducer warps, alternating over the items
+constexpr int ST_THREADS = NCT + 32 * (2 + ST_REDUCERS);  // consumers, producer (warp NCW),
+                                      // reducers (NCW+1 ..), stager (last warp)
 constexpr int ST_NB = 4;              // partial-sum buffers between consumers and reducer
 constexpr int ST_DNB = 4;             // down-projection input buffers (stager to consumers)
-constexpr int EXIT_BAR = 2;           // named barrier: consumers + reducer
+constexpr int EXIT_BAR = 2;           // named barrier: consumers + reducers
 
 struct StDense {
   const uint16_t* x;
@@ -572,77 +574,60 @@ __device__ __forceinline__ void split_compute(const Item& it, const Split& sp,
   }
 }
 
-// Partial sums of an item's warps are handed to the reducer warp through a
+// Partial sums of an item's warps are handed to the reducer warps through a
 // small ring of shared-memory buffers: every consumer warp stores the partial
 // of its (matrix, row block, reduction slice) and arrives on the buffer's
-// `done` mbarrier (count NCW); the reducer waits for it, sums the slices of
-// each row block in fixed order (so results do not depend on timing), writes
-// the outputs and arrives on `free` (count 1) so the buffer can be refilled.
+// `done` mbarrier (count NCW); the reducer that owns the item (items
+// alternate between the ST_REDUCERS reducer warps) waits for it, sums the
+// slices of each row block in fixed order (so results do not depend on
+// timing), writes the outputs and arrives on the buffer's `free` mbarrier
+// (count 1) so it can be refilled.
 struct Partials {
   float* buf;      // [ST_NB][NCW slots][16 rows][T tokens]
-  uint64_t* done;  // [ST_NB]
-  int* taken;      // items the reducer has finished reading (release store by the reducer)
+  uint64_t* done;  // [ST_NB] count NCW
+  uint64_t* free;  // [ST_NB] count 1
   int T;
-  int slot;
-  uint32_t phase;
-  int count;       // items published (consumers) or taken (reducer) so far
-  __device__ __forceinline__ void advance() {
-    if (++slot == ST_NB) {
-      slot = 0;
-      phase ^= 1u;
-    }
+  int count;       // items published (consumers) or seen (reducers) so far
+  __device__ __forceinline__ int slot() const { return count & (ST_NB - 1); }
+  __device__ __forceinline__ uint32_t phase() const { return (uint32_t)(count / ST_NB) & 1u; }
+  __device__ __forceinline__ const float* cur() const {
+    return buf + (size_t)slot() * NCW * 16 * T;
   }
-  __device__ __forceinline__ float* cur() const { return buf + (size_t)slot * NCW * 16 * T; }
+  // Reducer r owns the items whose sequence number is r modulo ST_REDUCERS.
+  __device__ __forceinline__ bool mine(int r) const { return count % ST_REDUCERS == r; }
 };
 
 // Consumer side: store this warp's partial in slot `pslot` (matrix*RBc*KS +
 // rb*KS + reduction slice) and arrive.  D fragment element e is row
 // g + 8*(e>>1), token 2t + (e&1).
-__device__ __forceinline__ int ld_acquire_cta_shared(const int* p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_cta_shared(int* p, int v) {
-  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ void partial_publish(const StepParams& P, Partials& pa, StPlan* pl,
                                                 int pslot, int ntok, const float (&acc)[1][4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  // The buffer is free once the reducer has taken the item published ST_NB ago.
-  if (pa.count >= ST_NB && ld_acquire_cta_shared(pa.taken) <= pa.count - ST_NB) {
-    const long long t0 = now_ns();
-    while (ld_acquire_cta_shared(pa.taken) <= pa.count - ST_NB) {
-      if (*((volatile const int*)&pl->abort) != 0 || now_ns() - t0 > ST_WAIT_NS) {
-        if (lane == 0 && !pl->abort) raise_abort(P, pl, ERR_TIMEOUT);
-        break;
-      }
-    }
-  }
-  ++pa.count;
-  float* base = pa.cur() + (size_t)pslot * 16 * pa.T;
+  const int s = pa.slot();
+  // The buffer is free once its reducer has read the item published ST_NB ago.
+  if (pa.count >= ST_NB && !stage_wait(&pa.free[s], pa.phase() ^ 1u, pl) && lane == 0 &&
+      !pl->abort)
+    raise_abort(P, pl, ERR_TIMEOUT);
+  float* base = pa.buf + ((size_t)s * NCW + pslot) * 16 * pa.T;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int row = g + ((e >> 1) << 3), tok = 2 * t + (e & 1);
     if (tok < ntok) base[row * pa.T + tok] = acc[0][e];
   }
   __syncwarp();
-  if (lane == 0) mbar_arrive(&pa.done[pa.slot]);
-  pa.advance();
+  if (lane == 0) mbar_arrive(&pa.done[s]);
+  ++pa.count;
 }
 
 // Reducer side: wait for the next item's partials (false when aborting).
 __device__ __forceinline__ bool partial_take(Partials& pa, const StPlan* pl) {
-  return stage_wait(&pa.done[pa.slot], pa.phase, pl);
+  return stage_wait(&pa.done[pa.slot()], pa.phase(), pl);
 }
 
 __device__ __forceinline__ void partial_release(Partials& pa) {
   __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&pa.free[pa.slot()]);
   ++pa.count;
-  if ((threadIdx.x & 31) == 0) st_release_cta_shared(pa.taken, pa.count);
-  pa.advance();
 }
 
 // Sum of the KS slices of row block rb (matrix m) at (row, tok).
@@ -1726,8 +1711,9 @@ __device__ bool combine_pairs(const StepParams& P, const MoeEpi& m, StPlan* pl, 
   return true;
 }
 
+// Reducer `rid` walks the consumers' item sequence and takes its own items.
 __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint64_t* plan_bar,
-                             uint64_t* plan_ack) {
+                             uint64_t* plan_ack, int rid) {
   const int lane = threadIdx.x & 31;
   const int G = gridDim.x;
   uint32_t plan_phase = 0;
@@ -1758,6 +1744,10 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
           pair = Dg.mats == 2;
           y = Dg.y;
           ys = Dg.ys;
+        }
+        if (!pa.mine(rid)) {
+          ++pa.count;
+          continue;
         }
         if (!partial_take(pa, pl)) {
           ok = false;
@@ -1790,12 +1780,20 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       const MoeEpi m = moe_epi(P, op);
       ExpertIter ei;
       ei.start(first_item(op.rot), m.items_rb);
-      for (; ei.i < m.items_rb && ok; ei.next(G, m.items_rb))
-        ok = reduce_up_item(m, pl, pa, 0, op.T, ei);
+      for (; ei.i < m.items_rb && ok; ei.next(G, m.items_rb)) {
+        if (pa.mine(rid))
+          ok = reduce_up_item(m, pl, pa, 0, op.T, ei);
+        else
+          ++pa.count;
+      }
       if (!ok) break;
       if (!stage_wait(plan_bar, plan_phase, pl)) break;
       const int n = pl->nslots * m.items_rb;
       for (; ei.i < n && ok; ei.next(G, m.items_rb)) {
+        if (!pa.mine(rid)) {
+          ++pa.count;
+          continue;
+        }
         const int abase = pl->slot_start[ei.slot];
         ok = reduce_up_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei);
       }
@@ -1804,14 +1802,20 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       const int n = pl->nslots * m.items_rb;
       int items = 0;
       ExpertIter ei;
-      for (ei.start(first_item(op.rot), m.items_rb); ei.i < n && ok; ei.next(G, m.items_rb), ++items) {
+      for (ei.start(first_item(op.rot), m.items_rb); ei.i < n && ok; ei.next(G, m.items_rb)) {
+        if (!pa.mine(rid)) {
+          ++pa.count;
+          continue;
+        }
         const int abase = pl->slot_start[ei.slot];
         ok = reduce_down_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei);
+        ++items;
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0 && items > 0) red_release(m.items_done, items);
-      ok = combine_pairs(P, m, pl, op.T, op.rot, n);
+      // One reducer writes the combine output.
+      if (rid == 0) ok = combine_pairs(P, m, pl, op.T, op.rot, n);
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(plan_ack);
@@ -1844,17 +1848,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   Partials pa;
   pa.buf = reinterpret_cast<float*>(smem + P.red_off);
   pa.done = plan_ack + 1;
-  pa.taken = reinterpret_cast<int*>(pa.done + ST_NB);
+  pa.free = pa.done + ST_NB;
   pa.T = P.T;
-  pa.slot = 0;
-  pa.phase = 0;
   pa.count = 0;
   XBufs X;
   X.base = smem;
   X.x_bytes = P.x_bytes;
   X.nxb = P.nxb;
   X.desc = reinterpret_cast<StOp*>(smem + P.desc_off);
-  X.ready = reinterpret_cast<uint64_t*>(pa.taken + 2);
+  X.ready = pa.free + ST_NB;
   X.free = X.ready + 2;
   X.dready = X.free + 2;
   X.dfree = X.dready + ST_DNB;
@@ -1867,9 +1869,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
       mbar_init(&R.empty[s], NCW);
     }
     mbar_init(plan_bar, 1);
-    mbar_init(plan_ack, 2);  // producer and reducer
-    for (int b = 0; b < ST_NB; ++b) mbar_init(&pa.done[b], NCW);
-    *pa.taken = 0;
+    mbar_init(plan_ack, 1 + ST_REDUCERS);  // producer and reducers
+    for (int b = 0; b < ST_NB; ++b) {
+      mbar_init(&pa.done[b], NCW);
+      mbar_init(&pa.free[b], 1);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&X.ready[b], 1);
       mbar_init(&X.free[b], NCW);
@@ -1891,12 +1895,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     producer_main(P, pl, R, plan_bar, plan_ack);
     return;
   }
-  if (warp == NCW + 1) {
-    reducer_main(P, pl, pa, plan_bar, plan_ack);
-    named_barrier(EXIT_BAR, NCT + 32);
+  if (warp > NCW && warp <= NCW + ST_REDUCERS) {
+    reducer_main(P, pl, pa, plan_bar, plan_ack, warp - NCW - 1);
+    named_barrier(EXIT_BAR, NCT + 32 * ST_REDUCERS);
     return;
   }
-  if (warp == NCW + 2) {
+  if (warp == NCW + 1 + ST_REDUCERS) {
     pdl_wait();
     stager_main(P, pl, X, plan_bar);
     return;
@@ -1953,7 +1957,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   }
   // Exit: once the reducer is done too, the last CTA resets every counter for
   // the next launch (all of its consumer threads; the exit counter last).
-  named_barrier(EXIT_BAR, NCT + 32);
+  named_barrier(EXIT_BAR, NCT + 32 * ST_REDUCERS);
   if (threadIdx.x == 0) {
     __threadfence();
     const int old = atomicAdd(&P.sync[P.exit_idx], 1);
@@ -2466,7 +2470,8 @@ int kb_step_finalize(kb_step* step) {
   P.drow_bytes = std::max(128, (drow + 127) / 128 * 128);
   P.dnb = std::max(1, std::min(kb::ST_DNB, P.x_bytes / P.drow_bytes));
   const int desc_bytes = ((int)sizeof(kb::StOp) + 127) / 128 * 128;
-  const int nbar = 2 + kb::ST_NB + 1 + 4 + 2 * kb::ST_DNB;
+  const int nbar = 2 + 2 * kb::ST_NB + 4 + 2 * kb::ST_DNB;  // plan, ack, partial done/free,
+                                                           // x ready/free, down ready/free
   for (int nxb = 2; nxb >= 1; --nxb) {
     P.nxb = nxb;
     P.desc_off = nxb * P.x_bytes;
