@@ -280,7 +280,7 @@ KB_API int kb_step_info(const kb_step* step, int* n_ops, int* stages, int* stage
 /* Optional timeline: with a device buffer of kb_step_trace_entries() int64   */
 /* set, every launch records %globaltimer ns per (CTA, operation) in 8 fields: */
 /* consumers start, inputs ready, routing built (expert blocks), end, producer */
-/* done issuing the weights, reducer done, shared-expert items done (expert    */
+/* done issuing the weights, reducers done, shared-expert items done (expert   */
 /* gate/up), spare.  NULL switches it off.                                    */
 KB_API int kb_step_set_trace(kb_step* step, int64_t* trace, int64_t entries);
 KB_API int64_t kb_step_trace_entries(const kb_step* step);

@@ -179,7 +179,7 @@ class StepProgram:
     def enable_trace(self) -> torch.Tensor:
         """Record a timeline on every launch; returns the int64 buffer
         [grid, n_ops, 8] (consumers start, inputs ready, routing built, end,
-        producer done issuing, reducer done, shared-expert items done, spare;
+        producer done issuing, reducers done, shared-expert items done, spare;
         %globaltimer ns)."""
         n = int(_lib.lib().kb_step_trace_entries(self._h))
         buf = torch.zeros(n, dtype=torch.int64, device="cuda")
