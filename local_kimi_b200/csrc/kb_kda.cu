@@ -9,7 +9,7 @@
 //   S' = C + (beta * k)[:, None] * d[None, :]
 //   o  = S'^T (q * scale)
 // Columns of S are independent, so a CTA owns one (batch, head) and a slice of
-// 32 columns: lane = column, the eight warps split the rows, the state slice
+// 32 columns: lane = column, the sixteen warps split the rows, the state slice
 // is read from HBM once into registers and written once.  Row-wise factors
 // (exp(decay), k, beta*k, q*scale) are computed once per CTA in shared memory.
 // Products and sums are kept as separate rounded fp32 operations in the order
@@ -18,7 +18,7 @@
 
 namespace kb {
 
-constexpr int KDA_WARPS = 8;
+constexpr int KDA_WARPS = 16;
 constexpr int KDA_COLS = 32;
 
 template <int RPW>
@@ -121,8 +121,8 @@ extern "C" int kb_kda_decode_step(float* state, int64_t sb, int64_t sh, int64_t 
   const dim3 grid((unsigned)(B * H), (unsigned)((Dv + kb::KDA_COLS - 1) / kb::KDA_COLS));
   const dim3 block(kb::KDA_WARPS * 32);
   if (Dk <= 128)
-    return kb::launch(kb::kda_step_kernel<16>, grid, block, 0, stream, state, sb, sh, sk, q, k,
+    return kb::launch(kb::kda_step_kernel<8>, grid, block, 0, stream, state, sb, sh, sk, q, k,
                       v, decay, beta, (int)H, (int)Dk, (int)Dv, scale, out, out_bf16);
-  return kb::launch(kb::kda_step_kernel<32>, grid, block, 0, stream, state, sb, sh, sk, q, k, v,
+  return kb::launch(kb::kda_step_kernel<16>, grid, block, 0, stream, state, sb, sh, sk, q, k, v,
                     decay, beta, (int)H, (int)Dk, (int)Dv, scale, out, out_bf16);
 }

@@ -499,6 +499,22 @@ __device__ void producer_main(const StepParams& P, StPlan* pl, Ring& R, uint64_t
         st_describe_moe(op, pl, i, it);
         produce_item(it, stage, full, pol);
       }
+    } else if (op.type == OP_KDA) {
+      // The consumers read their state slices as soon as the inputs are ready:
+      // bring the slices of this CTA's items into L2 now (the state is read
+      // only by this operation; a prefetch moves no data to the SM).
+      const int nsl = (op.Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
+      for (int u = first_item(op.rot); u < op.items; u += G) {
+        const int bh = u / nsl, sl = u - bh * nsl;
+        const int b = bh / op.H, h = bh - b * op.H;
+        const int cols = min(ST_KDA_COLS, op.Dv - sl * ST_KDA_COLS);
+        const float* base = op.state + (size_t)b * op.sb + (size_t)h * op.sh + sl * ST_KDA_COLS;
+        for (int i = lane; i < op.Dk; i += 32) {
+          const float* row = base + (size_t)i * op.sk;
+          if ((reinterpret_cast<uintptr_t>(row) & 15) == 0 && (cols & 3) == 0)
+            l2_prefetch_bulk(row, (uint32_t)cols * 4);
+        }
+      }
     } else if (op.type == OP_MOE_DOWN) {
       const int n = pl->nslots * op.items_rb;
       for (int i = first_item(op.rot); i < n && ok; i += G) {
@@ -1467,15 +1483,14 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
   }
 }
 
-// Warps 0..7 own rows i = r*8 + warp (r < 16) of a 32-column slice, as the
-// KDA kernel does, so the arithmetic (and its rounding) is the same; warps
-// 8..15 only keep the barriers.
+// Warp w owns rows i = r*16 + w (r < 8) of a 32-column slice, as the KDA
+// kernel does, so the arithmetic (and its rounding) is the same.
 __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* kd,
                         uint64_t* xready, uint32_t xphase) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
-  constexpr int KW = 8;    // computing warps
-  constexpr int RPW = 16;  // rows per computing warp (Dk <= 128)
+  constexpr int KW = NCW;  // computing warps
+  constexpr int RPW = 8;   // rows per warp (Dk <= 128)
   const bool worker = warp < KW;
   // Descriptor fields in registers: the loops below store to global memory
   // and must not re-read them.
