@@ -1059,42 +1059,49 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
     const float be = (rbias && warp < ST_RT_EXPERTS && e < E) ? __ldg(rbias + e) : 0.f;
     int s;
     const uint8_t* stage = consume_stage(P, R, pl, &s);
-    if (warp < ST_RT_EXPERTS && e < E) {
+    if (warp < ST_RT_EXPERTS && e < E && T == 1) {
+      // One token: a branch-free loop and a four-register accumulator (the
+      // general path below keeps eight tokens' accumulators live).
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint4* wp = reinterpret_cast<const uint4*>(stage + warp * K * 2) + lane;
+      const uint4* hp = reinterpret_cast<const uint4*>(xs) + lane;
+#pragma unroll 3
+      for (int w = lane; w < words; w += 32, wp += 32, hp += 32) router_word_fma(*wp, *hp, acc);
+      float v = router_lane_sum(acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      // Lane 0 publishes the word: the choice key of sigmoid + bias (plus
+      // one, so that zero means "not written") and the logit.
+      if (lane == 0) {
+        const float sc = 1.0f / (1.0f + expf(-v));
+        st_relaxed_u64(rwords + e, router_word(choice_key(sc + be), v));
+        next_rwords[e] = 0ull;
+      }
+    } else if (warp < ST_RT_EXPERTS && e < E) {
       float acc[ST_MAX_T][4];
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
       uint32_t wa = smem_addr(stage) + (uint32_t)(warp * K * 2 + lane * 16);
-      uint32_t ha = xs_s + (uint32_t)(lane * 16);
-      if (T == 1) {
-        // One token: a branch-free loop (the per-token conditions of the
-        // general loop below keep the compiler from overlapping iterations).
-        const uint4* wp = reinterpret_cast<const uint4*>(stage + warp * K * 2) + lane;
-        const uint4* hp = reinterpret_cast<const uint4*>(xs) + lane;
-#pragma unroll 3
-        for (int w = lane; w < words; w += 32, wp += 32, hp += 32)
-          router_word_fma(*wp, *hp, acc[0]);
-      } else {
-        for (int w = lane; w < words; w += 32, wa += 512, ha += 512) {
-          uint4 wv;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
-                       : "r"(wa));
+      const uint32_t ha = xs_s + (uint32_t)(lane * 16);
+      for (int w = lane; w < words; w += 32, wa += 512) {
+        uint4 wv;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
+                     : "r"(wa));
 #pragma unroll
-          for (int m = 0; m < ST_MAX_T; ++m) {
-            if (m < T) {
-              uint4 hv;
-              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                           : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
-                           : "r"(ha + (uint32_t)(m * K * 2)));
-              router_word_fma(wv, hv, acc[m]);
-            }
+        for (int m = 0; m < ST_MAX_T; ++m) {
+          if (m < T) {
+            uint4 hv;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
+                         : "r"(ha + (uint32_t)(m * K * 2 + (w - lane) * 16)));
+            router_word_fma(wv, hv, acc[m]);
           }
         }
       }
-      // Lane m publishes token m's word: the choice key of sigmoid + bias
-      // (plus one, so that zero means "not written") and the logit.
+      // Lane m publishes token m's word.
 #pragma unroll
       for (int m = 0; m < ST_MAX_T; ++m) {
         if (m < T) {
