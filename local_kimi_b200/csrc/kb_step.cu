@@ -697,8 +697,9 @@ struct XBufs {
   uint8_t* base;   // nxb buffers of x_bytes
   int x_bytes, nxb;
   StOp* desc;      // nxb descriptor copies
-  uint64_t* ready; // [nxb] count 1 (stager)
+  uint64_t* ready; // [nxb] count 1 (stager): dependencies complete, activations staged
   uint64_t* free;  // [nxb] count NCW (consumer warps)
+  uint64_t* dsc;   // [nxb] count 1 (stager): descriptor copied
   uint64_t* dready;  // [ST_DNB] down inputs staged, count 1 (stager)
   uint64_t* dfree;   // [ST_DNB] down inputs consumed, count NCW
   int dnb, drow_bytes;
@@ -753,6 +754,7 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
       reinterpret_cast<int*>(dst)[w] = src[w];
     __syncwarp();
     const StOp& op = *dst;
+    if (lane == 0) mbar_arrive(&X.dsc[b]);
     bool ok = true;
     for (int d = 0; d < op.ndeps && ok; ++d) {
       if (op.dep[d] == op.comb_src) continue;  // the consumers wait for its items
@@ -955,14 +957,18 @@ __device__ void run_dense_chunked(const StepParams& P, const StOp& op, StPlan* p
   }
 }
 
+// xready/xphase: the operation's inputs; the per-warp setup of the first
+// item is done before waiting for them.
 __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring& R, uint8_t* xs,
-                          Partials& pa) {
+                          Partials& pa, uint64_t* xready, uint32_t xphase) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
   const int G = gridDim.x;
   const int warp = threadIdx.x >> 5;
   const int nprob = op.nprob;
   const int n = op.p[nprob - 1].item_begin + op.p[nprob - 1].items;
   if (op.p[0].nchunk > 1) {
+    consumer_op_wait(P, pl, xready, xphase);
+    if (op.cstage) consumer_stage(P, pl, op, xs);
     run_dense_chunked(P, op, pl, R, xs, pa);
     return;
   }
@@ -976,8 +982,9 @@ __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring&
   const uint16_t* sglob = nullptr;
   const uint8_t* xrow0 = xs;
   int rot = 0;  // reduction slice of this warp = (ks + rot) % KS, rot advancing per item
-  for (int i = first_item(op.rot); i < n; i += G) {
-    if (i >= pend) {
+  bool waited = false;
+  for (int i = first_item(op.rot);; i += G) {
+    if (i < n && i >= pend) {
       do {
         ++p;
         pend = op.p[p].item_begin + op.p[p].items;
@@ -1008,6 +1015,14 @@ __device__ void run_dense(const StepParams& P, const StOp& op, StPlan* pl, Ring&
       base_ok = (reinterpret_cast<uintptr_t>(D.s) % 16 == 0) &&
                 (mats == 1 || reinterpret_cast<uintptr_t>(D.s3) % 16 == 0);
     }
+    if (!waited) {
+      // Inputs: wait for them (and stage them) once the first item's setup
+      // is done; every consumer thread passes here, with or without items.
+      consumer_op_wait(P, pl, xready, xphase);
+      if (op.cstage) consumer_stage(P, pl, op, xs);
+      waited = true;
+    }
+    if (i >= n) break;
     const int r0 = (i - ib) * item_rows;
     const int rows = min(item_rows, N - r0);
     const int rb_rows = min(16, rows - rb * 16);
@@ -1880,7 +1895,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   X.desc = reinterpret_cast<StOp*>(smem + P.desc_off);
   X.ready = pa.free + ST_NB;
   X.free = X.ready + 2;
-  X.dready = X.free + 2;
+  X.dsc = X.free + 2;
+  X.dready = X.dsc + 2;
   X.dfree = X.dready + ST_DNB;
   X.dnb = P.dnb;
   X.drow_bytes = P.drow_bytes;
@@ -1898,6 +1914,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&X.ready[b], 1);
+      mbar_init(&X.dsc[b], 1);
       mbar_init(&X.free[b], NCW);
     }
     for (int b = 0; b < ST_DNB; ++b) {
@@ -1943,18 +1960,21 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     }
     const int type = P.ops[o].type;
     uint8_t* xs = X.base + (size_t)xb * X.x_bytes;
+    // The descriptor copy is available before the operation's inputs are:
+    // work that needs only the descriptor goes before the input wait.
+    if (!stage_wait(&X.dsc[xb], xph, pl) && (threadIdx.x & 31) == 0 && !pl->abort)
+      raise_abort(P, pl, ERR_TIMEOUT);
     if (type == OP_KDA) {
       // The KDA state does not depend on this launch: its loads are issued
       // before the wait for the inputs (inside run_kda).
       run_kda(P, P.ops[o], pl, kd, &X.ready[xb], xph);
+    } else if (type == OP_DENSE) {
+      run_dense(P, X.desc[xb], pl, R, xs, pa, &X.ready[xb], xph);
     } else {
       consumer_op_wait(P, pl, &X.ready[xb], xph);
       const StOp& op = X.desc[xb];
       if (op.cstage) consumer_stage(P, pl, op, xs);
       switch (type) {
-        case OP_DENSE:
-          run_dense(P, op, pl, R, xs, pa);
-          break;
         case OP_ROUTER:
           run_router(P, op, pl, R, xs);
           break;
@@ -2492,8 +2512,8 @@ int kb_step_finalize(kb_step* step) {
   P.drow_bytes = std::max(128, (drow + 127) / 128 * 128);
   P.dnb = std::max(1, std::min(kb::ST_DNB, P.x_bytes / P.drow_bytes));
   const int desc_bytes = ((int)sizeof(kb::StOp) + 127) / 128 * 128;
-  const int nbar = 2 + 2 * kb::ST_NB + 4 + 2 * kb::ST_DNB;  // plan, ack, partial done/free,
-                                                           // x ready/free, down ready/free
+  const int nbar = 2 + 2 * kb::ST_NB + 6 + 2 * kb::ST_DNB;  // plan, ack, partial done/free,
+                                                           // x ready/free/desc, down ready/free
   for (int nxb = 2; nxb >= 1; --nxb) {
     P.nxb = nxb;
     P.desc_off = nxb * P.x_bytes;
