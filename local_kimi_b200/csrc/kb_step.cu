@@ -1214,19 +1214,23 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
       pl->cand_l[half][w8 * 8 + rank] = lg;
     }
     named_barrier(CBAR, NCT);
-    if (e < 64 && t < T) {
-      const int ec = pl->cand_e[half][e];
-      if (ec < E) {
-        const uint32_t kc = pl->cand_k[half][e];
-        int r2 = 0;
-        for (int j = 0; j < 64; ++j) {
-          const int ej = pl->cand_e[half][j];
-          r2 += (ej < E && choice_before(pl->cand_k[half][j], ej, kc, ec)) ? 1 : 0;
-        }
-        if (r2 < top_k) {
-          pl->pick_e[half][r2] = ec;
-          pl->pick_l[half][r2] = pl->cand_l[half][e];
-        }
+    // Rank of candidate e >> 2 among the 64, four threads (a quarter of the
+    // candidates each) per candidate.
+    {
+      const int c = e >> 2, q = e & 3;
+      const int ec = pl->cand_e[half][c];
+      const uint32_t kc = pl->cand_k[half][c];
+      int r2 = 0;
+#pragma unroll 4
+      for (int j = q * 16; j < q * 16 + 16; ++j) {
+        const int ej = pl->cand_e[half][j];
+        r2 += (ej < E && choice_before(pl->cand_k[half][j], ej, kc, ec)) ? 1 : 0;
+      }
+      r2 += __shfl_xor_sync(0xffffffffu, r2, 1);
+      r2 += __shfl_xor_sync(0xffffffffu, r2, 2);
+      if (q == 0 && t < T && ec < E && r2 < top_k) {
+        pl->pick_e[half][r2] = ec;
+        pl->pick_l[half][r2] = pl->cand_l[half][c];
       }
     }
     named_barrier(CBAR, NCT);
@@ -1257,24 +1261,26 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
         pl->route_e[tt * R + R - 1] = E;
         if (blockIdx.x == 0) rop.idx_out[(size_t)tt * (top_k + 1) + top_k] = E;
       }
+      if (T == 1) {
+        // One token: its routes are distinct experts, slot 1 + r holds
+        // route r (the plan, written by the same warp).
+        if (lane == 0) {
+          pl->assign[0] = R - 1;
+          pl->slot_expert[0] = E;
+          pl->slot_start[0] = 0;
+          pl->nslots = 1 + top_k;
+        }
+        if (lane < top_k) {
+          pl->slot_expert[1 + lane] = my_idx;
+          pl->slot_start[1 + lane] = 1 + lane;
+          pl->assign[1 + lane] = lane;
+        }
+        if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
+      }
     }
   }
-  named_barrier(CBAR, NCT);
-  if (warp == 0 && T == 1) {
-    // One token: its routes are distinct experts, slot 1 + r holds route r.
-    if (lane == 0) {
-      pl->assign[0] = R - 1;
-      pl->slot_expert[0] = E;
-      pl->slot_start[0] = 0;
-      pl->nslots = 1 + top_k;
-    }
-    if (lane < top_k) {
-      pl->slot_expert[1 + lane] = pl->route_e[lane];
-      pl->slot_start[1 + lane] = 1 + lane;
-      pl->assign[1 + lane] = lane;
-    }
-    if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
-  } else if (warp == 0) {
+  if (T > 1) named_barrier(CBAR, NCT);  // the plan below reads every token's routes
+  if (warp == 0 && T > 1) {
     if (lane < T) pl->assign[lane] = lane * R + R - 1;
     if (lane == 0) {
       pl->slot_expert[0] = E;
@@ -1662,7 +1668,15 @@ __device__ bool reduce_up_item(const MoeEpi& m, StPlan* pl, Partials& pa, int ab
   const int rows = min(m.item_rows, m.N - r0);
   uint16_t* const y = m.y;
   const int N = m.N;
-  if (cnt == 1) {
+  if (cnt == 1 && rows <= 16) {
+    // One token, one row block: lanes 0-15 sum the gate slices of row
+    // `lane`, lanes 16-31 the up slices of row `lane - 16`.
+    uint16_t* const yrow = y + (size_t)assign[0] * N + r0;
+    const int r = lane & 15, mat = lane >> 4;
+    const float v = r < rows ? partial_sum(pa, mat, m.RBc, m.KS, 0, r, 0) : 0.f;
+    const float uv = __shfl_down_sync(0xffffffffu, v, 16);
+    if (lane < rows) yrow[lane] = float_to_bf16_bits(swiglu_contract(v, uv));
+  } else if (cnt == 1) {
     uint16_t* const yrow = y + (size_t)assign[0] * N + r0;
     for (int r = lane; r < rows; r += 32) {
       const float gv = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, 0);
