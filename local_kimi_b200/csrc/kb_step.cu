@@ -1179,7 +1179,8 @@ __device__ __forceinline__ bool choice_before(uint32_t ka, int ea, uint32_t kb, 
 // shared expert (bank slot E, every token, route R-1); routed experts follow
 // in order of first use (token-major, then route order).  Indices are always
 // in [0, E), whatever the words hold.
-__device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
+__device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl,
+                              uint64_t* plan_bar) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const StOp& rop = P.ops[up.router_op];
   const int T = up.T, R = up.R, top_k = rop.top_k, E = rop.E;
@@ -1276,6 +1277,9 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
           pl->assign[1 + lane] = lane;
         }
         if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
+        // The plan is complete: the producer may stream the routed experts.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(plan_bar);
       }
     }
   }
@@ -1338,6 +1342,8 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl) {
     }
     __syncwarp();
     for (int sl = 1 + lane; sl < nslot; sl += 32) pl->slot_of[pl->slot_expert[sl]] = -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(plan_bar);
   }
   if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 2);
   named_barrier(CBAR, NCT);
@@ -1469,8 +1475,7 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
       raise_abort(P, pl, ERR_TIMEOUT);
     named_barrier(CBAR, NCT);
   }
-  build_routing(P, op, pl);
-  if (threadIdx.x == 0) mbar_arrive(plan_bar);
+  build_routing(P, op, pl, plan_bar);
   ++plan_round;
   const int n = pl->nslots * w.items_rb;
   for (; it.i < n; it.next(G, w.items_rb)) {
