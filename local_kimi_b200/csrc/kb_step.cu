@@ -811,7 +811,7 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
         const int a0 = pl->slot_start[slot], cnt = pl->slot_start[slot + 1] - a0;
         uint8_t* dst = xs + (size_t)j * X.drow_bytes;
         for (int m = 0; m < cnt; ++m)
-          stage_row_cg<1>(dst + m * ts, op.mx + (size_t)pl->assign[a0 + m] * op.mxs, op.K, lane,
+          stage_row_cg<4>(dst + m * ts, op.mx + (size_t)pl->assign[a0 + m] * op.mxs, op.K, lane,
                           32);
         __syncwarp();
         if (lane == 0) mbar_arrive(&X.dready[j]);
