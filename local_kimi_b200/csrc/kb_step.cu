@@ -81,6 +81,8 @@ struct StDense {
   int K, N, gshift, KS, RBc, nchunk, mats;
   int items, item_begin, x_off;
   int xcomb;  // x is the output of the down operation just before: staged as its combine
+  uint32_t* ytag;        // tagged copy of y ([T][N] words), read by the next operation
+  uint32_t* xtag;        // x read from the previous operation's tagged copy ([T][K] words)
 };
 
 struct StOp {
@@ -94,6 +96,10 @@ struct StOp {
   int items;   // static items (dense, router, KDA)
   int cstage;  // dense/router: the consumers stage the activations (input of the previous operation)
   int comb_src;  // dense: down operation whose combine the consumers compute while staging, or -1
+  int tag_src;   // operation whose output this one reads as tagged words (no counter wait), or -1
+  uint32_t* rxtag;        // router: hidden rows read from a tagged copy ([T][K] words)
+  uint32_t* ktag;         // KDA: tagged copy of the bf16 output ([B][H*Dv] words)
+  uint32_t* wtag;         // down: tagged copy of the per-route outputs ([T*R][N] words)
   // dense
   int nprob;
   StDense p[ST_MAX_PROB];
@@ -143,7 +149,7 @@ struct StepParams {
   int* sync;
   int nsync;
   int exit_idx, abort_idx;
-  int parity_idx;    // launch parity (selects the router words of this launch)
+  int parity_idx;    // launch count (its parity selects the router words of this launch)
   uint32_t* err;
   int stages, stage_bytes;
   int ring_off, red_off, scr_off, bar_off;
@@ -176,6 +182,7 @@ struct StPlan {
   int abort;
   int last;
   int parity;  // launch parity
+  uint32_t launch;  // launches of this program before this one
   int cur_op;  // operation the consumers are in (timeline)
 };
 
@@ -298,6 +305,70 @@ __device__ __forceinline__ void stage_row_cg(uint8_t* xs_row, const uint16_t* sr
         *reinterpret_cast<uint4*>(xs_row + ((w & 3) * NC + (w >> 2)) * 16) = permute_pairs(v[b]);
     }
   }
+}
+
+// Tagged activations.  An operation whose output feeds the one right after it
+// also writes each bf16 value as a 32-bit word with a tag in the high half:
+// (launch * nops + op + 1) mod 2^16, distinct for every writer of a launch and
+// from every word of the previous launch (2 * nops < 2^16), and never 0 in the
+// first launch (the buffers start zeroed).  The reader polls the words
+// themselves instead of a completion counter followed by the load: one L2
+// round trip instead of two.  A word is one 32-bit store, so a reader sees
+// the value and its tag together.  pl->launch is set by consumer thread 0
+// before the first consumer barrier.
+__device__ __forceinline__ uint32_t op_tag(const StPlan* pl, int nops, int o) {
+  return (pl->launch * (uint32_t)nops + (uint32_t)o + 1u) & 0xffffu;
+}
+
+__device__ __forceinline__ void st_tag(uint32_t* p, uint16_t v, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"((uint32_t)v | (tag << 16))
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_tags4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_tags2(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool tags_ok4(uint4 v, uint32_t tag) {
+  return ((v.x >> 16) == tag) & ((v.y >> 16) == tag) & ((v.z >> 16) == tag) & ((v.w >> 16) == tag);
+}
+
+// Eight tagged values (8 consecutive elements from p, 16-byte aligned) as
+// bf16x8 in natural order, once all carry `tag` (bounded wait).
+__device__ uint4 poll_tagged8(const StepParams& P, StPlan* pl, const uint32_t* p, uint32_t tag) {
+  uint4 a = ld_tags4(p), b = ld_tags4(p + 4);
+  if (!(tags_ok4(a, tag) && tags_ok4(b, tag))) {
+    const long long t0 = now_ns();
+    for (int spins = 1;; ++spins) {
+      __nanosleep(32);
+      a = ld_tags4(p);
+      b = ld_tags4(p + 4);
+      if (tags_ok4(a, tag) && tags_ok4(b, tag)) break;
+      if ((spins & 15) == 0) {
+        if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
+          pl->abort = 1;
+          break;
+        }
+        if (now_ns() - t0 > ST_WAIT_NS) {
+          raise_abort(P, pl, ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  return make_uint4(prmt(a.x, a.y, 0x5410), prmt(a.z, a.w, 0x5410), prmt(b.x, b.y, 0x5410),
+                    prmt(b.z, b.w, 0x5410));
 }
 
 // One combined value: bf16(sum_r routed_r * w_r, fp32 in route order) +
@@ -757,7 +828,9 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
     if (lane == 0) mbar_arrive(&X.dsc[b]);
     bool ok = true;
     for (int d = 0; d < op.ndeps && ok; ++d) {
-      if (op.dep[d] == op.comb_src) continue;  // the consumers wait for its items
+      // The consumers wait for the items of a combine source and poll the
+      // words of a tagged source.
+      if (op.dep[d] == op.comb_src || op.dep[d] == op.tag_src) continue;
       const StOp& dop = P.ops[op.dep[d]];
       ok = stager_poll(P, pl, dop.done, dop.target);
     }
@@ -834,7 +907,12 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
 // 8-byte half of a 16-byte word (few registers: this runs inside the
 // consumer loop) and trades a pair of values with its neighbour lane, which
 // holds the other half.  first/step: a warp-aligned thread index and stride.
+// TAGGED: the per-route outputs are read from their tagged copy (wtags, same
+// layout in 32-bit words), polling until every word carries `tag`.
+template <bool TAGGED>
 __device__ __forceinline__ void stage_combined(uint8_t* xs_row, const uint16_t* wrows,
+                                               const uint32_t* wtags, uint32_t tag,
+                                               const StepParams& P, StPlan* pl,
                                                const float* rw, int top_k, int R, int N,
                                                int first, int step) {
   const int NC = N >> 5;
@@ -843,12 +921,47 @@ __device__ __forceinline__ void stage_combined(uint8_t* xs_row, const uint16_t* 
     const bool valid = h < halves;
     const int part = h & 1, w = h >> 1;
     uint2 v[ST_MAX_TOPK];
+    uint2 sv;
+    if constexpr (TAGGED) {
+      const uint32_t f = tag << 16;
+      uint4 t[ST_MAX_TOPK], ts;
+      const long long t0 = now_ns();
+      for (int spins = 0;; ++spins) {
+        bool ok = true;
 #pragma unroll
-    for (int r = 0; r < ST_MAX_TOPK; ++r)
-      v[r] = (valid && r < top_k) ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)r * N) + h)
-                                  : make_uint2(0u, 0u);
-    const uint2 sv = valid ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)(R - 1) * N) + h)
-                           : make_uint2(0u, 0u);
+        for (int r = 0; r < ST_MAX_TOPK; ++r) {
+          t[r] = (valid && r < top_k) ? ld_tags4(wtags + (size_t)r * N + 4 * h)
+                                      : make_uint4(f, f, f, f);
+          ok &= tags_ok4(t[r], tag);
+        }
+        ts = valid ? ld_tags4(wtags + (size_t)(R - 1) * N + 4 * h) : make_uint4(f, f, f, f);
+        ok &= tags_ok4(ts, tag);
+        if (ok) break;
+        __nanosleep(32);
+        if ((spins & 15) == 15) {
+          if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
+            pl->abort = 1;
+            break;
+          }
+          if (now_ns() - t0 > ST_WAIT_NS) {
+            raise_abort(P, pl, ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < ST_MAX_TOPK; ++r)
+        v[r] = make_uint2(prmt(t[r].x, t[r].y, 0x5410), prmt(t[r].z, t[r].w, 0x5410));
+      sv = make_uint2(prmt(ts.x, ts.y, 0x5410), prmt(ts.z, ts.w, 0x5410));
+    } else {
+#pragma unroll
+      for (int r = 0; r < ST_MAX_TOPK; ++r)
+        v[r] = (valid && r < top_k)
+                   ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)r * N) + h)
+                   : make_uint2(0u, 0u);
+      sv = valid ? __ldcg(reinterpret_cast<const uint2*>(wrows + (size_t)(R - 1) * N) + h)
+                 : make_uint2(0u, 0u);
+    }
     uint32_t c[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -878,6 +991,7 @@ __device__ __forceinline__ void stage_combined(uint8_t* xs_row, const uint16_t* 
 // operation just before it: staged by all consumer threads (one L2 round
 // trip) once the stager has seen the input complete.
 __device__ void consumer_stage(const StepParams& P, StPlan* pl, const StOp& op, uint8_t* xs) {
+  const uint32_t tag = op.tag_src >= 0 ? op_tag(pl, P.nops, op.tag_src) : 0u;
   if (op.type == OP_DENSE) {
     int comb_off = -1, comb_k = 0;
     for (int p = 0; p < op.nprob; ++p) {
@@ -892,26 +1006,50 @@ __device__ void consumer_stage(const StepParams& P, StPlan* pl, const StOp& op, 
         continue;
       }
       const int ts = token_stride(D.K);
-      for (int m = 0; m < op.T; ++m)
-        stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+      if (D.xtag) {
+        const int NC = D.K >> 5, words = D.K >> 3;
+        for (int m = 0; m < op.T; ++m) {
+          uint8_t* const row = xs + D.x_off + m * ts;
+          for (int w = threadIdx.x; w < words; w += NCT)
+            *reinterpret_cast<uint4*>(row + ((w & 3) * NC + (w >> 2)) * 16) =
+                permute_pairs(poll_tagged8(P, pl, D.xtag + (size_t)m * D.K + 8 * w, tag));
+        }
+      } else {
+        for (int m = 0; m < op.T; ++m)
+          stage_row_cg(xs + D.x_off + m * ts, D.x + (size_t)m * D.xs, D.K, threadIdx.x, NCT);
+      }
     }
     if (comb_off >= 0) {
-      // The down operation's per-route outputs are complete once all of its
-      // items are (the plan in shared memory is still this layer's).
       const StOp& dop = P.ops[op.comb_src];
       const int R = dop.R, N = dop.N;
-      consumers_wait(P, pl, dop.items_done, pl->nslots * dop.items_rb);
       const int ts = token_stride(comb_k);
-      for (int m = 0; m < op.T; ++m)
-        stage_combined(xs + comb_off + m * ts, dop.wsy + (size_t)m * R * N,
-                       pl->route_w + m * (R - 1), R - 1, R, N, threadIdx.x, NCT);
+      if (dop.wtag) {
+        // Tagged per-route outputs: polled word by word.
+        for (int m = 0; m < op.T; ++m)
+          stage_combined<true>(xs + comb_off + m * ts, nullptr, dop.wtag + (size_t)m * R * N,
+                               tag, P, pl, pl->route_w + m * (R - 1), R - 1, R, N,
+                               threadIdx.x, NCT);
+      } else {
+        // The down operation's per-route outputs are complete once all of its
+        // items are (the plan in shared memory is still this layer's).
+        consumers_wait(P, pl, dop.items_done, pl->nslots * dop.items_rb);
+        for (int m = 0; m < op.T; ++m)
+          stage_combined<false>(xs + comb_off + m * ts, dop.wsy + (size_t)m * R * N, nullptr, 0u,
+                                P, pl, pl->route_w + m * (R - 1), R - 1, R, N, threadIdx.x,
+                                NCT);
+      }
     }
   } else {
     const int words = op.K >> 3;
     for (int m = 0; m < op.T; ++m) {
-      const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
       uint4* d4 = reinterpret_cast<uint4*>(xs + (size_t)m * op.K * 2);
-      for (int w = threadIdx.x; w < words; w += NCT) d4[w] = __ldcg(s4 + w);
+      if (op.rxtag) {
+        for (int w = threadIdx.x; w < words; w += NCT)
+          d4[w] = poll_tagged8(P, pl, op.rxtag + (size_t)m * op.K + 8 * w, tag);
+      } else {
+        const uint4* s4 = reinterpret_cast<const uint4*>(op.rx + (size_t)m * op.rxs);
+        for (int w = threadIdx.x; w < words; w += NCT) d4[w] = __ldcg(s4 + w);
+      }
     }
   }
   named_barrier(CBAR, NCT);
@@ -1518,7 +1656,7 @@ __device__ void run_moe_down(const StepParams& P, const StOp& op, StPlan* pl, Ri
 
 // Warp w owns rows i = r*16 + w (r < 8) of a 32-column slice, as the KDA
 // kernel does, so the arithmetic (and its rounding) is the same.
-__device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* kd,
+__device__ void run_kda(const StepParams& P, const StOp& op, int o, StPlan* pl, StKda* kd,
                         uint64_t* xready, uint32_t xphase) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
@@ -1538,6 +1676,8 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
   const float scale = op.scale;
   float* const kout = op.kout;
   uint16_t* const kout16 = op.kout_bf16;
+  uint32_t* const ktag = op.ktag;
+  const uint32_t tag = op_tag(pl, P.nops, o);
   int* const done = &P.sync[op.done];
   const int nsl = (Dv + ST_KDA_COLS - 1) / ST_KDA_COLS;
   bool waited = false;
@@ -1608,6 +1748,7 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
         for (int w = 0; w < KW; ++w) o = __fadd_rn(o, kd->red[w][lane]);
         if (kout) kout[(size_t)bh * Dv + col] = o;
         if (kout16) kout16[(size_t)bh * Dv + col] = float_to_bf16_bits(o);
+        if (ktag) st_tag(ktag + (size_t)bh * Dv + col, float_to_bf16_bits(o), tag);
       }
       // The outputs are published before the state is written back: only
       // the next launch reads the state, so its stores need not complete
@@ -1637,6 +1778,7 @@ __device__ void run_kda(const StepParams& P, const StOp& op, StPlan* pl, StKda* 
 struct MoeEpi {
   uint16_t* y;     // gate/up: activated rows
   uint16_t* wsy;   // down: per-route outputs
+  uint32_t* wtag;  // down: tagged copy of the per-route outputs (or null)
   uint16_t* out;   // down: combined rows
   int* slot_cnt;    // gate/up: per-slot counters
   int* items_done;  // down: finished items
@@ -1648,6 +1790,7 @@ __device__ __forceinline__ MoeEpi moe_epi(const StepParams& P, const StOp& op) {
   MoeEpi m;
   m.y = op.y;
   m.wsy = op.wsy;
+  m.wtag = op.wtag;
   m.out = op.out;
   m.slot_cnt = &P.sync[op.slot_cnt];
   m.items_done = &P.sync[op.items_done];
@@ -1704,7 +1847,7 @@ __device__ bool reduce_up_item(const MoeEpi& m, StPlan* pl, Partials& pa, int ab
 
 // Epilogue of one down item: the per-route outputs.
 __device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, int abase, int cnt,
-                                 const ExpertIter& ei) {
+                                 const ExpertIter& ei, uint32_t tag) {
   const int lane = threadIdx.x & 31;
   if (!partial_take(pa, pl)) return false;
   const int* assign = pl->assign + abase;
@@ -1712,16 +1855,23 @@ __device__ bool reduce_down_item(const MoeEpi& m, StPlan* pl, Partials& pa, int 
   const int rows = min(m.item_rows, m.N - r0);
   const int N = m.N;
   uint16_t* const wsy = m.wsy;
+  uint32_t* const wtag = m.wtag;
   if (cnt == 1) {
-    uint16_t* const yrow = wsy + (size_t)assign[0] * N + r0;
-    for (int r = lane; r < rows; r += 32)
-      yrow[r] = float_to_bf16_bits(partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, 0));
+    const size_t row0 = (size_t)assign[0] * N + r0;
+    for (int r = lane; r < rows; r += 32) {
+      const uint16_t b = float_to_bf16_bits(partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, 0));
+      wsy[row0 + r] = b;
+      if (wtag) st_tag(wtag + row0 + r, b, tag);
+    }
   } else {
     const int n = rows * cnt;
     for (int idx = lane; idx < n; idx += 32) {
       const int r = idx / cnt, tok = idx - r * cnt;
       const float v = partial_sum(pa, 0, m.RBc, m.KS, r >> 4, r & 15, tok);
-      wsy[(size_t)assign[tok] * N + r0 + r] = float_to_bf16_bits(v);
+      const size_t at = (size_t)assign[tok] * N + r0 + r;
+      const uint16_t b = float_to_bf16_bits(v);
+      wsy[at] = b;
+      if (wtag) st_tag(wtag + at, b, tag);
     }
   }
   partial_release(pa);
@@ -1784,6 +1934,7 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
       int p = -1, pend = 0, ib = 0, RBc = 1, KS = 1, N = 0, item_rows = 0;
       bool pair = false;
       uint16_t* y = nullptr;
+      uint32_t* ytag = nullptr;
       int64_t ys = 0;
       for (int i = first_item(op.rot); i < n && ok; i += G) {
         if (i >= pend) {
@@ -1799,6 +1950,7 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
           item_rows = RBc * 16;
           pair = Dg.mats == 2;
           y = Dg.y;
+          ytag = Dg.ytag;
           ys = Dg.ys;
         }
         if (!pa.mine(rid)) {
@@ -1817,7 +1969,9 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
             const float v0 = partial_sum(pa, 0, RBc, KS, r >> 4, r & 15, 0);
             const float val =
                 pair ? swiglu_contract(v0, partial_sum(pa, 1, RBc, KS, r >> 4, r & 15, 0)) : v0;
-            y[r0 + r] = float_to_bf16_bits(val);
+            const uint16_t b = float_to_bf16_bits(val);
+            y[r0 + r] = b;
+            if (ytag) st_tag(ytag + r0 + r, b, op_tag(pl, P.nops, o));
           }
         } else {
           for (int idx = lane; idx < rows * T; idx += 32) {
@@ -1825,7 +1979,9 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
             const float v0 = partial_sum(pa, 0, RBc, KS, r >> 4, r & 15, tok);
             const float val =
                 pair ? swiglu_contract(v0, partial_sum(pa, 1, RBc, KS, r >> 4, r & 15, tok)) : v0;
-            y[(size_t)tok * ys + r0 + r] = float_to_bf16_bits(val);
+            const uint16_t b = float_to_bf16_bits(val);
+            y[(size_t)tok * ys + r0 + r] = b;
+            if (ytag) st_tag(ytag + (size_t)tok * N + r0 + r, b, op_tag(pl, P.nops, o));
           }
         }
         partial_release(pa);
@@ -1864,7 +2020,8 @@ __device__ void reducer_main(const StepParams& P, StPlan* pl, Partials& pa, uint
           continue;
         }
         const int abase = pl->slot_start[ei.slot];
-        ok = reduce_down_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei);
+        ok = reduce_down_item(m, pl, pa, abase, pl->slot_start[ei.slot + 1] - abase, ei,
+                              op_tag(pl, P.nops, o));
         ++items;
       }
       if (!ok) break;
@@ -1966,7 +2123,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
 
   // Counters are reset by the previous launch; wait for it to finish.
   pdl_wait();
-  if (threadIdx.x == 0) pl->parity = *((volatile int*)&P.sync[P.parity_idx]) & 1;
+  if (threadIdx.x == 0) {
+    pl->launch = (uint32_t)*((volatile int*)&P.sync[P.parity_idx]);
+    pl->parity = (int)(pl->launch & 1u);
+  }
   named_barrier(CBAR, NCT);
   uint32_t plan_round = 0;
   DUse du;
@@ -1986,7 +2146,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     if (type == OP_KDA) {
       // The KDA state does not depend on this launch: its loads are issued
       // before the wait for the inputs (inside run_kda).
-      run_kda(P, P.ops[o], pl, kd, &X.ready[xb], xph);
+      run_kda(P, P.ops[o], o, pl, kd, &X.ready[xb], xph);
     } else if (type == OP_DENSE) {
       run_dense(P, X.desc[xb], pl, R, xs, pa, &X.ready[xb], xph);
     } else {
@@ -2029,7 +2189,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   if (pl->last) {
     for (int i = threadIdx.x; i < P.nsync; i += NCT)
       if (i != P.exit_idx && i != P.parity_idx) P.sync[i] = 0;
-    if (threadIdx.x == 0) P.sync[P.parity_idx] = pl->parity ^ 1;
+    if (threadIdx.x == 0) P.sync[P.parity_idx] = (int)(pl->launch + 1u);
     __threadfence();
     named_barrier(CBAR, NCT);
     if (threadIdx.x == 0) P.sync[P.exit_idx] = 0;
@@ -2047,6 +2207,7 @@ struct StepProgram {
   int device = -1;
   StOp* d_ops = nullptr;
   int* d_sync = nullptr;
+  uint32_t* d_tags = nullptr;  // tagged activation copies
   StepParams params = {};
   size_t smem = 0;
   int grid = 0;
@@ -2108,6 +2269,70 @@ static int current_sms() {
   return n > 0 ? n : 148;
 }
 
+// Tag field of the writer in `src` of the rows x[t * stride + k] (t < T,
+// k < K) as complete bf16 rows, or null: a dense problem's y or a KDA step's
+// bf16 output.
+static uint32_t** tag_writer(StOp& src, const uint16_t* x, int K, int64_t stride, int T) {
+  if (src.type == OP_DENSE) {
+    for (int q = 0; q < src.nprob; ++q) {
+      StDense& Q = src.p[q];
+      if (Q.y == x && Q.N == K && Q.ys == stride) return &Q.ytag;
+    }
+  } else if (src.type == OP_KDA) {
+    if (src.kout_bf16 == x && src.H * src.Dv == K && stride == K && src.B == T)
+      return &src.ktag;
+  }
+  return nullptr;
+}
+
+// Tagged activations: operation o reads the output of operation o - 1 as
+// tagged words (no wait for o - 1's completion counter) when every input it
+// stages comes from a writer that can keep a tagged copy.  Records (field,
+// word offset) pairs for the arena and sets op.tag_src.
+static void plan_tags(StepProgram* pr, size_t o, std::vector<std::pair<uint32_t**, size_t>>& fields,
+                      size_t& words) {
+  StOp& op = pr->ops[o];
+  op.tag_src = -1;
+  if (!op.cstage || o == 0) return;
+  StOp& src = pr->ops[o - 1];
+  const int T = pr->T;
+  auto offset_of = [&](uint32_t** writer, size_t n) {
+    for (const auto& f : fields)
+      if (f.first == writer) return f.second;
+    const size_t at = words;
+    words += (n + 31) / 32 * 32;
+    fields.emplace_back(writer, at);
+    return at;
+  };
+  if (op.type == OP_ROUTER) {
+    uint32_t** w = tag_writer(src, op.rx, op.K, op.rxs, T);
+    if (!w) return;
+    fields.emplace_back(&op.rxtag, offset_of(w, (size_t)T * op.K));
+    op.tag_src = (int)o - 1;
+    return;
+  }
+  if (op.type != OP_DENSE) return;
+  uint32_t** wr[ST_MAX_PROB] = {};
+  bool comb = false;
+  for (int i = 0; i < op.nprob; ++i) {
+    const StDense& D = op.p[i];
+    if (D.nchunk > 1) return;
+    bool dup = false;
+    for (int q = 0; q < i; ++q) dup |= (op.p[q].x_off == D.x_off);
+    if (dup) continue;
+    if (D.xcomb) {
+      comb = true;
+      continue;
+    }
+    wr[i] = tag_writer(src, D.x, D.K, D.xs, T);
+    if (!wr[i]) return;
+  }
+  for (int i = 0; i < op.nprob; ++i)
+    if (wr[i]) fields.emplace_back(&op.p[i].xtag, offset_of(wr[i], (size_t)T * op.p[i].K));
+  if (comb) offset_of(&src.wtag, (size_t)T * src.R * src.N);
+  op.tag_src = (int)o - 1;
+}
+
 }  // namespace kb
 
 using kb::StepProgram;
@@ -2130,12 +2355,13 @@ int kb_step_create(int64_t tokens, kb_step** out) {
 void kb_step_destroy(kb_step* step) {
   StepProgram* pr = reinterpret_cast<StepProgram*>(step);
   if (!pr) return;
-  if (pr->d_ops || pr->d_sync) {
+  if (pr->d_ops || pr->d_sync || pr->d_tags) {
     int cur = -1;
     cudaGetDevice(&cur);
     if (pr->device >= 0) cudaSetDevice(pr->device);
     cudaFree(pr->d_ops);
     cudaFree(pr->d_sync);
+    cudaFree(pr->d_tags);
     if (cur >= 0) cudaSetDevice(cur);
   }
   delete pr;
@@ -2448,6 +2674,8 @@ int kb_step_finalize(kb_step* step) {
   const int T = pr->T;
   // Rotations and the largest stage and activation regions.
   int stage = 0, xbytes = 0, cum = 0, drow = 0;
+  std::vector<std::pair<uint32_t**, size_t>> tag_fields;
+  size_t tag_words = 0;
   for (size_t o = 0; o < pr->ops.size(); ++o) {
     kb::StOp& op = pr->ops[o];
     // Inputs produced by the operation just before are staged by the
@@ -2469,6 +2697,7 @@ int kb_step_finalize(kb_step* step) {
         if (D.xcomb) op.comb_src = (int)o - 1;
       }
     }
+    kb::plan_tags(pr, o, tag_fields, tag_words);
     switch (op.type) {
       case kb::OP_DENSE: {
         op.rot = cum % G;
@@ -2553,6 +2782,13 @@ int kb_step_finalize(kb_step* step) {
   KB_REQUIRE(P.err, KB_ERR_DEVICE, "device error word unavailable");
   cudaError_t e = cudaMalloc(&pr->d_ops, pr->ops.size() * sizeof(kb::StOp));
   if (e == cudaSuccess) e = cudaMalloc(&pr->d_sync, (size_t)pr->nsync * sizeof(int));
+  // Tagged copies start zeroed (tag 0 is never a first launch's tag).
+  if (e == cudaSuccess && tag_words > 0) {
+    e = cudaMalloc(&pr->d_tags, tag_words * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(pr->d_tags, 0, tag_words * sizeof(uint32_t));
+    if (e == cudaSuccess)
+      for (const auto& f : tag_fields) *f.first = pr->d_tags + f.second;
+  }
   if (e == cudaSuccess)
     e = cudaMemcpy(pr->d_ops, pr->ops.data(), pr->ops.size() * sizeof(kb::StOp),
                    cudaMemcpyHostToDevice);
