@@ -809,12 +809,16 @@ __device__ bool stager_poll(const StepParams& P, StPlan* pl, int idx, int target
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uint64_t* plan_bar) {
+__device__ bool route_one(const StepParams& P, const StOp& up, StPlan* pl);
+
+__device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uint64_t* plan_bar,
+                            uint64_t* plan_ack) {
   const int lane = threadIdx.x & 31;
   const int G = gridDim.x;
   int b = 0;
   uint32_t ph = 0;
   uint32_t plan_phase = 0;
+  uint32_t route_round = 0;
   DUse du;
   int o = 0;
   for (; o < P.nops; ++o) {
@@ -863,6 +867,16 @@ __device__ void stager_main(const StepParams& P, StPlan* pl, const XBufs& X, uin
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&X.ready[b]);
+    if (op.type == OP_MOE_UP && op.T == 1) {
+      // One token: this warp builds the routing and the plan while the
+      // consumers compute the shared expert, once the producer and the
+      // reducers are done with the previous plan.
+      if (route_round > 0 && !stage_wait(plan_ack, (route_round - 1) & 1u, pl)) break;
+      ++route_round;
+      if (!route_one(P, op, pl)) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(plan_bar);
+    }
     if (op.type == OP_MOE_DOWN) {
       // Inputs of each down item of this CTA, in item order, as soon as the
       // gate/up of its slot is complete: the activated rows of the slot's
@@ -1306,8 +1320,125 @@ __device__ __forceinline__ bool choice_before(uint32_t ka, int ea, uint32_t kb, 
   return ka > kb || (ka == kb && ea < eb);
 }
 
-// Top-k of every token and the expert plan (warp 0), in every CTA from the
-// same router words, so every CTA holds the same plan.  The words are read as
+// Routing weight of a pick: unbiased sigmoid score renormalised over the
+// picks in pick order, scaled (lane r < top_k holds pick r's logit).
+__device__ __forceinline__ float route_weight(const StOp& rop, float logit, int lane) {
+  const int top_k = rop.top_k;
+  const float sc = lane < top_k ? 1.0f / (1.0f + expf(-logit)) : 0.f;
+  float wsum = 0.f;
+  for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, sc, r);
+  float wv = sc;
+  if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
+  return wv * rop.scaling;
+}
+
+// Routing and plan of a single token by one warp (the stager), the same as
+// build_routing computes them.  Lane l holds experts l + 32 j (j < 8).  Each
+// of top_k rounds takes every lane's best remaining expert (larger choice
+// key, then lower index), the warp's largest key (redux max) and the lowest
+// index holding it (redux min), and removes that expert.  Returns false when
+// a word wait gave up.
+__device__ bool route_one(const StepParams& P, const StOp& up, StPlan* pl) {
+  const int lane = threadIdx.x & 31;
+  const StOp& rop = P.ops[up.router_op];
+  const int R = up.R, top_k = rop.top_k, E = rop.E;
+  const unsigned long long* words = rop.rwords + (size_t)pl->parity * E;
+  // All eight words of a lane in flight at once, re-read together until all
+  // are written (bounded).
+  unsigned long long wd[8];
+  uint32_t missing = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (lane + 32 * j < E) missing |= 1u << j;
+  bool ok = true;
+  const long long t0 = now_ns();
+  for (int spins = 0; missing != 0u; ++spins) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if ((missing >> j) & 1u) wd[j] = ld_relaxed_u64(words + lane + 32 * j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (((missing >> j) & 1u) && (wd[j] >> 32) != 0ull) missing &= ~(1u << j);
+    if (missing == 0u) break;
+    __nanosleep(32);
+    if ((spins & 15) == 15) {
+      if (*((volatile int*)&P.sync[P.abort_idx]) != 0 || *((volatile int*)&pl->abort) != 0) {
+        pl->abort = 1;
+        ok = false;
+        break;
+      }
+      if (now_ns() - t0 > ST_WAIT_NS) {
+        raise_abort(P, pl, ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+  }
+  uint32_t k[8], ee[8];
+  float lg[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane + 32 * j;
+    const bool present = e < E;
+    k[j] = present ? (uint32_t)(wd[j] >> 32) - 1u : 0u;
+    ee[j] = present ? (uint32_t)e : 0xffffffffu;
+    lg[j] = present ? __uint_as_float((uint32_t)wd[j]) : 0.f;
+  }
+  if (!__all_sync(0xffffffffu, ok)) return false;
+  int my_e = 0;
+  float my_l = 0.f;
+  for (int r = 0; r < top_k; ++r) {
+    uint32_t bk = k[0], be = ee[0];
+    float bl = lg[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) {
+      const bool better = k[j] > bk || (k[j] == bk && ee[j] < be);
+      bk = better ? k[j] : bk;
+      be = better ? ee[j] : be;
+      bl = better ? lg[j] : bl;
+    }
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t win = __reduce_min_sync(0xffffffffu, bk == kmax ? be : 0xffffffffu);
+    const float l = __shfl_sync(0xffffffffu, bl, win & 31);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (ee[j] == win) {
+        k[j] = 0u;
+        ee[j] = 0xffffffffu;
+      }
+    }
+    if (lane == r) {
+      my_e = min((int)win, E - 1);
+      my_l = l;
+    }
+  }
+  const float wv = route_weight(rop, my_l, lane);
+  if (lane < top_k) {
+    pl->route_e[lane] = my_e;
+    pl->route_w[lane] = wv;
+    pl->slot_expert[1 + lane] = my_e;
+    pl->slot_start[1 + lane] = 1 + lane;
+    pl->assign[1 + lane] = lane;
+    if (blockIdx.x == 0) {
+      rop.idx_out[lane] = my_e;
+      rop.w_out[lane] = wv;
+    }
+  }
+  if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
+  if (lane == 0) {
+    pl->route_e[R - 1] = E;
+    pl->assign[0] = R - 1;
+    pl->slot_expert[0] = E;
+    pl->slot_start[0] = 0;
+    pl->nslots = 1 + top_k;
+    if (blockIdx.x == 0) rop.idx_out[top_k] = E;
+  }
+  return true;
+}
+
+// Top-k of every token and the expert plan (warp 0) for two or more tokens
+// (route_one builds a single token's), in every CTA from the same router
+// words, so every CTA holds the same plan.  The words are read as
 // soon as the router has written them (no completion counter between).  Two
 // tokens at a time, 256 consumer threads per token, one expert each: every
 // warp ranks its 32 experts with shuffles and keeps its best 8 (a superset
@@ -1377,18 +1508,9 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl,
     // renormalised in pick order, scaled.
     if (warp < 2 && t0 + warp < T) {
       const int tt = t0 + warp;
-      float sc = 0.f;
-      int my_idx = 0;
+      const int my_idx = lane < top_k ? min(max(pl->pick_e[warp][lane], 0), E - 1) : 0;
+      const float wv = route_weight(rop, lane < top_k ? pl->pick_l[warp][lane] : 0.f, lane);
       if (lane < top_k) {
-        my_idx = min(max(pl->pick_e[warp][lane], 0), E - 1);
-        sc = 1.0f / (1.0f + expf(-pl->pick_l[warp][lane]));
-      }
-      float wsum = 0.f;
-      for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, sc, r);
-      if (lane < top_k) {
-        float wv = sc;
-        if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
-        wv *= rop.scaling;
         pl->route_e[tt * R + lane] = my_idx;
         pl->route_w[tt * top_k + lane] = wv;
         if (blockIdx.x == 0) {
@@ -1400,29 +1522,10 @@ __device__ void build_routing(const StepParams& P, const StOp& up, StPlan* pl,
         pl->route_e[tt * R + R - 1] = E;
         if (blockIdx.x == 0) rop.idx_out[(size_t)tt * (top_k + 1) + top_k] = E;
       }
-      if (T == 1) {
-        // One token: its routes are distinct experts, slot 1 + r holds
-        // route r (the plan, written by the same warp).
-        if (lane == 0) {
-          pl->assign[0] = R - 1;
-          pl->slot_expert[0] = E;
-          pl->slot_start[0] = 0;
-          pl->nslots = 1 + top_k;
-        }
-        if (lane < top_k) {
-          pl->slot_expert[1 + lane] = my_idx;
-          pl->slot_start[1 + lane] = 1 + lane;
-          pl->assign[1 + lane] = lane;
-        }
-        if (lane == top_k) pl->slot_start[1 + top_k] = 1 + top_k;
-        // The plan is complete: the producer may stream the routed experts.
-        __syncwarp();
-        if (lane == 0) mbar_arrive(plan_bar);
-      }
     }
   }
-  if (T > 1) named_barrier(CBAR, NCT);  // the plan below reads every token's routes
-  if (warp == 0 && T > 1) {
+  named_barrier(CBAR, NCT);  // the plan below reads every token's routes
+  if (warp == 0) {
     if (lane < T) pl->assign[lane] = lane * R + R - 1;
     if (lane == 0) {
       pl->slot_expert[0] = E;
@@ -1607,13 +1710,21 @@ __device__ void run_moe_up(const StepParams& P, const StOp& op, StPlan* pl, Ring
   for (; it.i < w.items_rb; it.next(G, w.items_rb))
     expert_item(P, w, pl, R, pa, E, it.rbg, T, xshared, rot);
   if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 6);
-  // The producer must be done with the previous plan before it is replaced.
-  if (plan_round > 0) {
-    if (threadIdx.x == 0 && !stage_wait(plan_ack, (plan_round - 1) & 1, pl) && !pl->abort)
+  if (T == 1) {
+    // The stager builds a single token's plan (route_one).
+    if (threadIdx.x == 0 && !stage_wait(plan_bar, plan_round & 1u, pl) && !pl->abort)
       raise_abort(P, pl, ERR_TIMEOUT);
+    if (threadIdx.x == 0) trace_mark(P, pl->cur_op, 2);
     named_barrier(CBAR, NCT);
+  } else {
+    // The producer must be done with the previous plan before it is replaced.
+    if (plan_round > 0) {
+      if (threadIdx.x == 0 && !stage_wait(plan_ack, (plan_round - 1) & 1, pl) && !pl->abort)
+        raise_abort(P, pl, ERR_TIMEOUT);
+      named_barrier(CBAR, NCT);
+    }
+    build_routing(P, op, pl, plan_bar);
   }
-  build_routing(P, op, pl, plan_bar);
   ++plan_round;
   const int n = pl->nslots * w.items_rb;
   for (; it.i < n; it.next(G, w.items_rb)) {
@@ -2117,7 +2228,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   }
   if (warp == NCW + 1 + ST_REDUCERS) {
     pdl_wait();
-    stager_main(P, pl, X, plan_bar);
+    stager_main(P, pl, X, plan_bar, plan_ack);
     return;
   }
 
