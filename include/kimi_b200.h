@@ -249,8 +249,8 @@ KB_API int kb_step_add_swiglu(kb_step* step, const uint16_t* x, int64_t x_stride
 /* scratch: 16*tokens*E bytes, 8-byte aligned, one per router of the program  */
 /* and owned by it (zeroed by kb_step_finalize, not to be written between     */
 /* launches): per launch parity and (token, expert) a 64-bit word holding the */
-/* choice key + 1 and the fp32 logit.  idx_out int64 [tokens, top_k+1]       */
-/* (shared expert id E appended), w_out fp32 [tokens, top_k].                 */
+/* choice key + 1 and the fp32 sigmoid score.  idx_out int64                 */
+/* [tokens, top_k+1] (shared expert id E appended), w_out fp32 [tokens, top_k]. */
 KB_API int kb_step_add_router(kb_step* step, const uint16_t* hidden, int64_t h_stride,
                    int64_t K, const uint16_t* weight, const float* bias, int64_t E,
                    int64_t top_k, int renormalize, float scaling, void* scratch,

@@ -172,7 +172,9 @@ struct StPlan {
   int slot_of[ST_MAX_E + 1];
   int nslots;
   // Selection scratch, two tokens at a time: 8 candidates per warp of 32
-  // experts (choice key, expert, logit), then the picks in choice order.
+  // experts (choice key, expert, sigmoid score), then the picks in choice
+  // order.  A single token's routing (route_one) uses row 0 for the
+  // candidates at or above its threshold.
   uint32_t cand_k[2][64];
   int cand_e[2][64];
   float cand_l[2][64];
@@ -1238,10 +1240,10 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       // Lane 0 publishes the word: the choice key of sigmoid + bias (plus
-      // one, so that zero means "not written") and the logit.
+      // one, so that zero means "not written") and the sigmoid score.
       if (lane == 0) {
         const float sc = 1.0f / (1.0f + expf(-v));
-        st_relaxed_u64(rwords + e, router_word(choice_key(sc + be), v));
+        st_relaxed_u64(rwords + e, router_word(choice_key(sc + be), sc));
         next_rwords[e] = 0ull;
       }
     } else if (warp < ST_RT_EXPERTS && e < E) {
@@ -1277,7 +1279,7 @@ __device__ void run_router(const StepParams& P, const StOp& op, StPlan* pl, Ring
           for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
           if (lane == m) {
             const float sc = 1.0f / (1.0f + expf(-v));
-            st_relaxed_u64(rwords + (size_t)m * E + e, router_word(choice_key(sc + be), v));
+            st_relaxed_u64(rwords + (size_t)m * E + e, router_word(choice_key(sc + be), sc));
             next_rwords[(size_t)m * E + e] = 0ull;
           }
         }
@@ -1321,23 +1323,28 @@ __device__ __forceinline__ bool choice_before(uint32_t ka, int ea, uint32_t kb, 
 }
 
 // Routing weight of a pick: unbiased sigmoid score renormalised over the
-// picks in pick order, scaled (lane r < top_k holds pick r's logit).
-__device__ __forceinline__ float route_weight(const StOp& rop, float logit, int lane) {
+// picks in pick order, scaled (lane r < top_k holds pick r's score).
+__device__ __forceinline__ float route_weight(const StOp& rop, float score, int lane) {
   const int top_k = rop.top_k;
-  const float sc = lane < top_k ? 1.0f / (1.0f + expf(-logit)) : 0.f;
+  const float sc = lane < top_k ? score : 0.f;
+  float v[ST_MAX_TOPK];
+#pragma unroll
+  for (int r = 0; r < ST_MAX_TOPK; ++r) v[r] = __shfl_sync(0xffffffffu, sc, r);
   float wsum = 0.f;
-  for (int r = 0; r < top_k; ++r) wsum += __shfl_sync(0xffffffffu, sc, r);
+#pragma unroll
+  for (int r = 0; r < ST_MAX_TOPK; ++r)
+    if (r < top_k) wsum += v[r];
   float wv = sc;
   if (rop.renorm && top_k > 1) wv = wv / (wsum + 1e-20f);
   return wv * rop.scaling;
 }
 
 // Routing and plan of a single token by one warp (the stager), the same as
-// build_routing computes them.  Lane l holds experts l + 32 j (j < 8).  Each
-// of top_k rounds takes every lane's best remaining expert (larger choice
-// key, then lower index), the warp's largest key (redux max) and the lowest
-// index holding it (redux min), and removes that expert.  Returns false when
-// a word wait gave up.
+// build_routing computes them.  Lane l holds experts l + 32 j (j < 8).  The
+// lane bests ranked among themselves give a threshold H (the top_k-th best
+// of the lane bests): every pick is >= H in choice order, and the candidates
+// >= H (at most 8 * top_k, from top_k lanes) are ranked against each other
+// in shared memory.  Returns false when a word wait gave up.
 __device__ bool route_one(const StepParams& P, const StOp& up, StPlan* pl) {
   const int lane = threadIdx.x & 31;
   const StOp& rop = P.ops[up.router_op];
@@ -1374,44 +1381,57 @@ __device__ bool route_one(const StepParams& P, const StOp& up, StPlan* pl) {
       }
     }
   }
-  uint32_t k[8], ee[8];
-  float lg[8];
+  if (!__all_sync(0xffffffffu, ok)) return false;
+  // Choice order as one 64-bit value: key << 32 | ~expert (absent: 0).
+  unsigned long long c[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int e = lane + 32 * j;
-    const bool present = e < E;
-    k[j] = present ? (uint32_t)(wd[j] >> 32) - 1u : 0u;
-    ee[j] = present ? (uint32_t)e : 0xffffffffu;
-    lg[j] = present ? __uint_as_float((uint32_t)wd[j]) : 0.f;
+    c[j] = e < E ? ((wd[j] >> 32) - 1ull) << 32 | (uint32_t)~e : 0ull;
   }
-  if (!__all_sync(0xffffffffu, ok)) return false;
-  int my_e = 0;
-  float my_l = 0.f;
-  for (int r = 0; r < top_k; ++r) {
-    uint32_t bk = k[0], be = ee[0];
-    float bl = lg[0];
+  unsigned long long b = c[0];
 #pragma unroll
-    for (int j = 1; j < 8; ++j) {
-      const bool better = k[j] > bk || (k[j] == bk && ee[j] < be);
-      bk = better ? k[j] : bk;
-      be = better ? ee[j] : be;
-      bl = better ? lg[j] : bl;
-    }
-    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
-    const uint32_t win = __reduce_min_sync(0xffffffffu, bk == kmax ? be : 0xffffffffu);
-    const float l = __shfl_sync(0xffffffffu, bl, win & 31);
+  for (int j = 1; j < 8; ++j) b = c[j] > b ? c[j] : b;
+  int rank = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (ee[j] == win) {
-        k[j] = 0u;
-        ee[j] = 0xffffffffu;
-      }
-    }
-    if (lane == r) {
-      my_e = min((int)win, E - 1);
-      my_l = l;
+  for (int sl = 0; sl < 32; ++sl) rank += __shfl_sync(0xffffffffu, b, sl) > b ? 1 : 0;
+  const unsigned at = __ballot_sync(0xffffffffu, rank == top_k - 1);
+  const unsigned long long H = __shfl_sync(0xffffffffu, b, __ffs(at) - 1);
+  int cnt = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cnt += c[j] >= H ? 1 : 0;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  int w = incl - cnt;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (c[j] >= H) {
+      pl->cand_k[0][w] = (uint32_t)(c[j] >> 32);
+      pl->cand_e[0][w] = lane + 32 * j;
+      pl->cand_l[0][w] = __uint_as_float((uint32_t)wd[j]);
+      ++w;
     }
   }
+  __syncwarp();
+  for (int t = lane; t < total; t += 32) {
+    const uint32_t kt = pl->cand_k[0][t];
+    const int et = pl->cand_e[0][t];
+    int r = 0;
+#pragma unroll 1
+    for (int u = 0; u < total; ++u) r += choice_before(pl->cand_k[0][u], pl->cand_e[0][u], kt, et);
+    if (r < top_k) {
+      pl->pick_e[0][r] = et;
+      pl->pick_l[0][r] = pl->cand_l[0][t];
+    }
+  }
+  __syncwarp();
+  const int my_e = lane < top_k ? min(max(pl->pick_e[0][lane], 0), E - 1) : 0;
+  const float my_l = lane < top_k ? pl->pick_l[0][lane] : 0.f;
   const float wv = route_weight(rop, my_l, lane);
   if (lane < top_k) {
     pl->route_e[lane] = my_e;

@@ -110,7 +110,7 @@ class StepProgram:
                renormalize=True, deps=None) -> int:
         """Router logits into ``scratch`` (16 * T * E bytes, contiguous, owned by
         the program: per launch parity and (token, expert) a 64-bit word with
-        the choice key and the logit; one buffer per router, see
+        the choice key and the sigmoid score; one buffer per router, see
         ``router_scratch``); the selection runs in the expert block that uses
         this router and writes idx_out int64 [T, top_k+1] (shared id appended)
         and w_out."""
