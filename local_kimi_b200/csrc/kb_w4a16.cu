@@ -602,21 +602,9 @@ static int dense_multi_impl(const kb_dense_problem* probs, int count, void* stre
   const int nsub = (maxM > 8) ? 2 : 1;
   P.tok_cap = 8 * nsub;
   P.tstride = token_stride(maxK);
-  int items = 0, stage = 0;
-  for (int i = 0; i < P.nprob; ++i) {
-    DenseProb& D = P.prob[i];
-    D.items = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
-    D.item_begin = items;
-    items += D.items;
-    stage = std::max(stage, item_stage_bytes(D.K, 1, D.RBc, D.K >> (5 + D.gshift)));
-  }
   const int red_bytes = 2 * NCW * nsub * 128 * (int)sizeof(float);
-  const int x_budget =
-      std::min(X_RESIDENT_BUDGET, MAX_SMEM - SMEM_RESERVE - red_bytes - 2 * stage - 128);
-  KB_REQUIRE(x_budget >= P.tstride, KB_ERR_UNSUPPORTED,
-             "shared memory cannot hold one activation row of K=%d next to two stages", maxK);
-  // Resident activations: every distinct x, all of its tokens, if they fit.
-  int xbytes = 0;
+  // Resident activations: every distinct x, all of its tokens.
+  int xneed = 0;
   for (int i = 0; i < P.nprob; ++i) {
     DenseProb& D = P.prob[i];
     D.x_off = -1;
@@ -625,13 +613,63 @@ static int dense_multi_impl(const kb_dense_problem* probs, int count, void* stre
           P.prob[j].M == D.M)
         D.x_off = P.prob[j].x_off;
     if (D.x_off < 0) {
-      D.x_off = xbytes;
-      xbytes += D.M * P.tstride;
+      D.x_off = xneed;
+      xneed += D.M * P.tstride;
     }
   }
-  if (xbytes > x_budget) {
+  auto max_stage = [&P]() {
+    int st = 0;
+    for (int i = 0; i < P.nprob; ++i) {
+      const DenseProb& D = P.prob[i];
+      st = std::max(st, item_stage_bytes(D.K, 1, D.RBc, D.K >> (5 + D.gshift)));
+    }
+    return st;
+  };
+  // Room for activations beside the reduction buffers and two stages.
+  auto room = [&](int st) { return MAX_SMEM - SMEM_RESERVE - red_bytes - 2 * st - 128; };
+  // More tokens than the resident budget allows: smaller items (fewer rows,
+  // more reduction slices) when that lets every token stay resident, since
+  // otherwise each item restages its activations for every token group.
+  if (xneed > std::min(X_RESIDENT_BUDGET, room(max_stage()))) {
+    int ks[KB_MAX_DENSE_PROBLEMS], rbc[KB_MAX_DENSE_PROBLEMS];
+    for (int i = 0; i < P.nprob; ++i) {
+      ks[i] = P.prob[i].KS;
+      rbc[i] = P.prob[i].RBc;
+    }
+    bool shrunk = true;
+    while (xneed > room(max_stage()) && shrunk) {
+      shrunk = false;
+      for (int i = 0; i < P.nprob; ++i) {
+        DenseProb& D = P.prob[i];
+        if (D.RBc > 1 && D.KS * 2 <= (D.K + 127) / 128) {
+          D.RBc /= 2;
+          D.KS *= 2;
+          shrunk = true;
+        }
+      }
+    }
+    if (xneed > room(max_stage())) {
+      for (int i = 0; i < P.nprob; ++i) {
+        P.prob[i].KS = ks[i];
+        P.prob[i].RBc = rbc[i];
+      }
+    }
+  }
+  int items = 0;
+  for (int i = 0; i < P.nprob; ++i) {
+    DenseProb& D = P.prob[i];
+    D.items = (D.N + 16 * D.RBc - 1) / (16 * D.RBc);
+    D.item_begin = items;
+    items += D.items;
+  }
+  const int stage = max_stage();
+  KB_REQUIRE(room(stage) >= P.tstride, KB_ERR_UNSUPPORTED,
+             "shared memory cannot hold one activation row of K=%d next to two stages", maxK);
+  int xbytes = xneed;
+  if (xneed > room(stage)) {
+    const int cap = std::min(X_RESIDENT_BUDGET, room(stage));
     for (int i = 0; i < P.nprob; ++i) P.prob[i].x_off = -1;
-    P.tok_cap = std::min(P.tok_cap, x_budget / P.tstride);
+    P.tok_cap = std::min(P.tok_cap, std::max(1, cap / P.tstride));
     xbytes = P.tok_cap * P.tstride;
   }
   P.total_items = items;

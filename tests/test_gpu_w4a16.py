@@ -40,6 +40,8 @@ DENSE_SHAPES = [
     (1, 8192, 512, 128),     # MLA kv_b
     (4, 12288, 2304, 128),   # fused QKV width
     (16, 2304, 4096, 32),
+    (16, 12288, 2304, 128),  # 16 tokens resident once the items are made smaller
+    (32, 4096, 2304, 128),   # 32 tokens (147 KB of activations) resident
     (64, 2048, 2304, 128),   # more tokens than one staged group
     (3, 37, 96, 32),         # ragged N, partial 128-wide block
     (1, 5, 32, 32),          # one group
@@ -98,6 +100,11 @@ def test_fused_qkv_and_multi(cuda):
     q, k, v = ops.fused_qkv_w4a16(x, *mats[0], *mats[1], *mats[2])
     for out, (p, s) in zip((q, k, v), mats):
         assert_close(out, oref.dense(x.cpu(), p.cpu(), s.cpu()), what="fused qkv")
+    # batch 32: three problems sharing one resident activation block
+    x32 = rand_act((32, 2304), cuda_gen(2))
+    q, k, v = ops.fused_qkv_w4a16(x32, *mats[0], *mats[1], *mats[2])
+    for out, (p, s) in zip((q, k, v), mats):
+        assert_close(out, oref.dense(x32.cpu(), p.cpu(), s.cpu()), what="fused qkv M=32")
     # problems with different K and N in one launch (MLA q / kv_b / o_proj)
     a = quant_matrix(6144, 2304, 128, gen)
     b = quant_matrix(8192, 512, 128, gen)
