@@ -70,11 +70,14 @@ def _args() -> argparse.Namespace:
     ap.add_argument("--path", choices=("executor", "per-op"), default="executor",
                     help="executor: the whole step in one persistent launch (batch <= 8); "
                          "per-op: the registry-level launches captured in a CUDA graph")
-    ap.add_argument("--case", choices=("step", "lm_head", "moe", "eager", "program"),
+    ap.add_argument("--case",
+                    choices=("step", "lm_head", "moe", "eager", "program", "dense_sweep"),
                     default="step",
                     help="step = the benchmark; the others run one op family eagerly for "
                          "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
-                         "combine of one layer; eager: uncaptured decode steps)")
+                         "combine of one layer; eager: uncaptured decode steps); "
+                         "dense_sweep: the W4A16 dense GEMV/GEMM sweep (M 1/4/16/64 over the "
+                         "QKV, o_proj, shared gate|up and lm_head shapes), HBM GB/s vs peak")
     return ap.parse_args()
 
 
@@ -544,12 +547,73 @@ def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
+def run_dense_sweep(args) -> dict:
+    """The dense W4A16 sweep: y[M,N] = x[M,K] . dequant(W)^T for the decode
+    shapes at M in {1, 4, 16, 64}, group args.group.  Each point replays a CUDA
+    graph of calls over enough weight copies to exceed 400 MB (inputs larger
+    than L2, no host launch gaps); bytes = packed weights + scales +
+    activations + outputs."""
+    from local_kimi_b200 import ops
+
+    peak, peak_src = _peak_hbm()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    shapes = [("qkv", 2304, 12288), ("o_proj", 4096, 2304), ("shared_gate_up", 2304, 2048),
+              ("lm_head", 2304, 163840)]
+    points = []
+    for name, k, n in shapes:
+        w = (0.02 * torch.randn((n, k), generator=gen, device="cuda")).to(torch.bfloat16)
+        packed, scales = ops.quantise(w, args.group)
+        del w
+        wbytes = packed.numel() + scales.numel() * 2
+        copies = [(packed.clone(), scales.clone())
+                  for _ in range(max(1, -(-400 * 2**20 // wbytes)))]
+        for m in (1, 4, 16, 64):
+            gen_x = torch.Generator(device="cuda")
+            gen_x.manual_seed(1)
+            x = torch.randn((m, k), generator=gen_x, device="cuda").to(torch.bfloat16)
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for pk, sc in copies:
+                    ops.w4a16_dense(x, pk, sc)
+                with torch.cuda.graph(graph, stream=side):
+                    for pk, sc in copies:
+                        ops.w4a16_dense(x, pk, sc)
+            torch.cuda.current_stream().wait_stream(side)
+            for _ in range(max(args.warmup, 3)):
+                graph.replay()
+            reps = max(2, 60 // len(copies))
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            start.record()
+            for _ in range(reps):
+                graph.replay()
+            end.record()
+            torch.cuda.synchronize()
+            t = start.elapsed_time(end) / 1e3 / (reps * len(copies))
+            nbytes = wbytes + 2 * m * k + 2 * m * n
+            gbs = nbytes / t / 1e9
+            points.append({"shape": name, "K": k, "N": n, "M": m, "us": round(t * 1e6, 2),
+                           "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)})
+            del graph
+        del copies, packed, scales
+        torch.cuda.empty_cache()
+    return {"case": "dense_sweep", "group_size": args.group, "peak_gbs": peak,
+            "peak_source": peak_src, "timing": "CUDA-graph replay over weight copies > 400 MB",
+            "points": points}
+
+
 def run_case(args) -> dict:
     """One op family at full shape, launched eagerly K times after W warm-ups
     (for profilers: every launch is a separate kernel, no graph)."""
     import __graft_entry__ as entry
 
     entry.build()
+    if args.case == "dense_sweep":
+        return run_dense_sweep(args)
     from local_kimi_b200 import _lib, ops
     from local_kimi_b200.decode import HotPathDecoder, KimiLinearShape
     from local_kimi_b200.moe import moe_forward
