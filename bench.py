@@ -71,13 +71,16 @@ def _args() -> argparse.Namespace:
                     help="executor: the whole step in one persistent launch (batch <= 8); "
                          "per-op: the registry-level launches captured in a CUDA graph")
     ap.add_argument("--case",
-                    choices=("step", "lm_head", "moe", "eager", "program", "dense_sweep"),
+                    choices=("step", "lm_head", "moe", "eager", "program", "dense_sweep",
+                             "ep_moe"),
                     default="step",
                     help="step = the benchmark; the others run one op family eagerly for "
                          "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
                          "combine of one layer; eager: uncaptured decode steps); "
                          "dense_sweep: the W4A16 dense GEMV/GEMM sweep (M 1/4/16/64 over the "
-                         "QKV, o_proj, shared gate|up and lm_head shapes), HBM GB/s vs peak")
+                         "QKV, o_proj, shared gate|up and lm_head shapes), HBM GB/s vs peak; "
+                         "ep_moe: one MoE layer with its experts sharded over the torchrun "
+                         "ranks, --batch tokens in total split over them (NCCL all-to-all)")
     return ap.parse_args()
 
 
@@ -668,9 +671,90 @@ def run_case(args) -> dict:
     return out
 
 
+def run_ep_moe(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """One full-size MoE layer (256 experts + shared, hidden 2304, intermediate
+    1024, top-8, g128, random init, seeded) with the experts sharded over the
+    ranks and --batch tokens in total (batch / world per rank, random bf16
+    hidden states); K timed forwards after W warm-ups between barriers, device
+    time as the max over ranks.  Every rank runs the same collectives."""
+    import datetime
+
+    import __graft_entry__ as entry
+    import torch.distributed as dist
+
+    entry.build()
+    from local_kimi_b200 import ops
+    from local_kimi_b200.ep import ExpertParallelMoE
+    from local_kimi_b200.moe import MoELayerWeights
+
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device("cuda", local_rank))
+    E, H, I = 256, 2304, 1024
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+
+    def bank(n: int, k: int):
+        packed, scales = [], []
+        for _ in range(E + 1):
+            w = (0.02 * torch.randn((n, k), generator=gen, device="cuda")).to(torch.bfloat16)
+            p, sc = ops.quantise(w, args.group)
+            packed.append(p)
+            scales.append(sc)
+        return torch.stack(packed), torch.stack(scales)
+
+    w1 = bank(I, H)
+    w3 = bank(I, H)
+    w2 = bank(H, I)
+    router = (0.05 * torch.randn((E, H), generator=gen, device="cuda")).to(torch.bfloat16)
+    bias = 0.01 * torch.randn((E,), generator=gen, device="cuda")
+    layer = MoELayerWeights(router, bias, w1[0], w1[1], w2[0], w2[1], w3[0], w3[1])
+    ep = ExpertParallelMoE(layer)
+    del w1, w2, w3
+    torch.cuda.empty_cache()
+    if args.batch % world:
+        raise SystemExit("--batch must divide over the ranks")
+    per = args.batch // world
+    gx = torch.Generator(device="cuda")
+    gx.manual_seed(1 + rank)
+    x = torch.randn((per, H), generator=gx, device="cuda").to(torch.bfloat16)
+    for _ in range(max(args.warmup, 3)):
+        ep.forward(x)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        ep.forward(x)
+    end.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end) / 1e3 / args.steps], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    send, recv = ep.last_counts
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    step_s = float(t.item())
+    return {"case": "ep_moe", "metric": "MoE layer tokens/s (expert-parallel)",
+            "value": round(args.batch / step_s, 1), "unit": "tok/s", "n_gpus": world,
+            "ms_per_step": round(step_s * 1e3, 4), "steps": args.steps,
+            "warmup": args.warmup, "scaling": "strong",
+            "config": {"tokens": args.batch, "tokens_per_rank": per, "experts": E,
+                       "experts_per_rank": E // world, "hidden": H, "intermediate": I,
+                       "top_k": 8, "group_size": args.group,
+                       "rank0_rows_sent_per_dest": send, "rank0_rows_received": sum(recv),
+                       "data": "synthetic (random-init weights and hidden states, seeded)"}}
+
+
 def main() -> None:
     args = _args()
     rank, world, local_rank = _dist_env()
+    if args.case == "ep_moe":
+        out = run_ep_moe(args, rank, world, local_rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
     if args.case != "step":
         if rank == 0:
             print(json.dumps(run_case(args)), flush=True)

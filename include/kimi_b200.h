@@ -157,6 +157,18 @@ KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, 
                         int64_t E, int64_t N, int64_t group, uint16_t* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Routing-weighted combine of per-route outputs already in memory (the
+ * combine half of moe_combine.py:209-261, for expert parallelism, where the
+ * down projections run on the GPUs that own the experts):
+ *   out[t,n] = bf16( bf16(sum_{r<R-1} float(routes[t,r,n]) * weights[t,r])
+ *                    + routes[t,R-1,n] )
+ * fp32 sum in route order, the last route the shared expert (weight 1).
+ * routes bf16 [T,R,N] contiguous, 16-byte aligned; weights fp32 rows of
+ * stride w_stride (>= R-1); out bf16 [T,N], 16-byte aligned; N % 8 == 0. */
+KB_API int kb_moe_combine_routes(const uint16_t* routes, int64_t T, int64_t R, int64_t N,
+                                 const float* weights, int64_t w_stride, uint16_t* out,
+                                 void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Router (engine/klinear/router.py:47-85, sigmoid path, one expert group).   */
 /* logits = float(hidden) . float(W)^T; scores = sigmoid(logits);              */

@@ -423,6 +423,34 @@ def moe_down_combine(
     return _down_combine(activated, stable_indices, expert_weights, w2_packed, w2_scales, dims)
 
 
+def moe_combine_routes(routes: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """bf16(sum_r float(routes[:, r]) * weights[:, r]) + routes[:, -1], bf16 [T, N].
+
+    ``routes`` bf16 [T, R, N] holds the per-route expert outputs with the
+    shared expert last; ``weights`` fp32 [T, >= R-1] the routing weights.  The
+    combine half of fused_w2_combine, for outputs computed elsewhere (expert
+    parallelism).
+    """
+    if routes.dtype != torch.bfloat16 or routes.ndim != 3:
+        raise TypeError("routes must be BF16 [T, R, N]")
+    if weights.dtype != torch.float32 or weights.ndim != 2:
+        raise TypeError("weights must be FP32 [T, R-1]")
+    t, r, n = routes.shape
+    if weights.shape[0] != t or (r > 1 and weights.shape[1] < r - 1):
+        raise ValueError("weights must have T rows and at least R-1 columns")
+    if n % 8:
+        raise ValueError("width must be a multiple of 8")
+    _require_cuda(routes, "B200 combine")
+    out = torch.empty((t, n), dtype=torch.bfloat16, device=routes.device)
+    if t == 0:
+        return out
+    y = routes.contiguous()
+    w = weights if weights.stride(1) == 1 else weights.contiguous()
+    _lib.call("kb_moe_combine_routes", _p(y), c_int64(t), c_int64(r), c_int64(n), _p(w),
+              c_int64(w.stride(0)), _p(out), _stream(y.device))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # router
 # ---------------------------------------------------------------------------
