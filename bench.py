@@ -354,9 +354,12 @@ def _time_launches(fn, steps: int, warmup: int) -> float:
 
 
 def _max_over_ranks(value: float, dist) -> float:
+    """The largest of every rank's value (every rank gets it); NCCL groups
+    reduce on the GPU, others (gloo) on the CPU."""
     if dist is None:
         return value
-    t = torch.tensor([value], device="cuda")
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
