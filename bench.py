@@ -72,7 +72,7 @@ def _args() -> argparse.Namespace:
                          "per-op: the registry-level launches captured in a CUDA graph")
     ap.add_argument("--case",
                     choices=("step", "lm_head", "moe", "eager", "program", "dense_sweep",
-                             "ep_moe"),
+                             "ep_moe", "moe_layers"),
                     default="step",
                     help="step = the benchmark; the others run one op family eagerly for "
                          "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
@@ -80,7 +80,12 @@ def _args() -> argparse.Namespace:
                          "dense_sweep: the W4A16 dense GEMV/GEMM sweep (M 1/4/16/64 over the "
                          "QKV, o_proj, shared gate|up and lm_head shapes), HBM GB/s vs peak; "
                          "ep_moe: one MoE layer with its experts sharded over the torchrun "
-                         "ranks, --batch tokens in total split over them (NCCL all-to-all)")
+                         "ranks, --batch tokens in total split over them (NCCL all-to-all); "
+                         "moe_layers: router + gate/up + down/combine of distinct MoE layers "
+                         "back to back in one graph (--zipf S skews the expert popularity)")
+    ap.add_argument("--zipf", type=float, default=0.0,
+                    help="moe_layers: router bias giving expert e of a seeded permutation "
+                         "popularity ~ rank^-S (0: unskewed)")
     return ap.parse_args()
 
 
@@ -612,6 +617,72 @@ def run_dense_sweep(args) -> dict:
             "points": points}
 
 
+def run_moe_layers(args) -> dict:
+    """Configs C1 (--batch 1) and C3 (--batch 64 --zipf 1.1): the MoE layer
+    (router top-8 -> gate/up + SwiGLU over the routed and shared experts ->
+    down projection + weighted combine, three launches) of the distinct MoE
+    layers of a --layers model (weights > L2), captured in one CUDA graph and
+    replayed; bytes = router weights + the touched experts' three matrices.
+    With --zipf S the router bias of expert perm[j] is 0.25 (j+1)^-S (seeded
+    permutation), which skews the choices; the realised per-expert loads are
+    reported."""
+    from local_kimi_b200.decode import HotPathDecoder
+    from local_kimi_b200.moe import moe_forward
+
+    peak, peak_src = _peak_hbm()
+    model = HotPathDecoder(args.batch, group=args.group, layers=args.layers or 9)
+    moes = [lw.moe for lw in model.layers if lw.moe is not None]
+    experts = moes[0].num_experts
+    if args.zipf > 0:
+        g = torch.Generator().manual_seed(7)
+        perm = torch.randperm(experts, generator=g)
+        bias = torch.empty(experts)
+        bias[perm] = 0.25 * torch.arange(1, experts + 1, dtype=torch.float32).pow(-args.zipf)
+        for m in moes:
+            m.router_bias = bias.to(m.router_weight.device)
+    x = model.x0
+    per_matrix = [m.w1_packed[0].numel() + m.w1_scales[0].numel() * 2 for m in moes]
+    per_down = [m.w2_packed[0].numel() + m.w2_scales[0].numel() * 2 for m in moes]
+    touched, loads = [], []
+    for m in moes:
+        _, idx, _ = moe_forward(x, m)
+        cnt = torch.bincount(idx.reshape(-1), minlength=experts)
+        loads.append(cnt)
+        touched.append(int((cnt > 0).sum()) + 1)
+    nbytes = sum(t * (2 * a + b) + m.router_weight.numel() * 2
+                 for t, a, b, m in zip(touched, per_matrix, per_down, moes))
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for m in moes:
+            moe_forward(x, m)
+        with torch.cuda.graph(graph, stream=side):
+            for m in moes:
+                moe_forward(x, m)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    t = start.elapsed_time(end) / 1e3 / args.steps
+    load = torch.stack(loads)
+    gbs = nbytes / t / 1e9
+    return {"case": "moe_layers", "batch": args.batch, "group_size": args.group,
+            "zipf": args.zipf, "layers": len(moes), "steps": args.steps,
+            "us_per_layer": round(t * 1e6 / len(moes), 2),
+            "tokens_per_s_per_layer": round(args.batch * len(moes) / t, 1),
+            "touched_experts_per_layer": touched, "max_tokens_per_expert": int(load.max()),
+            "bytes_per_layer": nbytes // len(moes), "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_src,
+            "launches_per_layer": 3, "timing": "CUDA graph of all layers, replayed"}
+
+
 def run_case(args) -> dict:
     """One op family at full shape, launched eagerly K times after W warm-ups
     (for profilers: every launch is a separate kernel, no graph)."""
@@ -620,6 +691,8 @@ def run_case(args) -> dict:
     entry.build()
     if args.case == "dense_sweep":
         return run_dense_sweep(args)
+    if args.case == "moe_layers":
+        return run_moe_layers(args)
     from local_kimi_b200 import _lib, ops
     from local_kimi_b200.decode import HotPathDecoder, KimiLinearShape
     from local_kimi_b200.moe import moe_forward
