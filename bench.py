@@ -384,7 +384,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
     _lib.set_pdl(not args.no_pdl)
 
     model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
