@@ -69,6 +69,11 @@ def test_invalid_arguments_return_status_without_launching(library):
     assert status == 6  # KB_ERR_UNSUPPORTED (Dk > 256)
     with pytest.raises(_lib.KernelError, match="KB_ERR_BAD_GROUP"):
         _lib.check("kb_w4a16_dense", 3)
+    # Route combine: width not a multiple of 8, NULL routes, short weight rows.
+    assert library.kb_moe_combine_routes(None, 1, 2, 7, None, 1, None, None) == 2
+    assert library.kb_moe_combine_routes(None, 1, 2, 8, None, 1, None, None) == 1
+    assert "NULL" in _lib.last_error()
+    assert library.kb_moe_combine_routes(None, 0, 2, 8, None, 1, None, None) == 0
 
 
 def test_step_program_validation_without_gpu(library):
