@@ -179,6 +179,38 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
 
 }  // namespace kb
 
+namespace kb {
+
+// The router kernel stages up to RT_TOK rows of K <= 8192 bf16 activations in
+// dynamic shared memory (128 KiB at the limit), above the 48 KiB a launch gets
+// without opting in.  The opt-in is a per-device function attribute, so it is
+// set once for each device (with that device current), under a lock, and its
+// result is checked.
+constexpr int RT_MAX_DEVICES = 64;
+static std::mutex g_router_attr_mu;
+static bool g_router_attr_done[RT_MAX_DEVICES] = {};
+
+static int router_smem_limit() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= RT_MAX_DEVICES) {
+    set_error("router: no usable current device (%s)", cudaGetErrorString(e));
+    return KB_ERR_DEVICE;
+  }
+  std::lock_guard<std::mutex> lock(g_router_attr_mu);
+  if (g_router_attr_done[dev]) return KB_OK;
+  e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(RT_TOK * 8192 * sizeof(uint16_t)));
+  if (e != cudaSuccess) {
+    set_error("router: setting the shared-memory limit failed: %s", cudaGetErrorString(e));
+    return KB_ERR_DEVICE;
+  }
+  g_router_attr_done[dev] = true;
+  return KB_OK;
+}
+
+}  // namespace kb
+
 extern "C" size_t kb_router_workspace_size(int64_t T, int64_t E) {
   if (T <= 0 || E <= 0) return 0;
   const size_t lbytes = ((size_t)T * E * sizeof(float) + 255) / 256 * 256;
@@ -213,12 +245,8 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
   const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
                   (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
   const size_t smem = (size_t)std::min<int64_t>(T, kb::RT_TOK) * K * sizeof(uint16_t);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(kb::router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)(kb::RT_TOK * 8192 * sizeof(uint16_t)));
-    attr_done = true;
-  }
+  const int attr = kb::router_smem_limit();
+  if (attr != KB_OK) return attr;
   return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,
                     h_stride, (int)T, (int)K, weight, bias, (int)E, (int)top_k, renormalize,
                     scaling, idx_out, append_id, w_out, logits, counters);
@@ -245,6 +273,12 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
 // call before any stream capture.  All calls on one device share the one
 // scratch array, so calls that overlap in time on that device (other streams,
 // other host threads) race and give wrong results: serialise them.
+//
+// The scratch address found by the set-up is kept for the life of the process.
+// It assumes the device is not reset: after cudaDeviceReset the module (and
+// with it the array) is loaded again, possibly at another address, and the
+// kept address is stale.  A process that resets a device must not call this
+// entry point on it afterwards.
 // ---------------------------------------------------------------------------
 namespace kb {
 
@@ -279,9 +313,12 @@ static void* router_static_scratch(int* status, cudaStream_t stream) {
     *status = KB_ERR_DEVICE;
     return nullptr;
   }
-  e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)(RT_TOK * 8192 * sizeof(uint16_t)));
-  if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, RT_STATIC_COUNTER_BYTES, stream);
+  const int attr = router_smem_limit();
+  if (attr != KB_OK) {
+    *status = attr;
+    return nullptr;
+  }
+  e = cudaMemsetAsync(p, 0, RT_STATIC_COUNTER_BYTES, stream);
   if (e != cudaSuccess) {
     set_error("router (static scratch): set-up failed: %s", cudaGetErrorString(e));
     *status = KB_ERR_DEVICE;
@@ -307,12 +344,17 @@ extern "C" int kb_router_topk_static(const uint16_t* hidden, int64_t h_stride, i
              (long long)E);
   KB_REQUIRE(E <= 1024 && top_k <= 32 && K <= 8192 && K % 8 == 0, KB_ERR_UNSUPPORTED,
              "router supports E <= 1024, top_k <= 32, K <= 8192 with K %% 8 == 0");
-  KB_REQUIRE((size_t)T * (size_t)E <= kb::RT_STATIC_LOGITS &&
-                 (size_t)(T + kb::RT_TOK - 1) / kb::RT_TOK <= kb::RT_STATIC_COUNTERS,
-             KB_ERR_WORKSPACE,
+  KB_REQUIRE((size_t)T * (size_t)E <= kb::RT_STATIC_LOGITS, KB_ERR_WORKSPACE,
              "router (static scratch): T*E = %lld exceeds the fixed scratch of %zu logits; "
              "use kb_router_topk with a caller workspace",
              (long long)(T * E), kb::RT_STATIC_LOGITS);
+  KB_REQUIRE((size_t)(T + kb::RT_TOK - 1) / kb::RT_TOK <= kb::RT_STATIC_COUNTERS,
+             KB_ERR_WORKSPACE,
+             "router (static scratch): T = %lld needs %lld token blocks of %d, above the "
+             "fixed scratch's %zu arrival counters (T <= %zu); use kb_router_topk with a "
+             "caller workspace",
+             (long long)T, (long long)((T + kb::RT_TOK - 1) / kb::RT_TOK), kb::RT_TOK,
+             kb::RT_STATIC_COUNTERS, kb::RT_STATIC_COUNTERS * kb::RT_TOK);
   if (T == 0) return KB_OK;
   KB_REQUIRE(hidden && weight && idx_out && w_out, KB_ERR_NULL_POINTER, "NULL router pointer");
   KB_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0 && h_stride % 8 == 0 &&

@@ -441,6 +441,8 @@ def moe_combine_routes(routes: torch.Tensor, weights: torch.Tensor) -> torch.Ten
     if n % 8:
         raise ValueError("width must be a multiple of 8")
     _require_cuda(routes, "B200 combine")
+    if weights.device != routes.device:
+        raise ValueError("weights must be on the same CUDA device as routes")
     out = torch.empty((t, n), dtype=torch.bfloat16, device=routes.device)
     if t == 0:
         return out

@@ -34,14 +34,19 @@ class MoEBanks:
         return self.router_weight.shape[0]
 
 
-def moe_layer(hidden: torch.Tensor, banks: MoEBanks, *, return_parts: bool = False):
+def moe_layer(hidden: torch.Tensor, banks: MoEBanks, *, return_parts: bool = False,
+              lane_order: bool = False):
     """hidden bf16 [T, H] -> (output bf16 [T, H], indices [T, k], weights fp32 [T, k]).
 
     With ``return_parts`` a fourth element gives the per-element rounding bound
-    of the combine (ops.combine_rounding_bound).
+    of the combine (ops.combine_rounding_bound).  With ``lane_order`` the router
+    logits are summed in the fixed order of ops.router_logits_lanes instead of
+    the BLAS order.
     """
+    logits = (ops.router_logits_lanes(hidden, banks.router_weight) if lane_order else None)
     idx, weights, _ = ops.router_topk(
-        hidden, banks.router_weight, banks.router_bias, banks.top_k, scaling=banks.scaling
+        hidden, banks.router_weight, banks.router_bias, banks.top_k, scaling=banks.scaling,
+        logits=logits,
     )
     stable = ops.shape_stable_indices(idx, banks.num_experts)
     activated = ops.swiglu(

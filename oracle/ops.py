@@ -113,6 +113,52 @@ def router_logits(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     return F.linear(hidden.reshape(-1, hidden.shape[-1]).float(), weight.float())
 
 
+def router_logits_lanes(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """fp32 logits (engine/klinear/router.py:51) summed in one fixed, stated order.
+
+    The reference's F.linear leaves the order of the fp32 sum to the BLAS.
+    This restatement fixes it to the order the B200 router kernels use, so
+    that their logits -- and with them the top-k indices -- can be compared
+    bit for bit:
+
+    * the row of K bf16 values is cut into 16-byte words of 8 values; word w
+      belongs to lane w mod 32 of a 32-lane group, and each lane visits its
+      words in increasing order;
+    * a lane keeps four partial sums, one per value pair j of a word; values
+      2j and 2j+1 are added to partial j in that order (each bf16 x bf16
+      product is exact in fp32, so a fused multiply-add is one rounded add);
+    * the lane's total is (p0 + p1) + (p2 + p3);
+    * the 32 lane totals are combined by a butterfly: lane l adds lane
+      l xor 16, then l xor 8, 4, 2, 1; the result is lane 0's value.
+    """
+    h = hidden.reshape(-1, hidden.shape[-1]).float()
+    w = weight.float()
+    t, k = h.shape
+    e = w.shape[0]
+    words = k // 8
+    per_lane = -(-words // 32)
+    pad = per_lane * 32 * 8 - k
+    if pad:
+        h = F.pad(h, (0, pad))
+        w = F.pad(w, (0, pad))
+    # [T or E, per_lane, 32 lanes, 4 pairs, 2 values]
+    hv = h.view(t, per_lane, 32, 4, 2)
+    wv = w.view(e, per_lane, 32, 4, 2)
+    out = torch.empty((t, e), dtype=torch.float32)
+    for ti in range(t):
+        prod = hv[ti].unsqueeze(0) * wv                       # exact in fp32
+        acc = torch.zeros((e, 32, 4), dtype=torch.float32)
+        for i in range(per_lane):
+            acc = acc + prod[:, i, :, :, 0]
+            acc = acc + prod[:, i, :, :, 1]
+        lane = (acc[..., 0] + acc[..., 1]) + (acc[..., 2] + acc[..., 3])   # [E, 32]
+        idx = torch.arange(32)
+        for o in (16, 8, 4, 2, 1):
+            lane = lane + lane[:, idx ^ o]
+        out[ti] = lane[:, 0]
+    return out
+
+
 def router_topk(
     hidden: torch.Tensor,
     weight: torch.Tensor,

@@ -68,7 +68,8 @@ def test_moe_layer_matches_oracle(cuda, tokens, group, skew):
     out, idx, w = kmoe.moe_forward(hidden, layer)
     used = torch.unique(torch.cat((idx.flatten().cpu(), torch.tensor([256]))))
     banks = _oracle_layer(layer, used)
-    ref_out, ref_idx, ref_w, bound = omoe.moe_layer(hidden.cpu(), banks, return_parts=True)
+    ref_out, ref_idx, ref_w, bound = omoe.moe_layer(hidden.cpu(), banks, return_parts=True,
+                                                    lane_order=True)
     assert torch.equal(idx.cpu(), ref_idx), "router indices differ"
     torch.testing.assert_close(w.cpu(), ref_w, rtol=1e-5, atol=1e-6)
     # Where the routed sum and the shared output cancel, each element is also

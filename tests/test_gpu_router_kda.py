@@ -36,22 +36,51 @@ def test_router_matches_reference_golden(cuda, golden):
     torch.testing.assert_close(sw, golden["router.w_sorted"], rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("tokens", [1, 32, 64])
-def test_router_decode_shape_bit_exact_indices(cuda, tokens):
-    weight = rand_weight((256, 2304), cuda_gen(0))
+def _router_with_logits(hidden, weight, bias, top_k, scaling):
+    """kb_router_topk through the C ABI with a caller workspace, so that the
+    fp32 logits it leaves at the start of the workspace can be read back."""
+    from ctypes import c_float, c_int64, c_size_t, c_void_p
+
+    from local_kimi_b200 import _lib
+
+    tokens, width = hidden.shape
+    experts = weight.shape[0]
+    need = int(_lib.lib().kb_router_workspace_size(tokens, experts))
+    ws = torch.zeros(need, dtype=torch.uint8, device=hidden.device)
+    idx = torch.empty((tokens, top_k), dtype=torch.long, device=hidden.device)
+    wts = torch.empty((tokens, top_k), dtype=torch.float32, device=hidden.device)
+    _lib.call("kb_router_topk", c_void_p(hidden.data_ptr()), c_int64(hidden.stride(0)),
+              c_int64(tokens), c_int64(width), c_void_p(weight.data_ptr()),
+              c_void_p(bias.data_ptr()), c_int64(experts), c_int64(top_k), 1, c_float(scaling),
+              c_void_p(idx.data_ptr()), c_int64(-1), c_void_p(wts.data_ptr()),
+              c_void_p(ws.data_ptr()), c_size_t(need),
+              c_void_p(torch.cuda.current_stream(hidden.device).cuda_stream))
+    logits = ws[: tokens * experts * 4].view(torch.float32).view(tokens, experts)
+    return idx, wts, logits
+
+
+@pytest.mark.parametrize("tokens,width,seed", [(1, 2304, 0), (32, 2304, 0), (64, 2304, 0),
+                                               (200, 2304, 5), (16, 7168, 6), (9, 520, 7)])
+def test_router_bit_exact_logits_and_indices(cuda, tokens, width, seed):
+    # The oracle sums the logits in the kernel's stated lane order
+    # (oracle.ops.router_logits_lanes), so logits and indices must be
+    # identical, with no near-tie exemption.  Widths cover whole lane rounds
+    # (2304 = 9 x 32 words), a long row (7168) and a ragged last round (520).
+    weight = rand_weight((256, width), cuda_gen(seed))
     bias = (torch.randn(256, generator=torch.Generator().manual_seed(4)) * 1e-3).to(cuda)
-    hidden = rand_act((tokens, 2304), cuda_gen(1))
-    idx, w = ops.moe_router(hidden, weight, bias, 8, routed_scaling_factor=2.446)
-    ridx, rw, choice = oref.router_topk(hidden.cpu(), weight.cpu(), bias.cpu(), 8, scaling=2.446)
-    # Order is (choice desc, index asc) in both; logits differ only by fp32
-    # summation order, so indices must agree exactly unless the oracle's
-    # k-th and (k+1)-th choices are within a rounding of each other.
-    top = torch.sort(choice, dim=-1, descending=True).values
-    gap = (top[:, 7] - top[:, 8]).abs()
-    clear = gap > 1e-6
-    assert torch.equal(idx.cpu()[clear], ridx[clear])
-    torch.testing.assert_close(w.cpu()[clear], rw[clear], rtol=1e-5, atol=1e-6)
-    assert int(clear.sum()) >= tokens - 1
+    hidden = rand_act((tokens, width), cuda_gen(seed + 1))
+    idx, w, logits = _router_with_logits(hidden, weight, bias, 8, 2.446)
+    ref_logits = oref.router_logits_lanes(hidden.cpu(), weight.cpu())
+    assert torch.equal(logits.cpu(), ref_logits)
+    ridx, rw, _ = oref.router_topk(hidden.cpu(), weight.cpu(), bias.cpu(), 8, scaling=2.446,
+                                   logits=ref_logits)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, rtol=1e-5, atol=1e-6)
+    # The torch-facing op gives the same routing, shared route appended.
+    sidx, sw = ops.moe_router(hidden, weight, bias, 8, routed_scaling_factor=2.446,
+                              append_expert=256)
+    assert torch.equal(sidx[:, :8], idx) and bool((sidx[:, 8] == 256).all())
+    assert torch.equal(sw, w)
 
 
 def test_router_ties_go_to_lower_index_and_nan_stays_in_range(cuda):

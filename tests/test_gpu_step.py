@@ -107,7 +107,8 @@ def test_step_moe_layer_matches_oracle_and_per_op(cuda, tokens):
 
     used = torch.unique(torch.cat((idx.flatten().cpu(), torch.tensor([256]))))
     banks = _oracle_banks(layer, used)
-    ref_out, ref_idx, ref_wts, bound = omoe.moe_layer(h.cpu(), banks, return_parts=True)
+    ref_out, ref_idx, ref_wts, bound = omoe.moe_layer(h.cpu(), banks, return_parts=True,
+                                                     lane_order=True)
     assert torch.equal(idx[:, :8].cpu(), ref_idx)
     torch.testing.assert_close(wts.cpu(), ref_wts, rtol=1e-5, atol=1e-6)
     assert_close(out, ref_out, what=f"step moe T={tokens}", allowance=bound)
@@ -185,3 +186,64 @@ def test_step_program_matches_per_op_step(cuda, batch):
     for idx in buf["idx"]:
         assert int(idx.min()) >= 0 and int(idx[:, :-1].max()) < model.shape.experts
         assert bool((idx[:, -1] == model.shape.experts).all())
+
+
+def _oracle_model(model: HotPathDecoder, states: list) -> list:
+    from oracle.decode import OracleLayer
+
+    def cpu(pair):
+        return (pair[0].cpu(), pair[1].cpu())
+
+    layers = []
+    for lw, st in zip(model.layers, states):
+        ol = OracleLayer(kind=lw.kind)
+        if lw.kind == "kda":
+            ol.qkv = [cpu(p) for p in lw.qkv]
+            ol.kda_state = st.cpu().clone()
+        else:
+            ol.q_proj, ol.kv_b = cpu(lw.q_proj), cpu(lw.kv_b)
+        ol.o_proj = cpu(lw.o_proj)
+        if lw.dense_mlp is not None:
+            (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
+            ol.dense_mlp = ((w1p[0].cpu(), w1s[0].cpu()), (w3p[0].cpu(), w3s[0].cpu()),
+                            (w2p.cpu(), w2s.cpu()))
+        else:
+            m = lw.moe
+            ol.moe = omoe.MoEBanks(m.router_weight.cpu(), m.router_bias.cpu(),
+                                   m.w1_packed.cpu(), m.w1_scales.cpu(), m.w2_packed.cpu(),
+                                   m.w2_scales.cpu(), m.w3_packed.cpu(), m.w3_scales.cpu(),
+                                   m.top_k, m.scaling)
+        layers.append(ol)
+    return layers
+
+
+@pytest.mark.parametrize("batch", [1, 5])
+def test_step_program_matches_oracle_chain(cuda, batch):
+    # The whole multi-layer program against the CPU oracle chained layer by
+    # layer (oracle.decode): routing of every MoE layer exact, KDA states at
+    # the reference's single-step tolerance, logits at the north-star
+    # tolerance.
+    from oracle.decode import StepTrace, decode_step
+
+    model = HotPathDecoder(batch, shape=_small_shape(), seed=7)
+    x = model.x0.clone()
+    states = [lw.kda_state.clone() if lw.kda_state is not None else None for lw in model.layers]
+    layers = _oracle_model(model, states)
+    prog, buf = model.build_program(x)
+    prog.launch()
+    torch.cuda.synchronize()
+    inputs = {"kda_q": model.kda_q.cpu(), "kda_k": model.kda_k.cpu(), "kda_v": model.kda_v.cpu(),
+              "kda_decay": model.kda_decay.cpu(), "kda_beta": model.kda_beta.cpu(),
+              "mla_latent": model.mla_latent.cpu(), "mla_attn": model.mla_attn.cpu()}
+    trace = StepTrace()
+    ref_logits = decode_step(layers, (model.lm_head[0].cpu(), model.lm_head[1].cpu()), inputs,
+                             x.cpu(), kda_scale=model.shape.kda_head_dim ** -0.5, trace=trace)
+    for lw, ol in zip(model.layers, layers):
+        if lw.kda_state is not None:
+            torch.testing.assert_close(lw.kda_state.cpu(), ol.kda_state, rtol=3e-5, atol=3e-5)
+    assert len(buf["idx"]) == len(trace.routes)
+    for idx, wts, ref_idx, ref_w in zip(buf["idx"], buf["weights"], trace.routes,
+                                        trace.weights):
+        assert torch.equal(idx[:, :-1].cpu(), ref_idx)
+        torch.testing.assert_close(wts.cpu(), ref_w, rtol=1e-5, atol=1e-6)
+    assert_close(buf["logits"], ref_logits, what=f"program logits vs oracle B={batch}")

@@ -161,6 +161,37 @@ def test_router_matches_reference(golden):
                                rtol=1e-6, atol=1e-7)
 
 
+def test_lane_order_router_matches_reference(golden):
+    # The fixed lane summation order changes the logits only in the last fp32
+    # bits of the BLAS sum; it routes the reference's golden tokens the same.
+    lanes = ops.router_logits_lanes(golden["router.hidden"], golden["router.weight"])
+    blas = ops.router_logits(golden["router.hidden"], golden["router.weight"])
+    torch.testing.assert_close(lanes, blas, rtol=1e-5, atol=1e-5)
+    idx, w, _ = ops.router_topk(golden["router.hidden"], golden["router.weight"],
+                                golden["router.bias"], 4, scaling=2.446, logits=lanes)
+    order = torch.argsort(idx, dim=-1)
+    assert torch.equal(torch.gather(idx, 1, order), golden["router.idx_sorted"])
+    torch.testing.assert_close(torch.gather(w, 1, order), golden["router.w_sorted"],
+                               rtol=1e-6, atol=1e-6)
+
+
+def test_lane_order_logits_follow_the_stated_order():
+    # A row whose exact sum depends on the order: large terms that cancel
+    # with small ones between them.  The stated order is computed here by
+    # hand for K = 512 (64 words, two per lane).
+    k = 512
+    h = torch.ones((1, k), dtype=torch.bfloat16)
+    w = torch.zeros((1, k), dtype=torch.bfloat16)
+    w[0, 0] = 2.0 ** 24          # word 0, lane 0, pair 0, first value
+    w[0, 1] = 1.0                # lost against 2^24 in the same partial sum
+    w[0, 8 * 32] = -(2.0 ** 24)  # word 32: lane 0 again, pair 0
+    w[0, 2] = 1.0                # pair 1 of word 0: its own partial, kept
+    got = ops.router_logits_lanes(h, w)
+    # partial 0: (2^24 + 1) rounds to 2^24, then - 2^24 -> 0; partial 1 = 1.
+    assert got.item() == 1.0
+    assert float((h.double() * w.double()).sum()) == 2.0   # the exact sum differs
+
+
 def test_router_known_answer_and_tie_break():
     # tests/test_klinear_forward.py:43-75 of the reference
     weight = torch.tensor([[3.0, 0.0], [2.0, 0.0], [1.0, 0.0], [0.0, 0.0]]).to(torch.bfloat16)
