@@ -559,19 +559,61 @@ def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
+def _peak_tflops() -> tuple[float, str]:
+    try:
+        data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(data["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def _time_copies(fn, x, copies, warmup: int) -> float:
+    """Seconds per call of fn(x, packed, scales), replayed as one CUDA graph over
+    weight copies larger than L2."""
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for pk, sc in copies:
+            fn(x, pk, sc)
+        with torch.cuda.graph(graph, stream=side):
+            for pk, sc in copies:
+                fn(x, pk, sc)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    reps = max(2, 60 // len(copies))
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    del graph
+    return start.elapsed_time(end) / 1e3 / (reps * len(copies))
+
+
 def run_dense_sweep(args) -> dict:
     """The dense W4A16 sweep: y[M,N] = x[M,K] . dequant(W)^T for the decode
-    shapes at M in {1, 4, 16, 64}, group args.group.  Each point replays a CUDA
-    graph of calls over enough weight copies to exceed 400 MB (inputs larger
-    than L2, no host launch gaps); bytes = packed weights + scales +
-    activations + outputs."""
+    shapes, group args.group.  The projection engine (path "gemv") at M in
+    {1, 4, 16, 64} and the tcgen05 tensor-core path (path "tc") at M in
+    {16, 32, 64, 128, 256}.  Each point replays a CUDA graph of calls over
+    enough weight copies to exceed 400 MB (inputs larger than L2, no host
+    launch gaps); bytes = packed weights + scales + activations + outputs;
+    the tc points also give the tensor-pipe fraction (2 M N K flops over the
+    measured bf16 peak)."""
     from local_kimi_b200 import ops
 
     peak, peak_src = _peak_hbm()
+    tpeak, tpeak_src = _peak_tflops()
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0)
     shapes = [("qkv", 2304, 12288), ("o_proj", 4096, 2304), ("shared_gate_up", 2304, 2048),
               ("lm_head", 2304, 163840)]
+    paths = [("gemv", ops.w4a16_dense, (1, 4, 16, 64)),
+             ("tc", ops.w4a16_dense_tc, (16, 32, 64, 128, 256))]
     points = []
     for name, k, n in shapes:
         w = (0.02 * torch.randn((n, k), generator=gen, device="cuda")).to(torch.bfloat16)
@@ -580,42 +622,25 @@ def run_dense_sweep(args) -> dict:
         wbytes = packed.numel() + scales.numel() * 2
         copies = [(packed.clone(), scales.clone())
                   for _ in range(max(1, -(-400 * 2**20 // wbytes)))]
-        for m in (1, 4, 16, 64):
-            gen_x = torch.Generator(device="cuda")
-            gen_x.manual_seed(1)
-            x = torch.randn((m, k), generator=gen_x, device="cuda").to(torch.bfloat16)
-            graph = torch.cuda.CUDAGraph()
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                for pk, sc in copies:
-                    ops.w4a16_dense(x, pk, sc)
-                with torch.cuda.graph(graph, stream=side):
-                    for pk, sc in copies:
-                        ops.w4a16_dense(x, pk, sc)
-            torch.cuda.current_stream().wait_stream(side)
-            for _ in range(max(args.warmup, 3)):
-                graph.replay()
-            reps = max(2, 60 // len(copies))
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            start.record()
-            for _ in range(reps):
-                graph.replay()
-            end.record()
-            torch.cuda.synchronize()
-            t = start.elapsed_time(end) / 1e3 / (reps * len(copies))
-            nbytes = wbytes + 2 * m * k + 2 * m * n
-            gbs = nbytes / t / 1e9
-            points.append({"shape": name, "K": k, "N": n, "M": m, "us": round(t * 1e6, 2),
-                           "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)})
-            del graph
+        for path, fn, ms in paths:
+            for m in ms:
+                gen_x = torch.Generator(device="cuda")
+                gen_x.manual_seed(1)
+                x = torch.randn((m, k), generator=gen_x, device="cuda").to(torch.bfloat16)
+                t = _time_copies(fn, x, copies, args.warmup)
+                nbytes = wbytes + 2 * m * k + 2 * m * n
+                gbs = nbytes / t / 1e9
+                pt = {"shape": name, "K": k, "N": n, "M": m, "path": path,
+                      "us": round(t * 1e6, 2), "gbs": round(gbs, 1),
+                      "frac_of_peak": round(gbs / peak, 4)}
+                if path == "tc":
+                    pt["tensor_frac"] = round(2.0 * m * n * k / t / 1e12 / tpeak, 4)
+                points.append(pt)
         del copies, packed, scales
         torch.cuda.empty_cache()
     return {"case": "dense_sweep", "group_size": args.group, "peak_gbs": peak,
-            "peak_source": peak_src, "timing": "CUDA-graph replay over weight copies > 400 MB",
-            "points": points}
+            "peak_source": peak_src, "peak_bf16_tflops": tpeak, "tflops_source": tpeak_src,
+            "timing": "CUDA-graph replay over weight copies > 400 MB", "points": points}
 
 
 def run_moe_layers(args) -> dict:

@@ -136,6 +136,44 @@ KB_API int kb_w4a16_swiglu(const uint16_t* x, int64_t x_stride, int64_t T, int64
                     const uint16_t* w3_scales, int64_t E, int64_t N, int64_t group,
                     uint16_t* y, void* stream);
 
+/* ------------------------------------------------------------------------- */
+/* Tensor-core (tcgen05/TMEM) forms of the projections for many tokens.        */
+/* Replace the tensor-core W4A16 GEMM the reference falls back to for every    */
+/* M > 1 dense call (engine/quant/triton_w4a16.py:44-124, dispatched at        */
+/* engine/kernels/w4a16_dense_gemv.py:327-331) and, for expert groups of many  */
+/* rows, the grouped/SwiGLU ops above (engine/kernels/w4a16_grouped.py:121-194,*/
+/* engine/kernels/__init__.py:182-197).  Same arguments, layouts and results   */
+/* as kb_w4a16_dense / kb_w4a16_grouped / kb_w4a16_swiglu (decoded weights     */
+/* bf16(code*scale), fp32 accumulation, bf16 outputs); the reduction order     */
+/* inside the tensor core differs, so outputs agree within rounding.           */
+/* Limits: K % 64 == 0, N % 8 == 0, x row stride % 8 == 0, 16-byte aligned     */
+/* pointers, K/group small enough for the per-CTA scale buffers (at most 81    */
+/* groups per row), grouped T*R <= KB_MAX_ASSIGNMENTS and E <= 520; outside    */
+/* them the call returns KB_ERR_UNSUPPORTED without launching.  y of the       */
+/* grouped forms is bf16 [T*R, N] contiguous.                                  */
+/* ------------------------------------------------------------------------- */
+/* The dense form splits the reduction axis over several CTAs when the matrix
+ * has too few 256-row tiles to fill the GPU; the splits' fp32 partials are
+ * summed in split order by the last CTA of each tile (deterministic).  Its
+ * workspace (kb_w4a16_dense_tc_workspace_size bytes, 0 when no split is
+ * made) must be 256-byte aligned and zero-filled before its first use; every
+ * launch leaves its counters at zero again.  Calls that share a workspace
+ * must not overlap on the GPU. */
+KB_API size_t kb_w4a16_dense_tc_workspace_size(int64_t M, int64_t K, int64_t N);
+KB_API int kb_w4a16_dense_tc(const uint16_t* x, int64_t x_stride, int64_t M, int64_t K,
+                             const uint8_t* packed, const uint16_t* scales, int64_t N,
+                             int64_t group, uint16_t* y, int64_t y_stride, void* workspace,
+                             size_t workspace_bytes, void* stream);
+KB_API int kb_w4a16_grouped_tc(const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
+                               const int64_t* idx, int64_t R, const uint8_t* packed,
+                               const uint16_t* scales, int64_t E, int64_t N, int64_t group,
+                               uint16_t* y, void* stream);
+KB_API int kb_w4a16_swiglu_tc(const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
+                              const int64_t* idx, int64_t R, const uint8_t* w1_packed,
+                              const uint16_t* w1_scales, const uint8_t* w3_packed,
+                              const uint16_t* w3_scales, int64_t E, int64_t N, int64_t group,
+                              uint16_t* y, void* stream);
+
 /* Down projection + routing-weighted combine.  Replaces `fused_w2_combine`
  * (engine/kernels/moe_combine.py:264-324; reference sequence
  * engine/klinear/moe.py:317-334 and moe_combine.py:209-261):

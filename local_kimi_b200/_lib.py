@@ -74,6 +74,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     ),
+    "kb_w4a16_dense_tc_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
+    "kb_w4a16_dense_tc": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+         c_int64, c_void_p, c_size_t, c_void_p],
+    ),
+    "kb_w4a16_grouped_tc": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+         c_int64, c_int64, c_void_p, c_void_p],
+    ),
+    "kb_w4a16_swiglu_tc": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
+    ),
     "kb_w4a16_w2_combine_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "kb_w4a16_w2_combine": (
         c_int,

@@ -204,6 +204,30 @@ def fused_qkv_w4a16(
     return q, k, v
 
 
+def w4a16_dense_tc(
+    activations: torch.Tensor, packed_weights: torch.Tensor, scales: torch.Tensor,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """w4a16_dense on the tcgen05 tensor-core path (many tokens); same result contract."""
+    m, n, k, group = _validate_dense(activations, packed_weights, scales)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=activations.device)
+    if m == 0:
+        return out
+    x = _rows_16b(activations)
+    packed = _dense_contig(packed_weights)
+    sc = _dense_contig(scales)
+    need = int(_lib.lib().kb_w4a16_dense_tc_workspace_size(m, k, n))
+    ws = _workspace("dense_tc", x.device, need, (m, k, n)) if need else None
+    _lib.call(
+        "kb_w4a16_dense_tc",
+        _p(x), c_int64(x.stride(0)), c_int64(m), c_int64(k), _p(packed), _p(sc), c_int64(n),
+        c_int64(group), _p(out), c_int64(out.stride(0)), _p(ws),
+        c_size_t(0 if ws is None else ws.numel()), _stream(x.device),
+    )
+    return out
+
+
 # ---------------------------------------------------------------------------
 # grouped
 # ---------------------------------------------------------------------------
@@ -270,6 +294,60 @@ def w4a16_grouped(
         "kb_w4a16_grouped",
         _p(x), c_int64(x.stride(0)), c_int64(t), c_int64(k), _p(idx), c_int64(r), _p(packed),
         _p(sc), c_int64(e), c_int64(n), c_int64(group), _p(out), _stream(x.device),
+    )
+    return out
+
+
+def w4a16_grouped_tc(
+    activations: torch.Tensor,
+    expert_indices: torch.Tensor,
+    packed_weights: torch.Tensor,
+    scales: torch.Tensor,
+) -> torch.Tensor:
+    """w4a16_grouped on the tcgen05 tensor-core path; same result contract."""
+    t, r, n, k, e, group = _validate_grouped(activations, expert_indices, packed_weights, scales)
+    out = torch.empty((t, r, n), dtype=torch.bfloat16, device=activations.device)
+    if t == 0:
+        return out
+    x = _rows_16b(activations)
+    idx = _dense_contig(expert_indices)
+    packed = _dense_contig(packed_weights)
+    sc = _dense_contig(scales)
+    _lib.call(
+        "kb_w4a16_grouped_tc",
+        _p(x), c_int64(x.stride(0)), c_int64(t), c_int64(k), _p(idx), c_int64(r), _p(packed),
+        _p(sc), c_int64(e), c_int64(n), c_int64(group), _p(out), _stream(x.device),
+    )
+    return out
+
+
+def w4a16_swiglu_tc(
+    activations: torch.Tensor,
+    expert_indices: torch.Tensor,
+    w1_packed: torch.Tensor,
+    w1_scales: torch.Tensor,
+    w3_packed: torch.Tensor,
+    w3_scales: torch.Tensor,
+) -> torch.Tensor:
+    """w4a16_swiglu on the tcgen05 tensor-core path; same rounding contract."""
+    dims = _validate_grouped(activations, expert_indices, w1_packed, w1_scales)
+    if _validate_grouped(activations, expert_indices, w3_packed, w3_scales) != dims:
+        raise ValueError("grouped W1 and W3 dimensions must match")
+    if w3_packed.shape != w1_packed.shape or w3_scales.shape != w1_scales.shape:
+        raise ValueError("grouped W1 and W3 shapes must match")
+    t, r, n, k, e, group = dims
+    out = torch.empty((t, r, n), dtype=torch.bfloat16, device=activations.device)
+    if t == 0:
+        return out
+    x = _rows_16b(activations)
+    idx = _dense_contig(expert_indices)
+    p1, s1 = _dense_contig(w1_packed), _dense_contig(w1_scales)
+    p3, s3 = _dense_contig(w3_packed), _dense_contig(w3_scales)
+    _lib.call(
+        "kb_w4a16_swiglu_tc",
+        _p(x), c_int64(x.stride(0)), c_int64(t), c_int64(k), _p(idx), c_int64(r), _p(p1),
+        _p(s1), _p(p3), _p(s3), c_int64(e), c_int64(n), c_int64(group), _p(out),
+        _stream(x.device),
     )
     return out
 
