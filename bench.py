@@ -83,6 +83,8 @@ def _args() -> argparse.Namespace:
                          "ranks, --batch tokens in total split over them (NCCL all-to-all); "
                          "moe_layers: router + gate/up + down/combine of distinct MoE layers "
                          "back to back in one graph (--zipf S skews the expert popularity)")
+    ap.add_argument("--wide-sweep", action="store_true",
+                    help="dense_sweep: also the MLA and dense-MLP shapes, both paths at every M")
     ap.add_argument("--zipf", type=float, default=0.0,
                     help="moe_layers: router bias giving expert e of a seeded permutation "
                          "popularity ~ rank^-S (0: unskewed)")
@@ -612,8 +614,12 @@ def run_dense_sweep(args) -> dict:
     gen.manual_seed(0)
     shapes = [("qkv", 2304, 12288), ("o_proj", 4096, 2304), ("shared_gate_up", 2304, 2048),
               ("lm_head", 2304, 163840)]
-    paths = [("gemv", ops.w4a16_dense, (1, 4, 16, 64)),
-             ("tc", ops.w4a16_dense_tc, (16, 32, 64, 128, 256))]
+    gemv_ms, tc_ms = (1, 4, 16, 64), (16, 32, 64, 128, 256)
+    if args.wide_sweep:
+        shapes += [("mla_q", 2304, 6144), ("mla_kv_b", 512, 8192), ("dense_up", 2304, 9216),
+                   ("dense_down", 9216, 2304)]
+        gemv_ms, tc_ms = (1, 4, 16, 32, 64, 128, 256), (16, 32, 64, 128, 256)
+    paths = [("gemv", ops.w4a16_dense, gemv_ms), ("tc", ops.w4a16_dense_tc, tc_ms)]
     points = []
     for name, k, n in shapes:
         w = (0.02 * torch.randn((n, k), generator=gen, device="cuda")).to(torch.bfloat16)

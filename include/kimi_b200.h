@@ -116,8 +116,10 @@ KB_API int kb_w4a16_dense_multi(const kb_dense_problem* problems, int count, voi
 /* r < R.  x: bf16 [T,K] (row stride x_stride); idx: int64 [T,R] contiguous;   */
 /* packed: uint8 [E,N,K/2]; scales: bf16 [E,N,K/group]; y: bf16 [T,R,N]        */
 /* contiguous.  Assignments sharing an expert read that expert's weights once. */
-/* An index outside [0,E) is computed as expert 0 (never read out of bounds)  */
-/* and sets device error bit 0.  T*R must not exceed KB_MAX_ASSIGNMENTS.        */
+/* An index of -1 marks an empty slot: it is skipped (no output row written). */
+/* Any other index outside [0,E) is computed as expert 0 (never read out of   */
+/* bounds) and sets device error bit 0.  T*R must not exceed                  */
+/* KB_MAX_ASSIGNMENTS.                                                         */
 /* ------------------------------------------------------------------------- */
 #define KB_MAX_ASSIGNMENTS 4096
 KB_API int kb_w4a16_grouped(const uint16_t* x, int64_t x_stride, int64_t T, int64_t K,
@@ -206,6 +208,35 @@ KB_API int kb_w4a16_w2_combine(const uint16_t* activated, int64_t T, int64_t R, 
 KB_API int kb_moe_combine_routes(const uint16_t* routes, int64_t T, int64_t R, int64_t N,
                                  const float* weights, int64_t w_stride, uint16_t* out,
                                  void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Expert-parallel data plane (the layer of engine/klinear/moe.py:278-334 with */
+/* its experts sharded over ranks: expert e on rank e / per_rank).  Fixed-     */
+/* capacity exchange buffers, so no step needs a host-side count and the layer */
+/* can be captured in a CUDA graph.                                            */
+/*                                                                             */
+/* kb_ep_dispatch: for the routed pairs idx[t, r] (int64, row stride           */
+/* idx_stride, r < k) in token-major order, the destination rank d and the     */
+/* pair's position p among the pairs bound for d (stable); copies hidden[t]    */
+/* (bf16, row stride h_stride, H % 8 == 0) to payload row d * capacity + p of  */
+/* send_rows, bf16 [world * capacity, H + 8]: H values, then the owner-local   */
+/* expert id as an int64 (4 bf16 slots) and 4 bf16 of padding, so rows and ids */
+/* travel in one exchange; unused slots carry id -1 (the grouped kernels skip  */
+/* them).  slots[t * k + r] = d * capacity + p, int32 [T * k].                 */
+/* capacity >= T * k (then nothing can overflow); T * k <= 8192, world <= 64.  */
+/*                                                                             */
+/* kb_ep_combine: out[t] = bf16( bf16(sum_{r<k} float(y[slots[t*k+r]]) *       */
+/* weights[t, r]) + shared[t] ), fp32 sum in route order (the combine of       */
+/* engine/kernels/moe_combine.py:209-261); y bf16 rows of width H.             */
+/* ------------------------------------------------------------------------- */
+KB_API int kb_ep_dispatch(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t H,
+                          const int64_t* idx, int64_t idx_stride, int64_t k, int64_t per_rank,
+                          int64_t world, int64_t capacity, uint16_t* send_rows,
+                          int32_t* slots, void* stream);
+KB_API int kb_ep_combine(const uint16_t* y, const int32_t* slots, int64_t T, int64_t k,
+                         int64_t H, const float* weights, int64_t w_stride,
+                         const uint16_t* shared, int64_t shared_stride, uint16_t* out,
+                         int64_t out_stride, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* Router (engine/klinear/router.py:47-85, sigmoid path, one expert group).   */

@@ -99,6 +99,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kb_moe_combine_routes": (
         c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "kb_ep_dispatch": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
+         c_int64, c_void_p, c_void_p, c_void_p],
+    ),
+    "kb_ep_combine": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+         c_void_p, c_int64, c_void_p],
+    ),
     "kb_router_workspace_size": (c_size_t, [c_int64, c_int64]),
     "kb_router_topk": (
         c_int,

@@ -203,6 +203,11 @@ __device__ __forceinline__ void stage_row(uint8_t* xs_row, const uint16_t* src, 
   }
 }
 
+// Expert index of an empty assignment slot in the grouped and SwiGLU modes
+// (fixed-capacity exchange buffers of the expert-parallel layer): the slot is
+// skipped -- no weights read for it, no output row written.
+constexpr int64_t EXPERT_NONE = -1;
+
 __device__ __forceinline__ int clamp_expert(int64_t v, int E, uint32_t* err) {
   if (v < 0 || v >= E) {
     atomicOr(err, ERR_INDEX);

@@ -13,31 +13,40 @@
 // One persistent CTA per SM (24 warps) walks work units.  A unit is two
 // 128-row weight tiles -- rows [256 rt, 256 rt + 256) of one matrix (dense and
 // grouped modes) or the same 128 rows of the gate and up matrices (SwiGLU
-// mode) -- times up to NT token rows (one expert's rows in the grouped modes),
-// over the whole reduction axis in 64-wide k-chunks:
+// mode) -- times up to 64 token rows (one expert's rows in the grouped modes),
+// over the reduction axis (or one split of it) in 64-wide k-chunks:
 //
 //   warp 0 (lane 0): TMA producer.  Packed codes of both tiles, one 2-D tiled
 //     bulk tensor copy of 128 rows x 32 bytes per tile and k-chunk (plain, no
-//     multicast, L2 evict-first), into a ring of SW stages; the unit's bf16
-//     scales (rows contiguous) with one bulk copy per tile into a double
-//     buffer.
+//     multicast, L2 evict-first), into a ring of SW shared-memory stages; the
+//     unit's bf16 scales (rows contiguous) with one bulk copy per tile into a
+//     double buffer.
 //   warps 1, 3: activation loaders.  16-byte cp.async pieces of the unit's
 //     token rows (gathered through the expert plan in the grouped modes),
 //     written straight into the 128-byte-swizzled K-major layout the tensor
-//     core reads, into a ring of SA stages shared with the decoded weights.
-//   warps 8-23: decoders.  Two threads per weight row turn 32 packed bytes per
-//     k-chunk into bf16(code * scale) in k order (17 instructions per 8
-//     weights: one shift, four byte permutes, four LOP3s, four exact bf16x2
+//     core reads as its B operand, into a ring of SX stages; each stage is
+//     signalled by the copies' own completion (cp.async.mbarrier.arrive).
+//   warps 8-23: decoders, four per TMEM lane quarter (a warp reaches only the
+//     32 lanes of its quarter).  A thread turns 16 packed bytes of its row into
+//     32 weights bf16(code * scale) in k order (17 instructions per 8 weights:
+//     one shift, four byte permutes, four LOP3s, four exact bf16x2
 //     subtractions and four bf16x2 multiplies -- the one rounding of the
-//     reference) and store them 16 bytes at a time in the swizzled layout.
-//   warp 2 (lane 0): MMA issuer.  Four tcgen05.mma (M 128, N = tokens rounded
-//     up to 16, K 16, bf16 x bf16 -> fp32) per tile and k-chunk into a TMEM
-//     accumulator; tcgen05.commit frees each stage and, after the unit's last
-//     chunk, publishes the accumulator (two accumulator buffers, so the next
-//     unit's products overlap this unit's epilogue).
+//     reference) and writes them with one tcgen05.st into a ring of four
+//     decoded-weight stages held in tensor memory.
+//   warp 2 (lane 0): MMA issuer.  Per k-chunk, four tcgen05.mma per tile with
+//     A (the decoded weights) read from TMEM and B (the activations) from
+//     shared memory: M 128, N = tokens rounded up to 16, K 16, bf16 x bf16 ->
+//     fp32 into a TMEM accumulator; tcgen05.commit frees each stage and, after
+//     the unit's last chunk, publishes the accumulator (two accumulator
+//     buffers, so the next unit's products overlap this unit's epilogue).
 //   warps 4-7: epilogue.  tcgen05.ld of their 32 TMEM lanes (one weight row per
 //     thread), bf16 rounding (or the SwiGLU contract of the gate/up pair) and
-//     stores to the output rows.
+//     stores to the output rows; with a split reduction axis, fp32 partials to
+//     the workspace and the last CTA of the tile sums them in split order.
+//
+// The decoded weights never pass through shared memory: keeping them in TMEM
+// spares the 4 bytes of shared-memory traffic per weight (decoder store plus
+// tensor-core read) that made the shared-memory form bandwidth-bound.
 //
 // Every wait is bounded (2 s); a timeout sets device error bit 1 and a shared
 // abort flag, the roles leave their loops, the bulk copies and tensor-core
@@ -76,6 +85,7 @@ constexpr int MAX_SX = 12;
 constexpr int MAX_SW = 16;
 constexpr int MAX_ASSIGN = 4096;        // grouped modes: T * R
 constexpr int MAX_SLOTS = 520;          // grouped modes: experts in the bank
+constexpr int MAX_SPLITS = 4;           // reduction-axis splits per tile
 constexpr long long WAIT_NS = 2000000000LL;
 constexpr long long DRAIN_NS = 200000000LL;
 
@@ -401,7 +411,10 @@ __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
   const int E = A.E;
   for (int e = tid; e < E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
-  for (int a = tid; a < TR; a += NTHREADS) atomicAdd(&cnt[clamp_expert(A.idx[a], E, A.err)], 1);
+  for (int a = tid; a < TR; a += NTHREADS) {
+    const int64_t v = A.idx[a];
+    if (v != EXPERT_NONE) atomicAdd(&cnt[clamp_expert(v, E, A.err)], 1);
+  }
   __syncthreads();
   if (tid < 32) {
     const int lane = tid;
@@ -454,12 +467,10 @@ __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
     const int lane = tid;
     for (int base = 0; base < TR; base += 32) {
       const int a = base + lane;
-      const bool valid = a < TR;
+      const int64_t v = a < TR ? A.idx[a] : EXPERT_NONE;
+      const bool valid = v != EXPERT_NONE;
       int e = -1 - lane;
-      if (valid) {
-        const int64_t v = A.idx[a];
-        e = (v < 0 || v >= E) ? 0 : (int)v;
-      }
+      if (valid) e = (v < 0 || v >= E) ? 0 : (int)v;
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       const int pos = valid ? cnt[e] + __popc(peers & ((1u << lane) - 1u)) : 0;
       __syncwarp();
@@ -745,22 +756,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         named_barrier(1, 128);
         if (B->epi_last) {
           __threadfence();
-          const float* base = A.ws + (size_t)U.tile * A.splits * 2 * NT * BM;
-          for (int j = 0; j < U.nt; ++j) {
-            float g = 0.f, h = 0.f;
-            for (int k = 0; k < A.splits; ++k) {
-              const float* pk = base + (size_t)k * 2 * NT * BM;
-              g += __ldcg(pk + (size_t)j * BM + r);
-              h += __ldcg(pk + (size_t)(NT + j) * BM + r);
+          const float* base = A.ws + (size_t)U.tile * A.splits * 2 * NT * BM + r;
+          // Two tokens at a time: all splits' partials of both tiles are
+          // requested before any is summed (the loads are independent; the
+          // sums then run in split order).
+          for (int j0 = 0; j0 < U.nt; j0 += 2) {
+            float pg[MAX_SPLITS][2], ph[MAX_SPLITS][2];
+#pragma unroll
+            for (int k = 0; k < MAX_SPLITS; ++k) {
+              if (k < A.splits) {
+                const float* pk = base + (size_t)k * 2 * NT * BM;
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                  const int j = min(j0 + jj, U.nt - 1);
+                  pg[k][jj] = __ldcg(pk + (size_t)j * BM);
+                  ph[k][jj] = __ldcg(pk + (size_t)(NT + j) * BM);
+                }
+              }
             }
-            int xr, yr;
-            rows_of(A, P, U, j, xr, yr);
-            uint16_t* yrow = A.y + (size_t)yr * A.ys;
-            if (A.mode == SWIGLU) {
-              if (v0) yrow[row0 + r] = float_to_bf16_bits(swiglu_contract(g, h));
-            } else {
-              if (v0) yrow[row0 + r] = float_to_bf16_bits(g);
-              if (v1) yrow[row1 + r] = float_to_bf16_bits(h);
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const int j = j0 + jj;
+              if (j >= U.nt) break;
+              float g = 0.f, h = 0.f;
+#pragma unroll
+              for (int k = 0; k < MAX_SPLITS; ++k) {
+                if (k < A.splits) {
+                  g += pg[k][jj];
+                  h += ph[k][jj];
+                }
+              }
+              int xr, yr;
+              rows_of(A, P, U, j, xr, yr);
+              uint16_t* yrow = A.y + (size_t)yr * A.ys;
+              if (A.mode == SWIGLU) {
+                if (v0) yrow[row0 + r] = float_to_bf16_bits(swiglu_contract(g, h));
+              } else {
+                if (v0) yrow[row0 + r] = float_to_bf16_bits(g);
+                if (v1) yrow[row1 + r] = float_to_bf16_bits(h);
+              }
             }
           }
           named_barrier(1, 128);
@@ -968,8 +1002,12 @@ static void dense_split(int64_t M, int64_t K, int64_t N, int* nt, int* tiles, in
   const int n_rt = (int)((N + 2 * BM - 1) / (2 * BM));
   *tiles = n_rt * (int)((M + *nt - 1) / *nt);
   const int ks = (int)(K / KC);
+  // Splitting pays only when the tiles leave most SMs idle: each split adds
+  // an fp32 partial round trip through L2 and a reduction by the tile's last
+  // CTA.
   int sp = 1;
-  if (*tiles < TARGET_CTAS) sp = std::max(1, std::min(TARGET_CTAS / *tiles, ks / 3));
+  if (*tiles * 3 <= TARGET_CTAS)
+    sp = std::max(1, std::min(std::min(TARGET_CTAS / *tiles, MAX_SPLITS), ks / 4));
   *splits = sp;
 }
 

@@ -153,8 +153,9 @@ __device__ int build_plan(const GroupedArgs& G, uint32_t* err, int* cnt, int* sl
   for (int e = threadIdx.x; e <= E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
   for (int a = threadIdx.x; a < TR; a += NTHREADS) {
-    const int e = clamp_expert(G.idx[a], E, err);
-    atomicAdd(&cnt[e], 1);
+    const int64_t v = G.idx[a];
+    if (v == EXPERT_NONE) continue;  // empty slot: no weights read, no output written
+    atomicAdd(&cnt[clamp_expert(v, E, err)], 1);
   }
   __syncthreads();
   if (warp == 0) {
@@ -198,12 +199,10 @@ __device__ int build_plan(const GroupedArgs& G, uint32_t* err, int* cnt, int* sl
     __syncwarp();
     for (int base = 0; base < TR; base += 32) {
       const int a = base + lane;
-      const bool valid = a < TR;
+      const int64_t v = a < TR ? G.idx[a] : EXPERT_NONE;
+      const bool valid = v != EXPERT_NONE;
       int e = -1 - lane;
-      if (valid) {
-        const int64_t v = G.idx[a];
-        e = (v < 0 || v >= E) ? 0 : static_cast<int>(v);
-      }
+      if (valid) e = (v < 0 || v >= E) ? 0 : static_cast<int>(v);
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       const int rank = __popc(peers & ((1u << lane) - 1u));
       int pos = 0;

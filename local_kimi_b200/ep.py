@@ -7,26 +7,27 @@ are replicated.  Per layer every rank:
   1. routes its own tokens (``moe_router``: sigmoid, biased top-k, renormalised
      and scaled weights -- engine/klinear/router.py:47-85, the same kernel as
      the single-GPU layer);
-  2. sends each (token, route) pair's hidden row to the rank that owns the
-     route's expert, ordered by destination (stable, so token-major then route
-     order inside each destination): first the per-destination counts
-     (``all_to_all_single`` of int64 [G]), then the rows and the owner-local
-     expert ids with exact split sizes (no capacity padding; the counts are
-     read on the host once per layer);
-  3. runs gate/up + SwiGLU and the down projection for the rows it received
-     with its local expert bank (the grouped kernels, which read each local
-     expert's weights once for all rows that use it);
-  4. returns the per-route outputs to their source ranks with the reverse
-     ``all_to_all_single``;
-  5. computes the shared expert on its own tokens and combines
+  2. packs every (token, route) pair's hidden row for the rank that owns the
+     route's expert (``ep_dispatch``): fixed-capacity slots per destination
+     (tokens * top_k each, so nothing can overflow), the owner-local expert id
+     carried in the row's tail, unused slots marked -1;
+  3. exchanges the payloads with one equal-split ``all_to_all_single``;
+  4. runs gate/up + SwiGLU and the down projection for the rows it received
+     with its local expert bank (the grouped kernels read each local expert's
+     weights once for all rows that use it and skip the empty slots);
+  5. returns the outputs with a second equal-split ``all_to_all_single``;
+  6. computes the shared expert on its own tokens and combines
      bf16(sum_r y_r * w_r, fp32 in route order) + y_shared
      (engine/klinear/moe.py:317-334, moe_combine.py:209-261) with
-     ``moe_combine_routes``.
+     ``ep_combine``, reading each route's output at the slot it was sent from.
 
-The result equals the single-GPU layer's (``moe.moe_forward``) up to the fp32
-rounding of the combine.  The arithmetic is delegated to a backend object
-(``CudaExperts`` by default: this library's kernels), so the dispatch and
-combine logic can also run over ``gloo`` ranks on the CPU with a test backend.
+No step reads a count on the host, so a step made of these layers can be
+captured in one CUDA graph.  Every rank must run the layer on the same number
+of tokens (the capacity of the exchange buffers depends on it).  The result
+equals the single-GPU layer's (``moe.moe_forward``) up to the fp32 rounding of
+the combine.  The arithmetic is delegated to a backend object (``CudaExperts``
+by default: this library's kernels), so the dispatch and combine logic can also
+run over ``gloo`` ranks on the CPU with a test backend.
 """
 
 from __future__ import annotations
@@ -37,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .moe import MoELayerWeights
+from .moe import SHARED_TC_TOKENS, MoELayerWeights
 
 
 @dataclass
@@ -83,21 +84,41 @@ class CudaExperts:
                               routed_scaling_factor=layer.scaling,
                               append_expert=layer.num_experts)
 
-    def experts(self, rows: torch.Tensor, local_ids: torch.Tensor,
-                bank: LocalExpertBank) -> torch.Tensor:
-        """Down(SwiGLU(gate/up)) of each row with its local expert, bf16 [n, H]."""
-        idx = local_ids.view(-1, 1)
+    def dispatch(self, hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
+                 capacity: int):
+        """(payload bf16 [world*capacity, H+8], slots int32 [T*k])."""
+        return ops.ep_dispatch(hidden, routed, per_rank, world, capacity)
+
+    def experts(self, payload: torch.Tensor, bank: LocalExpertBank) -> torch.Tensor:
+        """Down(SwiGLU(gate/up)) of each payload row with its local expert, bf16 [n, H];
+        rows of empty slots (id -1) are skipped and left undefined."""
+        width = payload.shape[1] - 8
+        rows = payload[:, :width]
+        idx = ops.payload_ids(payload).contiguous()
         act = ops.w4a16_swiglu(rows, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed,
                                bank.w3_scales)
         return ops.w4a16_grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
 
-    def combine(self, routes: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
-        return ops.moe_combine_routes(routes, weights)
+    def shared(self, hidden: torch.Tensor, bank: LocalExpertBank) -> torch.Tensor:
+        """The shared expert (local bank slot per_rank) on this rank's tokens, bf16 [T, H]."""
+        t = hidden.shape[0]
+        idx = torch.full((t, 1), bank.per_rank, dtype=torch.long, device=hidden.device)
+        big = t >= SHARED_TC_TOKENS
+        swiglu = ops.w4a16_swiglu_tc if big else ops.w4a16_swiglu
+        grouped = ops.w4a16_grouped_tc if big else ops.w4a16_grouped
+        act = swiglu(hidden, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed,
+                     bank.w3_scales)
+        return grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
+
+    def combine(self, y: torch.Tensor, slots: torch.Tensor, weights: torch.Tensor,
+                shared: torch.Tensor) -> torch.Tensor:
+        return ops.ep_combine(y, slots, weights, shared)
 
 
 class ExpertParallelMoE:
     """One MoE layer with its experts sharded over ``group`` (the default
-    process group when None).  ``forward`` takes this rank's tokens."""
+    process group when None).  ``forward`` takes this rank's tokens; every
+    rank passes the same number of tokens."""
 
     def __init__(self, layer: MoELayerWeights, group=None, backend=None):
         self.group = group
@@ -106,11 +127,7 @@ class ExpertParallelMoE:
         self.layer = layer
         self.bank = shard_bank(layer, self.rank, self.world)
         self.backend = backend if backend is not None else CudaExperts()
-        self.last_counts: tuple[list[int], list[int]] | None = None
-
-    def _exchange(self, out: torch.Tensor, inp: torch.Tensor, out_split: list[int],
-                  in_split: list[int]) -> None:
-        dist.all_to_all_single(out, inp, out_split, in_split, group=self.group)
+        self.last_payload: torch.Tensor | None = None
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
         """hidden bf16 [T, H] (this rank's tokens) -> bf16 [T, H]."""
@@ -118,29 +135,14 @@ class ExpertParallelMoE:
         tokens, width = hidden.shape
         k = layer.top_k
         stable, weights = be.route(hidden, layer)
-        routed = stable[:, :k].reshape(-1)
-        dest = torch.div(routed, bank.per_rank, rounding_mode="floor")
-        order = torch.argsort(dest, stable=True)
-        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        send_split = send_counts.tolist()
-        recv_split = recv_counts.tolist()
-        self.last_counts = (send_split, recv_split)
-        send_rows = hidden.index_select(0, torch.div(order, k, rounding_mode="floor"))
-        send_ids = routed[order] - dest[order] * bank.per_rank
-        recv_rows = hidden.new_empty((sum(recv_split), width))
-        recv_ids = send_ids.new_empty((sum(recv_split),))
-        self._exchange(recv_rows, send_rows, recv_split, send_split)
-        self._exchange(recv_ids, send_ids, recv_split, send_split)
-        y_recv = be.experts(recv_rows, recv_ids, bank)
-        y_send = hidden.new_empty((tokens * k, width))
-        self._exchange(y_send, y_recv.contiguous(), send_split, recv_split)
-        y_routed = hidden.new_empty((tokens * k, width))
-        y_routed[order] = y_send
-        shared_ids = torch.full((tokens,), bank.per_rank, dtype=torch.int64,
-                                device=hidden.device)
-        y_shared = be.experts(hidden, shared_ids, bank)
-        routes = torch.cat((y_routed.view(tokens, k, width), y_shared.view(tokens, 1, width)),
-                           dim=1)
-        return be.combine(routes, weights)
+        routed = stable[:, :k].contiguous()
+        capacity = max(1, tokens * k)
+        payload, slots = be.dispatch(hidden, routed, bank.per_rank, self.world, capacity)
+        self.last_payload = payload
+        received = torch.empty_like(payload)
+        dist.all_to_all_single(received, payload, group=self.group)
+        y_recv = be.experts(received, bank)
+        y_back = torch.empty_like(y_recv)
+        dist.all_to_all_single(y_back, y_recv.contiguous(), group=self.group)
+        y_shared = be.shared(hidden, bank)
+        return be.combine(y_back, slots, weights, y_shared)

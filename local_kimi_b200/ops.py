@@ -131,10 +131,50 @@ def _validate_dense(
     return m, output_size, reduction, group
 
 
+# Tensor-core (tcgen05) limits: K a multiple of 64, N of 8, at most 81 scale
+# groups per row (the per-CTA scale buffers).
+TC_MAX_GROUPS_PER_ROW = 81
+
+
+def tc_supported(m: int, n: int, k: int, group: int) -> bool:
+    return k % 64 == 0 and n % 8 == 0 and k // group <= TC_MAX_GROUPS_PER_ROW and m > 0
+
+
+def prefer_tc(m: int, n: int, k: int, group: int) -> bool:
+    """Whether the tensor-core path beats the projection engine for this shape.
+
+    Measured on B200 (dense sweep over the decode shapes): the engine decodes
+    each weight once per 16-token group, the tensor-core path once per 64
+    tokens, so the tensor cores win from 64 tokens on every shape, from 32 on
+    matrices of 16M+ weights and from 16 on the 9216-wide reduction.
+    """
+    if not tc_supported(m, n, k, group):
+        return False
+    if m >= 64:
+        return True
+    if m >= 32 and n * k >= 16 * 2**20:
+        return True
+    return m >= 16 and k >= 8192
+
+
 def w4a16_dense(
     activations: torch.Tensor, packed_weights: torch.Tensor, scales: torch.Tensor
 ) -> torch.Tensor:
-    """y[M,N] = activations[M,K] . dequant(W[N,K])^T, bf16 out (registry op w4a16_dense)."""
+    """y[M,N] = activations[M,K] . dequant(W[N,K])^T, bf16 out (registry op w4a16_dense).
+
+    Small token counts run on the projection engine, many tokens on the
+    tcgen05 tensor-core path (``prefer_tc``); both keep the result contract.
+    """
+    m, n, k, group = _validate_dense(activations, packed_weights, scales)
+    if prefer_tc(m, n, k, group):
+        return w4a16_dense_tc(activations, packed_weights, scales)
+    return w4a16_dense_engine(activations, packed_weights, scales)
+
+
+def w4a16_dense_engine(
+    activations: torch.Tensor, packed_weights: torch.Tensor, scales: torch.Tensor
+) -> torch.Tensor:
+    """w4a16_dense on the projection engine (kb_w4a16_dense), whatever the token count."""
     m, n, k, group = _validate_dense(activations, packed_weights, scales)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=activations.device)
     if m == 0:
@@ -153,9 +193,12 @@ def w4a16_dense(
 def w4a16_dense_multi(
     problems: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
 ) -> list[torch.Tensor]:
-    """Several independent dense projections in one launch."""
+    """Several independent dense projections in one launch (one tensor-core
+    launch each when ``prefer_tc`` picks that path for every problem)."""
     if len(problems) > _lib.MAX_DENSE_PROBLEMS:
         raise ValueError(f"at most {_lib.MAX_DENSE_PROBLEMS} problems per launch")
+    if problems and all(prefer_tc(*_validate_dense(*pr)) for pr in problems):
+        return [w4a16_dense_tc(*pr) for pr in problems]
     arr = (_lib.DenseProblem * max(1, len(problems)))()
     outs: list[torch.Tensor] = []
     keep: list[torch.Tensor] = []
@@ -528,6 +571,79 @@ def moe_combine_routes(routes: torch.Tensor, weights: torch.Tensor) -> torch.Ten
     w = weights if weights.stride(1) == 1 else weights.contiguous()
     _lib.call("kb_moe_combine_routes", _p(y), c_int64(t), c_int64(r), c_int64(n), _p(w),
               c_int64(w.stride(0)), _p(out), _stream(y.device))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# expert-parallel data plane
+# ---------------------------------------------------------------------------
+
+
+def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
+                capacity: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Pack each routed (token, route) pair's hidden row for its expert's rank.
+
+    hidden bf16 [T, H]; routed int64 [T, k] global expert ids.  Returns
+    (payload bf16 [world*capacity, H+8]: per slot the row, then the
+    owner-local expert id as an int64 in the next four bf16 -- -1 for an
+    unused slot; slots int32 [T*k]: the payload slot of each pair).
+    capacity must be at least T*k.
+    """
+    if hidden.dtype != torch.bfloat16 or hidden.ndim != 2:
+        raise TypeError("hidden must be BF16 [T, H]")
+    if routed.dtype != torch.long or routed.ndim != 2 or routed.shape[0] != hidden.shape[0]:
+        raise TypeError("routed must be int64 [T, k]")
+    _require_cuda(hidden, "expert-parallel dispatch")
+    if routed.device != hidden.device:
+        raise ValueError("routed must be on the device of hidden")
+    t, h = hidden.shape
+    k = routed.shape[1]
+    if capacity < t * k:
+        raise ValueError("capacity must be at least tokens * top_k")
+    payload = torch.empty((world * capacity, h + 8), dtype=torch.bfloat16,
+                          device=hidden.device)
+    slots = torch.empty((t * k,), dtype=torch.int32, device=hidden.device)
+    if t == 0:
+        payload_ids(payload).fill_(-1)
+        return payload, slots
+    x = _rows_16b(hidden)
+    r = routed if routed.stride(1) == 1 else routed.contiguous()
+    _lib.call("kb_ep_dispatch", _p(x), c_int64(x.stride(0)), c_int64(t), c_int64(h), _p(r),
+              c_int64(r.stride(0)), c_int64(k), c_int64(per_rank), c_int64(world),
+              c_int64(capacity), _p(payload), _p(slots), _stream(x.device))
+    return payload, slots
+
+
+def payload_ids(payload: torch.Tensor) -> torch.Tensor:
+    """The int64 expert-id column of a dispatch payload, [n, 1] (a view)."""
+    h = payload.shape[1] - 8
+    return payload[:, h:h + 4].view(torch.long)
+
+
+def ep_combine(y: torch.Tensor, slots: torch.Tensor, weights: torch.Tensor,
+               shared: torch.Tensor) -> torch.Tensor:
+    """bf16(sum_r float(y[slots[t,r]]) * weights[t,r]) + shared[t], bf16 [T, H]."""
+    if y.dtype != torch.bfloat16 or shared.dtype != torch.bfloat16:
+        raise TypeError("y and shared must be BF16")
+    if weights.dtype != torch.float32 or slots.dtype != torch.int32:
+        raise TypeError("weights must be FP32 and slots int32")
+    _require_cuda(y, "expert-parallel combine")
+    if not (slots.device == weights.device == shared.device == y.device):
+        raise ValueError("combine inputs must share one device")
+    t, h = shared.shape
+    k = weights.shape[1]
+    if slots.numel() != t * k or y.shape[1] != h:
+        raise ValueError("slots must have T*k entries and y rows the width of shared")
+    out = torch.empty((t, h), dtype=torch.bfloat16, device=y.device)
+    if t == 0:
+        return out
+    yc = y.contiguous()
+    sc = slots.contiguous()
+    s = _rows_16b(shared)
+    w = weights if weights.stride(1) == 1 else weights.contiguous()
+    _lib.call("kb_ep_combine", _p(yc), _p(sc), c_int64(t), c_int64(k), c_int64(h), _p(w),
+              c_int64(w.stride(0)), _p(s), c_int64(s.stride(0)), _p(out), c_int64(out.stride(0)),
+              _stream(yc.device))
     return out
 
 

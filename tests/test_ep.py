@@ -18,6 +18,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from local_kimi_b200 import ops
 from local_kimi_b200.ep import ExpertParallelMoE, shard_bank
 from local_kimi_b200.moe import MoELayerWeights
 from oracle import codec
@@ -64,24 +65,57 @@ def _tokens(world: int, per_rank: int) -> torch.Tensor:
 
 
 class OracleExperts:
-    """The layer's arithmetic restated by the oracle (test backend)."""
+    """The layer's arithmetic and data plane restated on the CPU (test backend)."""
 
     def route(self, hidden, layer):
         idx, w, _ = oref.router_topk(hidden, layer.router_weight, layer.router_bias,
                                      layer.top_k, scaling=layer.scaling)
         return oref.shape_stable_indices(idx, layer.num_experts), w
 
-    def experts(self, rows, local_ids, bank):
-        idx = local_ids.view(-1, 1)
-        act = oref.swiglu(rows, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed,
+    def dispatch(self, hidden, routed, per_rank, world, capacity):
+        # Pairs in token-major order; each takes the next free slot of its
+        # destination rank (the stable scan of kb_ep_dispatch).
+        t, h = hidden.shape
+        k = routed.shape[1]
+        payload = torch.zeros((world * capacity, h + 8), dtype=torch.bfloat16)
+        ids = ops.payload_ids(payload)
+        ids.fill_(-1)
+        fill = [0] * world
+        slots = torch.empty((t * k,), dtype=torch.int32)
+        for a in range(t * k):
+            tok, r = divmod(a, k)
+            e = int(routed[tok, r])
+            d = e // per_rank
+            slot = d * capacity + fill[d]
+            fill[d] += 1
+            payload[slot, :h] = hidden[tok]
+            ids[slot, 0] = e - d * per_rank
+            slots[a] = slot
+        return payload, slots
+
+    def experts(self, payload, bank):
+        h = payload.shape[1] - 8
+        ids = ops.payload_ids(payload)[:, 0]
+        out = torch.zeros((payload.shape[0], h), dtype=torch.bfloat16)
+        valid = (ids >= 0).nonzero()[:, 0]
+        if valid.numel():
+            idx = ids[valid].view(-1, 1)
+            act = oref.swiglu(payload[valid, :h], idx, bank.w1_packed, bank.w1_scales,
+                              bank.w3_packed, bank.w3_scales)
+            out[valid] = oref.grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
+        return out
+
+    def shared(self, hidden, bank):
+        idx = torch.full((hidden.shape[0], 1), bank.per_rank, dtype=torch.long)
+        act = oref.swiglu(hidden, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed,
                           bank.w3_scales)
         return oref.grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
 
-    def combine(self, routes, weights):
-        r = routes.shape[1]
-        routed = (routes[:, : r - 1].float() * weights[:, : r - 1].float().unsqueeze(-1)).sum(
-            dim=1).to(torch.bfloat16)
-        return routed + routes[:, r - 1]
+    def combine(self, y, slots, weights, shared):
+        t, k = weights.shape
+        routes = y[slots.long()].view(t, k, -1)
+        routed = (routes.float() * weights.float().unsqueeze(-1)).sum(dim=1).to(torch.bfloat16)
+        return routed + shared
 
 
 def _cpu_rank(rank: int, world: int, port: int, per_rank: int) -> None:
@@ -97,13 +131,14 @@ def _cpu_rank(rank: int, world: int, port: int, per_rank: int) -> None:
         expected, idx, _ = omoe.moe_layer(x, banks)
         exp_mine = expected[rank * per_rank:(rank + 1) * per_rank]
         assert torch.equal(out, exp_mine), f"rank {rank}: EP output differs from the oracle"
-        # every (token, route) pair went to the owner of its expert
-        send, recv = ep.last_counts
+        # every (token, route) pair went to the owner of its expert: the
+        # filled slots of each destination block match the pairs it owns
+        capacity = per_rank * TOP_K
+        ids = ops.payload_ids(ep.last_payload)[:, 0]
         owners = torch.div(idx[rank * per_rank:(rank + 1) * per_rank], E // world,
                            rounding_mode="floor")
-        assert send == torch.bincount(owners.reshape(-1), minlength=world).tolist()
-        assert sum(recv) == int(
-            (torch.div(idx, E // world, rounding_mode="floor") == rank).sum())
+        sent = [(ids[d * capacity:(d + 1) * capacity] >= 0).sum().item() for d in range(world)]
+        assert sent == torch.bincount(owners.reshape(-1), minlength=world).tolist()
     finally:
         dist.destroy_process_group()
 
@@ -171,8 +206,37 @@ def test_combine_routes_matches_oracle(cuda):
     routes = torch.randn((37, 9, 2304), generator=g, device=cuda).to(torch.bfloat16)
     w = torch.rand((37, 8), generator=g, device=cuda)
     out = ops.moe_combine_routes(routes, w)
-    assert_close(out, OracleExperts().combine(routes.cpu(), w.cpu()), what="combine routes")
+    rc, wc = routes.cpu(), w.cpu()
+    routed = (rc[:, :8].float() * wc.unsqueeze(-1)).sum(dim=1).to(torch.bfloat16)
+    assert_close(out, routed + rc[:, 8], what="combine routes")
     assert torch.equal(out, ops.moe_combine_routes(routes, w)), "combine not deterministic"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,tokens", [(1, 64), (4, 17), (8, 32)])
+def test_dispatch_and_combine_kernels_match_cpu_restatement(cuda, world, tokens):
+    # kb_ep_dispatch against the CPU restatement of the slot layout (rows,
+    # ids, empty slots, pair slots), then kb_ep_combine on returned outputs.
+    from tests.conftest import assert_close
+
+    g = torch.Generator().manual_seed(world * 100 + tokens)
+    experts, k, h = 256, 8, 2304
+    per_rank = experts // world
+    hidden = torch.randn((tokens, h), generator=g).to(torch.bfloat16)
+    routed = torch.stack([torch.randperm(experts, generator=g)[:k] for _ in range(tokens)])
+    cap = tokens * k
+    payload, slots = ops.ep_dispatch(hidden.to(cuda), routed.to(cuda), per_rank, world, cap)
+    ref_payload, ref_slots = OracleExperts().dispatch(hidden, routed, per_rank, world, cap)
+    ids = ops.payload_ids(payload).cpu()
+    assert torch.equal(ids, ops.payload_ids(ref_payload))
+    assert torch.equal(slots.cpu(), ref_slots)
+    used = (ids[:, 0] >= 0).nonzero()[:, 0]
+    assert torch.equal(payload.cpu()[used, :h], ref_payload[used, :h])
+    y = torch.randn((world * cap, h), generator=g).to(torch.bfloat16)
+    w = torch.rand((tokens, k), generator=g)
+    shared = torch.randn((tokens, h), generator=g).to(torch.bfloat16)
+    out = ops.ep_combine(y.to(cuda), slots, w.to(cuda), shared.to(cuda))
+    assert_close(out, OracleExperts().combine(y, ref_slots, w, shared), what="ep combine")
 
 
 @pytest.mark.gpu

@@ -59,7 +59,7 @@ def test_dense_tc_agrees_with_gemv_engine(cuda):
     packed, scales = quant_matrix(4096, 2304, 128, gen)
     x = rand_act((32, 2304), gen)
     a = ops.w4a16_dense_tc(x, packed, scales)
-    b = ops.w4a16_dense(x, packed, scales)
+    b = ops.w4a16_dense_engine(x, packed, scales)
     assert_close(a, b, what="tc vs gemv")
 
 

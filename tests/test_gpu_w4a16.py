@@ -49,15 +49,19 @@ DENSE_SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("path", ["dispatch", "engine"])
 @pytest.mark.parametrize("m,n,k,group", DENSE_SHAPES)
-def test_dense_matches_oracle(cuda, m, n, k, group):
+def test_dense_matches_oracle(cuda, m, n, k, group, path):
+    # "dispatch" is the registry op (engine or tensor-core path by shape);
+    # "engine" forces the projection engine at every token count.
+    fn = ops.w4a16_dense if path == "dispatch" else ops.w4a16_dense_engine
     gen = cuda_gen(0)
     packed, scales = quant_matrix(n, k, group, gen)
     x = rand_act((m, k), cuda_gen(1))
-    y = ops.w4a16_dense(x, packed, scales)
+    y = fn(x, packed, scales)
     expected = oref.dense(x.cpu(), packed.cpu(), scales.cpu())
-    assert_close(y, expected, what=f"dense {m}x{n}x{k} g{group}")
-    again = ops.w4a16_dense(x, packed, scales)
+    assert_close(y, expected, what=f"dense {m}x{n}x{k} g{group} ({path})")
+    again = fn(x, packed, scales)
     assert torch.equal(y, again), "dense output is not deterministic"
 
 
