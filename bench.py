@@ -1,33 +1,35 @@
 #!/usr/bin/env python
 """Decode-throughput benchmark of the Kimi-Linear-48B-A3B W4A16 hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--total-batch B] [--impl b200|reference]
 
-A step is one decode step of the hot path (local_kimi_b200.decode): for all
-27 layers the INT4 attention projections, the KDA recurrent-state step, the
-MoE router/experts/combine, then the INT4 lm_head, over B tokens, with
-random-init weights of the real shapes (about 25 GB, resident in HBM).
+The benchmark step (every N, one process per GPU under torchrun) is one decode
+step of the hot path (local_kimi_b200.decode) for B = 256 concurrent sequences
+in total, B/N per rank, with random-init weights of the real shapes (about
+25 GB, resident in HBM): for all 27 layers the INT4 attention projections and
+the KDA recurrent-state step on the rank's own sequences, every MoE layer
+expert-parallel over the N ranks (local_kimi_b200.ep: 256/N routed experts per
+rank, fixed-capacity dispatch, NCCL all-to-all over NVLink, shared expert and
+combine on the owning rank), then the INT4 lm_head.  N = 1 runs the same step
+with all experts local.  The step is captured as one CUDA graph (eager
+launches where capture is unavailable).
 
-The step runs on the decode-step executor (local_kimi_b200.step: the whole
-program in one persistent launch, batch <= 8); the same step as registry-level
-launches captured in one CUDA graph (as the reference engine captures its
-decode step, engine/klinear/generate.py:226-276) is timed beside it and its
-logits are compared with the executor's (``parity_vs_per_op``).
-
-Printed: one JSON line.  ``value`` = tokens/s over all ranks with inputs
-resident in HBM (device-timed, max over ranks); ``e2e`` = the same metric
-with a host->device copy of the step input and a device->host copy of the
-logits inside the timed region; ``roofline`` = algorithmic bytes of the step
-over its time, against the measured HBM copy bandwidth; ``cpu_baseline`` =
-the CPU oracle on a bounded sample of the same step.  Every step reads ~1.7 GB
-of weights, far more than the 126 MB L2, so no L2 flush is needed between
-steps.
+Printed: one JSON line.  ``value`` = tokens/s over all ranks (B / step time,
+device-timed, max over ranks; strong scaling: B is fixed as N grows);
+``e2e`` = the same with a host->device copy of the step input and a
+device->host copy of the logits inside the timed region; ``roofline`` =
+algorithmic bytes of rank 0's step over its time against the measured HBM
+copy bandwidth; ``cpu_baseline`` = the oracle on a bounded sample of the same
+step (BatchCpuSample, median of 10 after 3 warm-ups).  At N = 1 the line also
+carries ``bs1`` (the batch-1 step on the one-launch decode-step executor, with
+the per-operation graph and their logits compared), ``bs32`` (batch 32,
+per-operation graph) and ``dense_sweep`` (the C2 sweep at M 1/16/64).  Every
+step reads GBs of weights and KDA state, far more than the 126 MB L2, so no L2
+flush is needed between steps.
 
 ``--impl reference`` times the reference's CPU path restated in ``oracle/``
 (the reference is pure Python/torch and does not exist on the GPU box) on all
-host cores, on a bounded per-step sample, and prints the same metric.
-With torchrun (N > 1) each rank runs its own replica of the step (weak
-scaling; the expert-parallel exchange is not part of this benchmark).
+host cores, on the same bounded per-step sample, and prints the same metric.
 """
 
 from __future__ import annotations
@@ -49,19 +51,20 @@ import torch  # noqa: E402
 
 METRIC = "decode tok/s Kimi-Linear-48B W4A16 (hot path step)"
 HBM_FALLBACK_GBS = 6650.0
-# DRAM traffic over algorithmic bytes of step_kernel, from an ncu capture of a
-# 3-layer program (profiles/step_kernel_decode_bs1.md: 368.6 MB read+write for
-# 366.9 MB algorithmic); traffic grows with the bytes streamed, so the full
-# step's traffic is reported as this ratio times its algorithmic bytes.
-STEP_TRAFFIC_RATIO = 1.005
 
 
 def _args() -> argparse.Namespace:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1, help="token count of the single-case runs")
+    ap.add_argument("--total-batch", type=int, default=256,
+                    help="sequences of the benchmark step over all ranks")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="leave the dense-sweep sub-record out of the N=1 line")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="only the benchmark step (no sub-records, no CPU baseline)")
     ap.add_argument("--group", type=int, default=128)
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (testing only)")
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
@@ -314,6 +317,255 @@ class CpuSample:
         return total, sample, torch.get_num_threads()
 
 
+class BatchCpuSample:
+    """The oracle (torch CPU, all cores) on a bounded sample of the batch decode
+    step: one KDA attention block, one MLA attention block, one MoE layer, the
+    dense MLP of layer 0 and 1/8 of the lm_head rows, at ``batch`` tokens.
+
+    The MoE layer routes all tokens but computes the routed experts for only
+    ``expert_sample`` of the experts it touches (each with its own tokens),
+    scaled by the number touched; the shared expert runs on every token.  The
+    KDA state step runs at ``kda_batch`` sequences and is scaled by
+    batch / kda_batch (its cost is linear in the batch).  Weights are seeded
+    synthetic values with the real shapes (the timing does not depend on the
+    values); the per-step time is extrapolated to the 27-layer step.
+    """
+
+    LM_HEAD_FRACTION = 8
+
+    def __init__(self, batch: int, group: int, seed: int = 0, expert_sample: int = 8,
+                 kda_batch: int = 32) -> None:
+        from local_kimi_b200.decode import KimiLinearShape
+        from oracle import synth
+
+        s = KimiLinearShape()
+        self.shape, self.batch, self.group = s, batch, group
+        self.expert_sample = expert_sample
+        self.kda_batch = min(kda_batch, batch)
+        gen = synth.generator(seed)
+        act = synth.generator(seed + 1)
+        H, D = s.kda_heads, s.kda_head_dim
+        proj = H * D
+        q = lambda n, k: synth.quantised(n, k, group, gen)  # noqa: E731
+        self.x = synth.activations((batch, s.hidden), act)
+        self.attn = synth.activations((batch, s.mla_heads * s.mla_v_head_dim), act)
+        self.latent = synth.activations((batch, s.kv_lora_rank), act)
+        self.kda_in = synth.activations((batch, proj), act)
+        kb = self.kda_batch
+        self.q = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
+        self.k = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
+        self.v = 0.2 * torch.randn((kb, H, D), generator=act)
+        self.decay = -(0.005 + 0.075 * torch.rand((kb, H, D), generator=act))
+        self.beta = torch.sigmoid(torch.randn((kb, H), generator=act))
+        self.state = 0.05 * torch.randn((kb, H, D, D), generator=gen)
+        self.qkv = [q(proj, s.hidden) for _ in range(3)]
+        self.kda_o = q(s.hidden, proj)
+        self.mla_q = q(s.mla_heads * s.mla_q_head_dim, s.hidden)
+        self.kv_b = q(s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
+        self.mla_o = q(s.hidden, s.mla_heads * s.mla_v_head_dim)
+        self.router = synth.weight((s.experts, s.hidden), gen)
+        self.experts = [(q(s.moe_intermediate, s.hidden), q(s.moe_intermediate, s.hidden),
+                         q(s.hidden, s.moe_intermediate)) for _ in range(expert_sample + 1)]
+        w1, w3 = q(s.dense_intermediate, s.hidden), q(s.dense_intermediate, s.hidden)
+        w2 = q(s.hidden, s.dense_intermediate)
+        self.dense = (w1, w3, w2)
+        self.lm_head = q(s.vocab_size // self.LM_HEAD_FRACTION, s.hidden)
+        self.n_kda = sum(1 for i in range(s.layers) if not s.is_mla(i))
+        self.n_mla = s.layers - self.n_kda
+        self.n_moe = s.layers - s.first_k_dense
+
+    @staticmethod
+    def _ffn(x: torch.Tensor, w1, w3, w2) -> torch.Tensor:
+        from oracle import ops as oref
+
+        idx = torch.zeros((x.shape[0], 1), dtype=torch.long)
+        a = oref.swiglu(x, idx, w1[0][None], w1[1][None], w3[0][None], w3[1][None])[:, 0]
+        return oref.dense(a, *w2)
+
+    def seconds_per_step(self) -> tuple[float, str, int]:
+        from oracle import ops as oref
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        s, B = self.shape, self.batch
+        scale = s.kda_head_dim ** -0.5
+        t0 = time.perf_counter()
+        oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
+        t_qkv = time.perf_counter() - t0
+        # The KDA state step's cost is linear in the batch: timed at kda_batch
+        # sequences and scaled.
+        st = self.state.clone()
+        t0 = time.perf_counter()
+        oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
+        t_state = (time.perf_counter() - t0) * (B / self.kda_batch)
+        t0 = time.perf_counter()
+        oref.dense(self.kda_in, *self.kda_o)
+        t_kda_block = t_qkv + t_state + (time.perf_counter() - t0)
+
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.mla_q)
+        oref.dense(self.latent, *self.kv_b)
+        h = oref.dense(self.attn, *self.mla_o)
+        omoe.moe_layer(h, banks_mla)
+        t_mla = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        d = self.dense
+        a = oref.swiglu(self.x, torch.zeros((B, 1), dtype=torch.long), d[0], d[1], d[2], d[3])
+        oref.dense(a.view(B, -1), d[4], d[5])
+        t_dense = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.lm_head)
+        t_head = (time.perf_counter() - t0) * self.LM_HEAD_FRACTION
+
+        total = t_kda * self.n_kda + t_mla * self.n_mla + t_dense + t_head
+        sample = (f"oracle (torch CPU, {torch.get_num_threads()} threads) on 1 KDA+MoE layer, "
+                  f"1 MLA+MoE layer, the dense layer 0 and 1/{self.LM_HEAD_FRACTION} of the "
+                  f"lm_head rows at batch {B}; per-step time extrapolated to {self.n_kda} "
+                  f"KDA+MoE + {self.n_mla} MLA+MoE layers + layer 0 + the full lm_head")
+        return total, sample, torch.get_num_threads()
+
+
+class BatchCpuSample:
+    """The oracle (torch CPU, all cores) on a bounded sample of the batch decode
+    step: one KDA attention block, one MLA attention block, one MoE layer, the
+    dense MLP of layer 0 and 1/8 of the lm_head rows, at ``batch`` tokens.
+
+    The MoE layer routes all tokens but computes the routed experts for only
+    ``expert_sample`` of the experts it touches (each with its own tokens),
+    scaled by the number touched; the shared expert runs on every token.  The
+    KDA state step runs at ``kda_batch`` sequences and is scaled by
+    batch / kda_batch (its cost is linear in the batch).  Weights are seeded
+    synthetic values with the real shapes (the timing does not depend on the
+    values); the per-step time is extrapolated to the 27-layer step.
+    """
+
+    LM_HEAD_FRACTION = 8
+
+    def __init__(self, batch: int, group: int, seed: int = 0, expert_sample: int = 8,
+                 kda_batch: int = 32) -> None:
+        from local_kimi_b200.decode import KimiLinearShape
+        from oracle import synth
+
+        s = KimiLinearShape()
+        self.shape, self.batch, self.group = s, batch, group
+        self.expert_sample = expert_sample
+        self.kda_batch = min(kda_batch, batch)
+        gen = synth.generator(seed)
+        act = synth.generator(seed + 1)
+        H, D = s.kda_heads, s.kda_head_dim
+        proj = H * D
+        q = lambda n, k: synth.quantised(n, k, group, gen)  # noqa: E731
+        self.x = synth.activations((batch, s.hidden), act)
+        self.attn = synth.activations((batch, s.mla_heads * s.mla_v_head_dim), act)
+        self.latent = synth.activations((batch, s.kv_lora_rank), act)
+        self.kda_in = synth.activations((batch, proj), act)
+        kb = self.kda_batch
+        self.q = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
+        self.k = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
+        self.v = 0.2 * torch.randn((kb, H, D), generator=act)
+        self.decay = -(0.005 + 0.075 * torch.rand((kb, H, D), generator=act))
+        self.beta = torch.sigmoid(torch.randn((kb, H), generator=act))
+        self.state = 0.05 * torch.randn((kb, H, D, D), generator=gen)
+        self.qkv = [q(proj, s.hidden) for _ in range(3)]
+        self.kda_o = q(s.hidden, proj)
+        self.mla_q = q(s.mla_heads * s.mla_q_head_dim, s.hidden)
+        self.kv_b = q(s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
+        self.mla_o = q(s.hidden, s.mla_heads * s.mla_v_head_dim)
+        self.router = synth.weight((s.experts, s.hidden), gen)
+        self.experts = [(q(s.moe_intermediate, s.hidden), q(s.moe_intermediate, s.hidden),
+                         q(s.hidden, s.moe_intermediate)) for _ in range(expert_sample + 1)]
+        w1, w3 = q(s.dense_intermediate, s.hidden), q(s.dense_intermediate, s.hidden)
+        w2 = q(s.hidden, s.dense_intermediate)
+        self.dense = (w1, w3, w2)
+        self.lm_head = q(s.vocab_size // self.LM_HEAD_FRACTION, s.hidden)
+        self.n_kda = sum(1 for i in range(s.layers) if not s.is_mla(i))
+        self.n_mla = s.layers - self.n_kda
+        self.n_moe = s.layers - s.first_k_dense
+
+    @staticmethod
+    def _ffn(x: torch.Tensor, w1, w3, w2) -> torch.Tensor:
+        from oracle import ops as oref
+
+        idx = torch.zeros((x.shape[0], 1), dtype=torch.long)
+        a = oref.swiglu(x, idx, w1[0][None], w1[1][None], w3[0][None], w3[1][None])[:, 0]
+        return oref.dense(a, *w2)
+
+    def seconds_per_step(self) -> tuple[float, str, int]:
+        from oracle import ops as oref
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        s, B = self.shape, self.batch
+        scale = s.kda_head_dim ** -0.5
+        t0 = time.perf_counter()
+        oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
+        st = self.state.clone()
+        oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
+        t_kda_state = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        oref.dense(self.kda_in, *self.kda_o)
+        t_kda = (time.perf_counter() - t1) + t_kda_state * 0  # o_proj
+        t_kda += t_kda_state
+        t_kda_scaled = t_kda + (t_kda_state - 0) * 0
+        # KDA state step cost scales with the batch: measure it alone and scale.
+        t2 = time.perf_counter()
+        st = self.state.clone()
+        oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
+        t_state = time.perf_counter() - t2
+        t_kda_block = t_kda_scaled - t_state + t_state * (B / self.kda_batch)
+
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.mla_q)
+        oref.dense(self.latent, *self.kv_b)
+        oref.dense(self.attn, *self.mla_o)
+        t_mla = time.perf_counter() - t0
+
+        t0 = time.perf_counter()
+        idx, w, _ = oref.router_topk(self.x, self.router, None, s.top_k,
+                                     scaling=s.routed_scaling_factor)
+        shared = self._ffn(self.x, *self.experts[-1])
+        t_route_shared = time.perf_counter() - t0
+        touched = torch.unique(idx)
+        sample = touched[: self.expert_sample].tolist()
+        t0 = time.perf_counter()
+        for j, e in enumerate(sample):
+            rows = (idx == e).any(dim=1).nonzero()[:, 0]
+            self._ffn(self.x[rows], *self.experts[j])
+        t_routed = (time.perf_counter() - t0) * (touched.numel() / max(1, len(sample)))
+        del shared, w
+        t_moe = t_route_shared + t_routed
+
+        t0 = time.perf_counter()
+        self._ffn(self.x, *self.dense)
+        t_dense = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        oref.dense(self.x, *self.lm_head)
+        t_head = (time.perf_counter() - t0) * self.LM_HEAD_FRACTION
+
+        total = (self.n_kda * t_kda_block + self.n_mla * t_mla + self.n_moe * t_moe + t_dense
+                 + t_head)
+        desc = (f"oracle (torch CPU, {torch.get_num_threads()} threads) at batch {B}: one KDA "
+                f"block (q/k/v, state step at {self.kda_batch} sequences scaled x"
+                f"{B / self.kda_batch:g}, o_proj), one MLA block (q_proj, kv_b, o_proj), one "
+                f"MoE layer (router, shared expert, {len(sample)} of the {touched.numel()} "
+                f"touched routed experts scaled to all), the layer-0 dense MLP and "
+                f"1/{self.LM_HEAD_FRACTION} of the lm_head rows; per-step time extrapolated to "
+                f"{self.n_kda} KDA + {self.n_mla} MLA blocks, {self.n_moe} MoE layers, layer 0 "
+                f"and the full lm_head")
+        return total, desc, torch.get_num_threads()
+
+
+def cpu_median(sampler, warmup: int = 3, runs: int = 10) -> tuple[float, str, int, int]:
+    """Median seconds per step of ``sampler`` after ``warmup`` untimed samples."""
+    for _ in range(warmup):
+        sampler.seconds_per_step()
+    times, desc, cores = [], "", 1
+    for _ in range(runs):
+        t, desc, cores = sampler.seconds_per_step()
+        times.append(t)
+    return statistics.median(times), desc, cores, runs
+
+
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
@@ -371,64 +623,28 @@ def _max_over_ranks(value: float, dist) -> float:
     return float(t.item())
 
 
-def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
-    import __graft_entry__ as entry
+def _profile_traffic_ratio() -> tuple[float | None, str | None]:
+    """DRAM traffic over algorithmic bytes of step_kernel from the committed ncu
+    summary (profiles/step_kernel_traffic.txt: 'key value' lines)."""
+    path = ROOT / "profiles" / "step_kernel_traffic.txt"
+    try:
+        vals = {}
+        for line in path.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and not line.startswith("#"):
+                vals[parts[0]] = float(parts[1])
+        return vals["dram_bytes"] / vals["algorithmic_bytes"], str(path.relative_to(ROOT))
+    except Exception:
+        return None, None
 
-    entry.build()
-    from local_kimi_b200 import _lib
-    from local_kimi_b200.decode import HotPathDecoder
-    from local_kimi_b200.step import MAX_TOKENS
 
-    torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local_rank))
-    _lib.set_pdl(not args.no_pdl)
-
-    model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
-    counts = model.touched_experts(model.x0)
-    bytes_step = model.step_bytes(counts)
-    static_x = model.x0.clone()
-    use_executor = args.path == "executor" and args.batch <= MAX_TOKENS
-
-    # Per-operation path: the step's registry-level launches in one CUDA graph.
-    graph, graph_out = _capture(model.step, static_x)
-    per_op_s = _max_over_ranks(_time_graph(graph, max(10, args.steps // 2), 3), dist)
-
-    if use_executor:
-        prog, buf = model.build_program(static_x)
-        out_buf = buf["logits"]
-        # Parity of the two paths on one step from the same KDA states.
-        states = [lw.kda_state.clone() for lw in model.layers if lw.kda_state is not None]
-        graph.replay()
-        torch.cuda.synchronize()
-        ref = graph_out.float().clone()
-        for lw, st in zip([lw for lw in model.layers if lw.kda_state is not None], states):
-            lw.kda_state.copy_(st)
-        prog.launch()
-        torch.cuda.synchronize()
-        diff = (out_buf.float() - ref).abs()
-        tol = torch.maximum(torch.full_like(ref, 1e-3), 2e-2 * ref.abs())
-        parity = float((diff <= tol).float().mean().item())
-        step_fn = prog.launch
-        launches = 1
-        path = "executor"
-    else:
-        out_buf = graph_out
-        step_fn = graph.replay
-        launches = model.launches_per_step
-        parity = None
-        path = "per-op graph"
-
-    # Timed region: K steps.
+def _timed(step_fn, steps: int, warmup: int, dist, local_rank: int) -> tuple[float, dict]:
+    """Seconds per step (device time, max over ranks) of ``steps`` calls after
+    ``warmup`` untimed ones, barrier and synchronize on both sides; the SM
+    clocks are sampled during the timed region."""
     if dist is not None:
         dist.barrier()
-    for _ in range(args.warmup):
+    for _ in range(max(warmup, 3)):
         step_fn()
     torch.cuda.synchronize()
     if dist is not None:
@@ -437,17 +653,22 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             step_fn()
         end.record()
         torch.cuda.synchronize()
-    step_s = _max_over_ranks(start.elapsed_time(end) / 1e3 / args.steps, dist)
+    step_s = _max_over_ranks(start.elapsed_time(end) / 1e3 / steps, dist)
     if dist is not None:
         dist.barrier()
+    return step_s, clocks.summary()
 
-    # End to end: pinned host input in, logits out, every step.
+
+def _e2e(step_fn, static_x: torch.Tensor, x_host: torch.Tensor, out_buf: torch.Tensor,
+         steps: int, dist) -> tuple[float, int, int]:
+    """The step through the public API with the input copied host->device and
+    the logits device->host (pinned buffers) every step."""
     host_x = torch.empty(static_x.shape, dtype=static_x.dtype, pin_memory=True)
-    host_x.copy_(model.x0.cpu())
+    host_x.copy_(x_host)
     host_out = torch.empty(out_buf.shape, dtype=out_buf.dtype, pin_memory=True)
 
     def e2e_step():
@@ -455,68 +676,283 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         step_fn()
         host_out.copy_(out_buf, non_blocking=True)
 
-    e2e_s = _max_over_ranks(_time_launches(e2e_step, max(1, args.steps), 2), dist)
+    if dist is not None:
+        dist.barrier()
+    e2e_s = _max_over_ranks(_time_launches(e2e_step, max(1, steps), 2), dist)
+    return (e2e_s, host_x.numel() * host_x.element_size(),
+            host_out.numel() * host_out.element_size())
 
+
+def _capture_all(fn, x, dist):
+    """Capture fn(x) in a CUDA graph on every rank, or on none: each rank tries,
+    then the ranks agree (MIN of the outcomes) before any replay.  Capture
+    records collectives without running them, so a failed capture on one rank
+    leaves no other rank waiting."""
+    graph, out, ok = None, None, 1
+    try:
+        graph, out = _capture(fn, x)
+    except Exception:
+        graph, out, ok = None, None, 0
+        torch.cuda.synchronize()
+    if dist is not None:
+        flag = torch.tensor([ok], device="cuda", dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = int(flag.item())
+    if not ok:
+        graph, out = None, None
+    return graph, out
+
+
+def _ep_step_bytes(model) -> dict[str, int]:
+    """Algorithmic bytes of one expert-parallel step on this rank: every dense
+    matrix and the lm_head once, the routers, the local experts the step
+    touched (plus the shared expert) per MoE layer, the KDA states read and
+    written, activations in and out."""
+    out = model.step_bytes([1] * sum(1 for lw in model.layers if lw.moe is not None))
+    expert_bytes = 0
+    for li, ep in (model.ep_layers or {}).items():
+        b = ep.bank
+        per_expert = sum(t[0].numel() * t.element_size() for t in (
+            b.w1_packed, b.w1_scales, b.w2_packed, b.w2_scales, b.w3_packed, b.w3_scales))
+        expert_bytes += per_expert * (ep.touched_local_experts() + 1)
+    out["total"] += expert_bytes - out["experts"]
+    out["experts"] = expert_bytes
+    return out
+
+
+def _ep_launches(model) -> int:
+    """This library's kernel launches in one expert-parallel step (the NCCL
+    exchanges and torch's small copies not counted)."""
+    from local_kimi_b200 import ops
+
+    s, b = model.shape, model.batch
+    tc = lambda n, k: ops.prefer_tc(b, n, k, model.group)  # noqa: E731
+    proj = s.kda_heads * s.kda_head_dim
+    n = 1  # lm_head
+    for lw in model.layers:
+        if lw.kind == "kda":
+            n += (3 if tc(proj, s.hidden) else 1) + 2
+        else:
+            both = tc(s.mla_heads * s.mla_q_head_dim, s.hidden) and tc(
+                s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
+            n += (2 if both else 1) + 1
+        n += 2 if lw.dense_mlp is not None else 7
+    return n
+
+
+def _roofline(nbytes: int, step_s: float, kernel: str, traffic=None, traffic_source=None):
     peak, peak_src = _peak_hbm()
-    achieved = bytes_step["total"] / step_s / 1e9
+    achieved = nbytes / step_s / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "traffic_source": traffic_source, "kernel": kernel, "peak_source": peak_src,
+            "bytes_per_launch": nbytes}
+
+
+def _bs1_record(base, args, with_cpu: bool) -> dict:
+    """Batch 1 on the decode-step executor (the whole step in one persistent
+    launch), the same step as per-operation launches in a CUDA graph beside it,
+    the two paths' logits compared; roofline against the measured HBM peak."""
+    model = base.with_batch(1, seed=0)
+    counts = model.touched_experts(model.x0)
+    nbytes = model.step_bytes(counts)
+    static_x = model.x0.clone()
+    graph, graph_out = _capture(model.step, static_x)
+    per_op_s = _time_graph(graph, max(10, args.steps // 2), 3)
+    prog, buf = model.build_program(static_x)
+    out_buf = buf["logits"]
+    kda = [lw for lw in model.layers if lw.kda_state is not None]
+    states = [lw.kda_state.clone() for lw in kda]
+    graph.replay()
+    torch.cuda.synchronize()
+    ref = graph_out.float().clone()
+    for lw, st in zip(kda, states):
+        lw.kda_state.copy_(st)
+    prog.launch()
+    torch.cuda.synchronize()
+    diff = (out_buf.float() - ref).abs()
+    tol = torch.maximum(torch.full_like(ref, 1e-3), 2e-2 * ref.abs())
+    parity = float((diff <= tol).float().mean().item())
+    del graph
+    step_s, clocks = _timed(prog.launch, args.steps, args.warmup, None, 0)
+    e2e_s, h2d, d2h = _e2e(prog.launch, static_x, model.x0.cpu(), out_buf, args.steps, None)
+    ratio, src = _profile_traffic_ratio()
+    rec = {
+        "workload": "C4 hot-path decode step at batch 1 on the decode-step executor",
+        "value": round(1 / step_s, 2), "unit": "tok/s", "ms_per_step": round(step_s * 1e3, 4),
+        "e2e": {"value": round(1 / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": _roofline(nbytes["total"], step_s,
+                              "step_kernel (the whole step in one launch)",
+                              int(nbytes["total"] * ratio) if ratio else None,
+                              f"ncu dram bytes / algorithmic bytes of {src}, times this "
+                              f"step's algorithmic bytes" if ratio else None),
+        "per_op_graph": {"ms_per_step": round(per_op_s * 1e3, 4),
+                         "value": round(1 / per_op_s, 2),
+                         "launches_per_step": model.launches_per_step},
+        "parity_vs_per_op": round(parity, 6), "launches_per_step": 1,
+        "gpu_launches": args.steps, "step_bytes": nbytes, "clocks": clocks,
+    }
+    if with_cpu:
+        cpu_s, desc, cores = CpuSample(1, args.group, model).seconds_per_step()
+        rec["cpu_baseline"] = {"value": round(1 / cpu_s, 4), "unit": "tok/s", "cores": cores,
+                               "kind": "port", "sample": desc + " (one sample)"}
+    return rec
+
+
+def _batch_record(base, batch: int, args) -> dict:
+    """A batch of ``batch`` tokens through the per-operation path (registry
+    ops: the projection engine for few tokens, the tcgen05 tensor-core path for
+    many) captured in one CUDA graph."""
+    model = base.with_batch(batch, seed=batch)
+    counts = model.touched_experts(model.x0)
+    nbytes = model.step_bytes(counts)
+    static_x = model.x0.clone()
+    graph, out_buf = _capture(model.step, static_x)
+    step_s, clocks = _timed(graph.replay, args.steps, args.warmup, None, 0)
+    e2e_s, h2d, d2h = _e2e(graph.replay, static_x, model.x0.cpu(), out_buf, args.steps, None)
+    del graph
+    return {
+        "workload": f"C4 hot-path decode step at batch {batch}, per-operation CUDA graph",
+        "value": round(batch / step_s, 2), "unit": "tok/s",
+        "ms_per_step": round(step_s * 1e3, 4),
+        "e2e": {"value": round(batch / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": _roofline(nbytes["total"], step_s, "all launches of the step"),
+        "launches_per_step": model.launches_per_step, "step_bytes": nbytes, "clocks": clocks,
+    }
+
+
+def _sweep_record(args) -> dict:
+    """The C2 dense sweep at M 1, 16 and 64 through the registry op (engine or
+    tensor-core path by shape): time, HBM GB/s and fraction of the peak."""
+    from local_kimi_b200 import ops
+
+    peak, _ = _peak_hbm()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    points = []
+    for name, k, n in (("qkv", 2304, 12288), ("o_proj", 4096, 2304),
+                       ("shared_gate_up", 2304, 2048), ("lm_head", 2304, 163840)):
+        w = (0.02 * torch.randn((n, k), generator=gen, device="cuda")).to(torch.bfloat16)
+        packed, scales = ops.quantise(w, args.group)
+        del w
+        wbytes = packed.numel() + scales.numel() * 2
+        copies = [(packed.clone(), scales.clone())
+                  for _ in range(max(1, -(-400 * 2**20 // wbytes)))]
+        for m in (1, 16, 64):
+            x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+            t = _time_copies(ops.w4a16_dense, x, copies, 3)
+            gbs = (wbytes + 2 * m * k + 2 * m * n) / t / 1e9
+            path = "tc" if ops.prefer_tc(m, n, k, args.group) else "engine"
+            points.append({"shape": name, "M": m, "path": path, "us": round(t * 1e6, 2),
+                           "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)})
+        del copies, packed, scales
+        torch.cuda.empty_cache()
+    return {"timing": "CUDA-graph replay over weight copies > 400 MB", "points": points}
+
+
+WORKLOAD = ("C5 batch decode: {total} concurrent sequences in total ({per} per rank), the "
+            "Kimi-Linear-48B-A3B W4A16 hot-path decode step (27 layers: INT4 attention "
+            "projections, KDA state step, MoE router + experts + combine, INT4 lm_head) with "
+            "every MoE layer expert-parallel over the {world} rank(s) ({experts} routed experts "
+            "per rank, fixed-capacity exchange, NCCL all-to-all over NVLink); norms, short "
+            "conv, gates, MLA softmax attention and BF16 projections not computed")
+
+
+def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import __graft_entry__ as entry
+
+    entry.build()
+    from local_kimi_b200 import _lib
+    from local_kimi_b200.decode import HotPathDecoder
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+        group = dist.group.WORLD
+    _lib.set_pdl(not args.no_pdl)
+    if args.total_batch % world:
+        raise SystemExit("--total-batch must divide over the ranks")
+    per = args.total_batch // world
+
+    base = HotPathDecoder(1, group=args.group, layers=args.layers, seed=0)
+    # Each rank's own sequences (the weights are the same on every rank).
+    model = base.with_batch(per, seed=100 + rank)
+    records = {}
+    if world == 1 and not args.headline_only:
+        records["bs1"] = _bs1_record(base, args, with_cpu=False)
+        records["bs32"] = _batch_record(base, 32, args)
+        if not args.no_sweep:
+            records["dense_sweep"] = _sweep_record(args)
+    model.enable_expert_parallel(group)
+    static_x = model.x0.clone()
+    model.step(static_x)                         # routing for the byte count
+    torch.cuda.synchronize()
+    nbytes = _ep_step_bytes(model)
+    graph, graph_out = _capture_all(model.step, static_x, dist)
+    if graph is not None:
+        step_fn, out_buf, launch = graph.replay, graph_out, "one CUDA graph per step"
+    else:
+        holder = {}
+
+        def step_fn():
+            holder["out"] = model.step(static_x)
+
+        step_fn()
+        torch.cuda.synchronize()
+        out_buf, launch = holder["out"], "eager launches (graph capture unavailable)"
+    step_s, clocks = _timed(step_fn, args.steps, args.warmup, dist, local_rank)
+    e2e_s, h2d, d2h = _e2e(step_fn, static_x, model.x0.cpu(), out_buf, args.steps, dist)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_s, sample, cores = CpuSample(args.batch, args.group, model).seconds_per_step()
-        cpu = {"value": round(args.batch / cpu_s, 4), "unit": "tok/s", "cores": cores,
-               "kind": "port", "sample": sample, "seconds_per_step": round(cpu_s, 3)}
-
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.headline_only):
+        cpu_s, desc, cores, runs = cpu_median(BatchCpuSample(per, args.group))
+        cpu = {"value": round(per / cpu_s, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": desc + f"; median of {runs} samples after 3 warm-ups",
+               "seconds_per_step": round(cpu_s, 3)}
+    per_layer_launches = 9                        # router, dispatch, 2 exchanges, 2+2 expert, combine
     out = {
         "metric": METRIC,
-        "value": round(world * args.batch / step_s, 2),
+        "value": round(args.total_batch / step_s, 2),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (random-init weights of the real shapes, seeded)",
+        "data": "synthetic (random-init weights of the real shapes, seeded; per-rank tokens)",
         "config": {
-            "workload": ("C4 hot path: Kimi-Linear-48B-A3B W4A16 decode step, 27 layers "
-                         "(INT4 attention projections, KDA state step, MoE router + "
-                         "experts + combine, INT4 lm_head); norms, short conv, gates, MLA "
-                         "softmax attention and BF16 projections not computed"),
-            "batch": args.batch,
-            "group_size": args.group,
-            "layers": model.nlayers,
-            "path": path,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
-            "weights_gb": round(model.weight_bytes() / 1e9, 2),
-            "bytes_per_step": bytes_step["total"],
-            "l2": "inputs larger than L2 (each step streams ~1.7 GB of weights)",
+            "workload": WORKLOAD.format(total=args.total_batch, per=per, world=world,
+                                        experts=256 // world),
+            "total_batch": args.total_batch, "batch_per_rank": per,
+            "group_size": args.group, "layers": model.nlayers,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "launch": launch,
+            "l2": "inputs larger than L2 (each step streams GBs of weights and KDA state)",
         },
-        "e2e": {"value": round(world * args.batch / e2e_s, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
-                "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": (int(bytes_step["total"] * STEP_TRAFFIC_RATIO) if use_executor
-                                 else None),
-                     "traffic_source": ("ncu dram bytes of a 3-layer capture, scaled by bytes"
-                                        if use_executor else None),
-                     "kernel": ("step_kernel (the whole step in one launch)" if use_executor
-                                else "all launches of the step"),
-                     "peak_source": peak_src, "bytes_per_launch": bytes_step["total"]},
-        "gpu_launches": launches * args.steps,
-        "launches_per_step": launches,
-        "per_op_graph": {"ms_per_step": round(per_op_s * 1e3, 4),
-                         "value": round(world * args.batch / per_op_s, 2),
-                         "launches_per_step": model.launches_per_step},
-        "step_bytes": bytes_step,
-        "clocks": clocks.summary(),
+        "e2e": {"value": round(args.total_batch / e2e_s, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": _roofline(nbytes["total"], step_s,
+                              "all launches of the step (rank 0's bytes)"),
+        "gpu_launches": _ep_launches(model) * args.steps,
+        "launches_per_step": _ep_launches(model),
+        "step_bytes": nbytes,
+        "clocks": clocks,
     }
-    if parity is not None:
-        out["parity_vs_per_op"] = round(parity, 6)
     if cpu is not None:
         out["cpu_baseline"] = cpu
+    out.update(records)
     if dist is not None:
         del graph
         dist.destroy_process_group()
@@ -524,20 +960,16 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
 
 
 def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
-    """The reference path restated in oracle/, on the host cores (rank 0 only)."""
+    """The reference path restated in oracle/ on the host cores (rank 0 only),
+    on the b200 arm's workload: each step a bounded sample of the batch decode
+    step (BatchCpuSample), extrapolated."""
     if rank != 0:
         return None
-    sample = CpuSample(args.batch, args.group)
-    warm = min(args.warmup, 1)
-    for _ in range(warm):
-        sample.seconds_per_step()
-    steps = max(1, min(args.steps, 3))
-    times, desc, cores = [], "", 1
-    for _ in range(steps):
-        t, desc, cores = sample.seconds_per_step()
-        times.append(t)
-    step_s = statistics.median(times)
-    value = round(args.batch / step_s, 4)
+    sample = BatchCpuSample(args.total_batch, args.group)
+    warm = max(args.warmup, 3)
+    steps = max(1, args.steps)
+    step_s, desc, cores, _ = cpu_median(sample, warmup=warm, runs=steps)
+    value = round(args.total_batch / step_s, 4)
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -548,14 +980,15 @@ def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": warm,
         "ms_per_step": round(step_s * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random-init weights of the real shapes, seeded)",
-        "config": {"workload": "C4 hot path decode step (see the b200 arm), CPU sample",
-                   "batch": args.batch, "group_size": args.group},
+        "config": {"workload": WORKLOAD.format(total=args.total_batch, per=args.total_batch,
+                                               world=1, experts=256) + " (CPU sample)",
+                   "total_batch": args.total_batch, "group_size": args.group},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": desc},
+                         "sample": desc + f"; median of {steps} samples after {warm} warm-ups"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -839,7 +1272,10 @@ def run_ep_moe(args, rank: int, world: int, local_rank: int) -> dict | None:
     t = torch.tensor([start.elapsed_time(end) / 1e3 / args.steps], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dist.barrier()
-    send, recv = ep.last_counts
+    ids = ops.payload_ids(ep.last_payload)[:, 0]
+    cap = ids.numel() // world
+    send = [int((ids[d * cap:(d + 1) * cap] >= 0).sum()) for d in range(world)]
+    recv = [int(ep.touched_local_experts())]
     dist.destroy_process_group()
     if rank != 0:
         return None
@@ -851,7 +1287,8 @@ def run_ep_moe(args, rank: int, world: int, local_rank: int) -> dict | None:
             "config": {"tokens": args.batch, "tokens_per_rank": per, "experts": E,
                        "experts_per_rank": E // world, "hidden": H, "intermediate": I,
                        "top_k": 8, "group_size": args.group,
-                       "rank0_rows_sent_per_dest": send, "rank0_rows_received": sum(recv),
+                       "rank0_rows_sent_per_dest": send,
+                       "rank0_local_experts_touched": recv[0],
                        "data": "synthetic (random-init weights and hidden states, seeded)"}}
 
 

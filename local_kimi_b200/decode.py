@@ -172,11 +172,58 @@ class HotPathDecoder:
                                     device=self.device).to(torch.bfloat16)
         self.dense_idx = torch.zeros((B, 1), dtype=torch.long, device=self.device)
 
+    # -- batch views and expert parallelism -------------------------------------------
+    def with_batch(self, batch: int, seed: int | None = None) -> "HotPathDecoder":
+        """A decoder for ``batch`` tokens sharing this one's weights (no copy):
+        new KDA states and synthetic inputs, the same quantised matrices."""
+        import copy
+
+        other = copy.copy(self)
+        other.batch = batch
+        g = torch.Generator(device=self.device)
+        g.manual_seed(1000 + batch if seed is None else seed)
+        s = self.shape
+        other.layers = []
+        for lw in self.layers:
+            nl = copy.copy(lw)
+            if lw.kda_state is not None:
+                nl.kda_state = 0.05 * torch.randn(
+                    (batch, s.kda_heads, s.kda_head_dim, s.kda_head_dim), generator=g,
+                    device=self.device)
+            other.layers.append(nl)
+        other.ep_layers = None
+        other._make_inputs((seed if seed is not None else 1) + 1)
+        return other
+
+    def enable_expert_parallel(self, group=None) -> None:
+        """Run every MoE layer through ExpertParallelMoE over ``group`` (one
+        process per GPU; without an initialised process group, one GPU).  The
+        routed experts of a layer are sharded over the ranks; a rank keeps only
+        its shard of each bank."""
+        from .ep import ExpertParallelMoE
+
+        self.ep_layers = {}
+        for li, lw in enumerate(self.layers):
+            if lw.moe is None:
+                continue
+            ep = ExpertParallelMoE(lw.moe, group=group)
+            self.ep_layers[li] = ep
+            if ep.world > 1:
+                m = lw.moe
+                # The full bank is no longer needed on this rank.
+                lw.moe = MoELayerWeights(m.router_weight, m.router_bias, m.w1_packed[:0],
+                                         m.w1_scales[:0], m.w2_packed[:0], m.w2_scales[:0],
+                                         m.w3_packed[:0], m.w3_scales[:0], top_k=m.top_k,
+                                         scaling=m.scaling)
+                ep.layer = lw.moe
+        torch.cuda.empty_cache()
+
     # -- one step --------------------------------------------------------------------
     def step(self, x: torch.Tensor) -> torch.Tensor:
         """x bf16 [B, hidden] -> logits bf16 [B, vocab]."""
         s = self.shape
-        for lw in self.layers:
+        eps = getattr(self, "ep_layers", None)
+        for li, lw in enumerate(self.layers):
             if lw.kind == "kda":
                 ops.w4a16_dense_multi([(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
                 ops.kda_decode_step(lw.kda_state, self.kda_q, self.kda_k, self.kda_v,
@@ -191,6 +238,8 @@ class HotPathDecoder:
                 (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
                 act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
                 x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
+            elif eps is not None:
+                x = eps[li].forward(h)
             else:
                 x, _, _ = moe_forward(h, lw.moe)
         return ops.w4a16_dense(x, *self.lm_head)
@@ -309,8 +358,9 @@ class HotPathDecoder:
                 out["dense_proj"] += sum(_bytes(t) for t in (w1p, w1s, w3p, w3s, w2p, w2s))
             if lw.moe is not None:
                 m = lw.moe
-                per_expert = sum(_bytes(t[0]) for t in (m.w1_packed, m.w1_scales, m.w2_packed,
-                                                        m.w2_scales, m.w3_packed, m.w3_scales))
+                per_expert = (sum(_bytes(t[0]) for t in (m.w1_packed, m.w1_scales, m.w2_packed,
+                                                         m.w2_scales, m.w3_packed, m.w3_scales))
+                              if m.w1_packed.shape[0] else 0)  # bank sharded away
                 touched = (expert_counts[moe_i] if expert_counts is not None
                            else min(s.experts + 1, B * s.top_k + 1))
                 out["experts"] += per_expert * touched

@@ -122,12 +122,36 @@ class ExpertParallelMoE:
 
     def __init__(self, layer: MoELayerWeights, group=None, backend=None):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        # Without a process group the layer runs on one GPU: the same data
+        # plane with the exchanges reduced to identities and the bank used in
+        # place.
+        self.single = group is None and not (dist.is_available() and dist.is_initialized())
+        self.rank = 0 if self.single else dist.get_rank(group)
+        self.world = 1 if self.single else dist.get_world_size(group)
         self.layer = layer
-        self.bank = shard_bank(layer, self.rank, self.world)
+        if self.world == 1:
+            self.bank = LocalExpertBank(0, layer.num_experts, layer.w1_packed, layer.w1_scales,
+                                        layer.w3_packed, layer.w3_scales, layer.w2_packed,
+                                        layer.w2_scales)
+        else:
+            self.bank = shard_bank(layer, self.rank, self.world)
         self.backend = backend if backend is not None else CudaExperts()
         self.last_payload: torch.Tensor | None = None
+        self.last_received: torch.Tensor | None = None
+
+    def _exchange(self, tensor: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return tensor
+        out = torch.empty_like(tensor)
+        dist.all_to_all_single(out, tensor.contiguous(), group=self.group)
+        return out
+
+    def touched_local_experts(self) -> int:
+        """Distinct local experts the last forward's received rows used (host read)."""
+        if self.last_received is None:
+            return 0
+        ids = ops.payload_ids(self.last_received)[:, 0]
+        return int(torch.unique(ids[ids >= 0]).numel())
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
         """hidden bf16 [T, H] (this rank's tokens) -> bf16 [T, H]."""
@@ -138,11 +162,9 @@ class ExpertParallelMoE:
         routed = stable[:, :k].contiguous()
         capacity = max(1, tokens * k)
         payload, slots = be.dispatch(hidden, routed, bank.per_rank, self.world, capacity)
-        self.last_payload = payload
-        received = torch.empty_like(payload)
-        dist.all_to_all_single(received, payload, group=self.group)
+        received = self._exchange(payload)
+        self.last_payload, self.last_received = payload, received
         y_recv = be.experts(received, bank)
-        y_back = torch.empty_like(y_recv)
-        dist.all_to_all_single(y_back, y_recv.contiguous(), group=self.group)
+        y_back = self._exchange(y_recv)
         y_shared = be.shared(hidden, bank)
         return be.combine(y_back, slots, weights, y_shared)
