@@ -65,6 +65,9 @@ def _args() -> argparse.Namespace:
                     help="leave the dense-sweep sub-record out of the N=1 line")
     ap.add_argument("--headline-only", action="store_true",
                     help="only the benchmark step (no sub-records, no CPU baseline)")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after the timing, run one eager benchmark step between "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--group", type=int, default=128)
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (testing only)")
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
@@ -912,6 +915,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
     step_s, clocks = _timed(step_fn, args.steps, args.warmup, dist, local_rank)
     e2e_s, h2d, d2h = _e2e(step_fn, static_x, model.x0.cpu(), out_buf, args.steps, dist)
 
+    if args.profile_step:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        model.step(static_x)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.headline_only):
         cpu_s, desc, cores, runs = cpu_median(BatchCpuSample(per, args.group))

@@ -95,9 +95,24 @@ class CudaExperts:
         width = payload.shape[1] - 8
         rows = payload[:, :width]
         idx = ops.payload_ids(payload).contiguous()
-        act = ops.w4a16_swiglu(rows, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed,
-                               bank.w3_scales)
-        return ops.w4a16_grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
+        tc = self.use_tc(payload.shape[0], bank)
+        swiglu = ops.w4a16_swiglu_tc if tc else ops.w4a16_swiglu
+        grouped = ops.w4a16_grouped_tc if tc else ops.w4a16_grouped
+        act = swiglu(rows, idx, bank.w1_packed, bank.w1_scales, bank.w3_packed, bank.w3_scales)
+        return grouped(act[:, 0], idx, bank.w2_packed, bank.w2_scales)[:, 0]
+
+    @staticmethod
+    def use_tc(slots: int, bank: LocalExpertBank) -> bool:
+        """Tensor-core path for the received rows when the exchange buffer holds
+        several rows per local expert on average (upper bound of the real load:
+        the buffer includes empty slots): its units share each activation chunk
+        across 256 weight rows, the engine restages it per 16."""
+        if slots < 4 * bank.per_rank:
+            return False
+        h = bank.w1_packed.shape[2] * 2
+        inter = bank.w1_packed.shape[1]
+        return (ops.tc_supported(slots, inter, h, h // bank.w1_scales.shape[2])
+                and ops.tc_supported(slots, h, inter, inter // bank.w2_scales.shape[2]))
 
     def shared(self, hidden: torch.Tensor, bank: LocalExpertBank) -> torch.Tensor:
         """The shared expert (local bank slot per_rank) on this rank's tokens, bf16 [T, H]."""

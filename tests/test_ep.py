@@ -240,6 +240,35 @@ def test_dispatch_and_combine_kernels_match_cpu_restatement(cuda, world, tokens)
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("tokens", [64, 200])
+def test_single_gpu_expert_parallel_layer_matches_oracle(cuda, tokens):
+    # The layer without a process group (one GPU: the same data plane with the
+    # exchanges as identities) at decode widths, where the received rows run
+    # on the tensor-core path, against the oracle layer.
+    from local_kimi_b200.ep import CudaExperts
+    from local_kimi_b200.moe import MoELayerWeights as W
+    from tests.conftest import assert_close
+    from tests.gpu_util import cuda_gen, quant_bank, rand_act, rand_weight
+
+    gen = cuda_gen(600 + tokens)
+    experts, hid, inter = 16, 2304, 1024
+    w1 = quant_bank(experts + 1, inter, hid, 128, gen)
+    w2 = quant_bank(experts + 1, hid, inter, 128, gen)
+    w3 = quant_bank(experts + 1, inter, hid, 128, gen)
+    router = rand_weight((experts, hid), gen)
+    bias = 0.01 * torch.randn(experts, generator=gen, device=cuda)
+    layer = W(router, bias, *w1, *w2, *w3, top_k=4, scaling=2.446)
+    ep = ExpertParallelMoE(layer)
+    assert ep.world == 1 and CudaExperts.use_tc(tokens * 4, ep.bank)
+    x = rand_act((tokens, hid), gen)
+    out = ep.forward(x)
+    banks = omoe.MoEBanks(router.cpu(), bias.cpu(), w1[0].cpu(), w1[1].cpu(), w2[0].cpu(),
+                          w2[1].cpu(), w3[0].cpu(), w3[1].cpu(), top_k=4, scaling=2.446)
+    ref, idx, _, bound = omoe.moe_layer(x.cpu(), banks, return_parts=True, lane_order=True)
+    assert_close(out, ref, what=f"single-GPU EP layer T={tokens}", allowance=bound)
+
+
+@pytest.mark.gpu
 @pytest.mark.timeout(300)
 def test_expert_parallel_one_nccl_rank_matches_single_gpu(cuda):
     mp.spawn(_gpu_rank, args=(1, _free_port(), 5), nprocs=1, join=True)
