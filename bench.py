@@ -687,20 +687,16 @@ def _e2e(step_fn, static_x: torch.Tensor, x_host: torch.Tensor, out_buf: torch.T
 
 
 def _capture_all(fn, x, dist):
-    """Capture fn(x) in a CUDA graph on every rank, or on none: each rank tries,
-    then the ranks agree (MIN of the outcomes) before any replay.  Capture
-    records collectives without running them, so a failed capture on one rank
-    leaves no other rank waiting."""
+    """Capture fn(x) in a CUDA graph (one process).  With several ranks the
+    step runs as eager launches: its NCCL exchanges are not captured."""
+    if dist is not None:
+        return None, None
     graph, out, ok = None, None, 1
     try:
         graph, out = _capture(fn, x)
     except Exception:
         graph, out, ok = None, None, 0
         torch.cuda.synchronize()
-    if dist is not None:
-        flag = torch.tensor([ok], device="cuda", dtype=torch.int32)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        ok = int(flag.item())
     if not ok:
         graph, out = None, None
     return graph, out
@@ -856,11 +852,17 @@ def _sweep_record(args) -> dict:
 
 
 WORKLOAD = ("C5 batch decode: {total} concurrent sequences in total ({per} per rank), the "
-            "Kimi-Linear-48B-A3B W4A16 hot-path decode step (27 layers: INT4 attention "
+            "Kimi-Linear-48B-A3B W4A16 hot-path decode step ({layers} layers: INT4 attention "
             "projections, KDA state step, MoE router + experts + combine, INT4 lm_head) with "
             "every MoE layer expert-parallel over the {world} rank(s) ({experts} routed experts "
             "per rank, fixed-capacity exchange, NCCL all-to-all over NVLink); norms, short "
             "conv, gates, MLA softmax attention and BF16 projections not computed")
+
+
+def _progress(rank: int, what: str) -> None:
+    """One line per phase on stderr, so that a stalled run shows where it stopped."""
+    print(f"[bench] rank {rank} {time.strftime('%H:%M:%S')} {what}", file=sys.stderr,
+          flush=True)
 
 
 def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -886,6 +888,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         raise SystemExit("--total-batch must divide over the ranks")
     per = args.total_batch // world
 
+    _progress(rank, f"process group ready ({world} rank(s)); building weights")
     base = HotPathDecoder(1, group=args.group, layers=args.layers, seed=0)
     # Each rank's own sequences (the weights are the same on every rank).
     model = base.with_batch(per, seed=100 + rank)
@@ -895,9 +898,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         records["bs32"] = _batch_record(base, 32, args)
         if not args.no_sweep:
             records["dense_sweep"] = _sweep_record(args)
+    _progress(rank, "weights built; sub-records done; sharding experts")
     model.enable_expert_parallel(group)
     static_x = model.x0.clone()
     model.step(static_x)                         # routing for the byte count
+    _progress(rank, "first expert-parallel step done")
     torch.cuda.synchronize()
     nbytes = _ep_step_bytes(model)
     graph, graph_out = _capture_all(model.step, static_x, dist)
@@ -912,8 +917,10 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         step_fn()
         torch.cuda.synchronize()
         out_buf, launch = holder["out"], "eager launches (graph capture unavailable)"
+    _progress(rank, f"timing ({launch})")
     step_s, clocks = _timed(step_fn, args.steps, args.warmup, dist, local_rank)
     e2e_s, h2d, d2h = _e2e(step_fn, static_x, model.x0.cpu(), out_buf, args.steps, dist)
+    _progress(rank, "timed")
 
     if args.profile_step:
         torch.cuda.synchronize()
@@ -943,7 +950,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         "data": "synthetic (random-init weights of the real shapes, seeded; per-rank tokens)",
         "config": {
             "workload": WORKLOAD.format(total=args.total_batch, per=per, world=world,
-                                        experts=256 // world),
+                                        experts=256 // world, layers=model.nlayers),
             "total_batch": args.total_batch, "batch_per_rank": per,
             "group_size": args.group, "layers": model.nlayers,
             "parallelism": f"ep{world}" if world > 1 else "single",
@@ -994,7 +1001,7 @@ def run_reference(args, rank: int, world: int, local_rank: int) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic (random-init weights of the real shapes, seeded)",
         "config": {"workload": WORKLOAD.format(total=args.total_batch, per=args.total_batch,
-                                               world=1, experts=256) + " (CPU sample)",
+                                               world=1, experts=256, layers=27) + " (CPU sample)",
                    "total_batch": args.total_batch, "group_size": args.group},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
                          "sample": desc + f"; median of {steps} samples after {warm} warm-ups"},
