@@ -210,6 +210,26 @@ KB_API int kb_moe_combine_routes(const uint16_t* routes, int64_t T, int64_t R, i
                                  void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* KDA decode preparation (engine/klinear/attention.py:192-230; replaces the  */
+/* reference's fused_short_conv_triple + fused_kda_gates,                      */
+/* engine/kernels/kda_prepare.py:475-536, 618-665) in one launch.              */
+/* q_in/k_in/v_in: bf16 [B, H*D] projections (row stride in_stride); states:  */
+/* bf16 [B, H*D, 4] contiguous, updated in place (shift left, token last);    */
+/* weights: bf16 [H*D, 4]; raw_decay bf16 [B, H*D]; dt_bias fp32 [H*D];       */
+/* a_log fp32 [H]; raw_beta bf16 [B, H].  Outputs fp32: q, k (each head       */
+/* normalised by rsqrt(sum of squares + eps)), v, decay [B, H, D], beta       */
+/* [B, H] -- the inputs of kb_kda_decode_step.  D a multiple of 32, <= 256.   */
+/* ------------------------------------------------------------------------- */
+KB_API int kb_kda_prepare(const uint16_t* q_in, const uint16_t* k_in, const uint16_t* v_in,
+                          int64_t in_stride, uint16_t* q_state, uint16_t* k_state,
+                          uint16_t* v_state, const uint16_t* q_weight, const uint16_t* k_weight,
+                          const uint16_t* v_weight, const uint16_t* raw_decay,
+                          int64_t raw_decay_stride, const float* dt_bias, const float* a_log,
+                          const uint16_t* raw_beta, int64_t raw_beta_stride, int64_t B,
+                          int64_t H, int64_t D, float eps, float* q_out, float* k_out,
+                          float* v_out, float* decay_out, float* beta_out, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* Expert-parallel data plane (the layer of engine/klinear/moe.py:278-334 with */
 /* its experts sharded over ranks: expert e on rank e / per_rank).  Fixed-     */
 /* capacity exchange buffers, so no step needs a host-side count and the layer */

@@ -99,6 +99,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kb_moe_combine_routes": (
         c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "kb_kda_prepare": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+         c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p],
+    ),
     "kb_ep_dispatch": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,

@@ -71,6 +71,12 @@ class LayerWeights:
     o_proj: tuple[torch.Tensor, torch.Tensor] | None = None
     kda_state: torch.Tensor | None = None                        # fp32 [B, H, 128, 128]
     moe: MoELayerWeights | None = None
+    # KDA decode preparation: short-convolution weights and states of q, k, v
+    # (bf16 [C, 4] and [B, C, 4]), dt_bias fp32 [C], A_log fp32 [H]
+    conv_w: list[torch.Tensor] | None = None
+    conv_state: list[torch.Tensor] | None = None
+    dt_bias: torch.Tensor | None = None
+    a_log: torch.Tensor | None = None
     dense_mlp: tuple | None = None  # (w1p, w1s, w3p, w3s) banks [1, I, H/2], (w2p, w2s)
 
 
@@ -83,7 +89,12 @@ class HotPathDecoder:
 
     def __init__(self, batch: int, *, group: int = 128, device: str | torch.device = "cuda",
                  shape: KimiLinearShape | None = None, seed: int = 0,
-                 layers: int | None = None) -> None:
+                 layers: int | None = None, kda_prepare: bool = True) -> None:
+        # With kda_prepare the KDA inputs come from the layer's q/k/v
+        # projections through the short convolutions and gates
+        # (kb_kda_prepare); without it they are fixed synthetic tensors (the
+        # decode-step executor's programs use those).
+        self.kda_prepare = kda_prepare
         self.shape = shape or KimiLinearShape()
         self.batch = batch
         self.group = group
@@ -97,7 +108,7 @@ class HotPathDecoder:
             self.layers.append(self._make_layer(layer))
         self.lm_head = self._quant(s.vocab_size, s.hidden)
         self._make_inputs(seed + 1)
-        self.launches_per_step = self._count_launches()
+
 
     # -- weights ---------------------------------------------------------------
     def _randn(self, shape) -> torch.Tensor:
@@ -137,7 +148,14 @@ class HotPathDecoder:
                 o_proj=self._quant(s.hidden, proj),
                 kda_state=0.05 * torch.randn((B, s.kda_heads, s.kda_head_dim, s.kda_head_dim),
                                              generator=self._gen, device=self.device),
+                conv_w=[(0.3 * torch.randn((proj, 4), generator=self._gen,
+                                           device=self.device)).to(torch.bfloat16)
+                        for _ in range(3)],
+                dt_bias=torch.randn(proj, generator=self._gen, device=self.device),
+                a_log=torch.log(1.0 + 15.0 * torch.rand(s.kda_heads, generator=self._gen,
+                                                        device=self.device)),
             )
+            lw.conv_state = self._conv_states(B, self._gen)
         if layer < s.first_k_dense:
             w1 = self._bank(1, s.dense_intermediate, s.hidden)
             w3 = self._bank(1, s.dense_intermediate, s.hidden)
@@ -151,6 +169,11 @@ class HotPathDecoder:
             lw.moe = MoELayerWeights(router, torch.zeros(s.experts, device=self.device), *w1,
                                      *w2, *w3, top_k=s.top_k, scaling=s.routed_scaling_factor)
         return lw
+
+    def _conv_states(self, batch: int, gen: torch.Generator) -> list[torch.Tensor]:
+        proj = self.shape.kda_heads * self.shape.kda_head_dim
+        return [torch.randn((batch, proj, 4), generator=gen, device=self.device).to(
+            torch.bfloat16) for _ in range(3)]
 
     def _make_inputs(self, seed: int) -> None:
         s = self.shape
@@ -166,6 +189,11 @@ class HotPathDecoder:
                                                       device=self.device))
         self.kda_beta = torch.sigmoid(torch.randn((B, H), generator=g, device=self.device))
         self.kda_out = torch.empty((B, H * D), dtype=torch.bfloat16, device=self.device)
+        # outputs of the BF16 gate projections (f_a/f_b and b_proj, not on the
+        # INT4 path), fixed
+        self.raw_decay = torch.randn((B, H * D), generator=g, device=self.device).to(
+            torch.bfloat16)
+        self.raw_beta = torch.randn((B, H), generator=g, device=self.device).to(torch.bfloat16)
         self.mla_latent = torch.randn((B, s.kv_lora_rank), generator=g,
                                       device=self.device).to(torch.bfloat16)
         self.mla_attn = torch.randn((B, s.mla_heads * s.mla_v_head_dim), generator=g,
@@ -190,6 +218,7 @@ class HotPathDecoder:
                 nl.kda_state = 0.05 * torch.randn(
                     (batch, s.kda_heads, s.kda_head_dim, s.kda_head_dim), generator=g,
                     device=self.device)
+                nl.conv_state = self._conv_states(batch, g)
             other.layers.append(nl)
         other.ep_layers = None
         other._make_inputs((seed if seed is not None else 1) + 1)
@@ -219,15 +248,22 @@ class HotPathDecoder:
         torch.cuda.empty_cache()
 
     # -- one step --------------------------------------------------------------------
-    def step(self, x: torch.Tensor) -> torch.Tensor:
-        """x bf16 [B, hidden] -> logits bf16 [B, vocab]."""
+    def step(self, x: torch.Tensor, routes: list | None = None) -> torch.Tensor:
+        """x bf16 [B, hidden] -> logits bf16 [B, vocab].  With ``routes`` (a
+        list) the routed expert ids of every single-GPU MoE layer are appended."""
         s = self.shape
         eps = getattr(self, "ep_layers", None)
         for li, lw in enumerate(self.layers):
             if lw.kind == "kda":
-                ops.w4a16_dense_multi([(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
-                ops.kda_decode_step(lw.kda_state, self.kda_q, self.kda_k, self.kda_v,
-                                    self.kda_decay, self.kda_beta, scale=s.kda_head_dim ** -0.5,
+                q_in, k_in, v_in = ops.w4a16_dense_multi(
+                    [(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
+                if self.kda_prepare:
+                    kin = ops.kda_prepare(q_in, k_in, v_in, *lw.conv_state, *lw.conv_w,
+                                          self.raw_decay, lw.dt_bias, lw.a_log, self.raw_beta,
+                                          num_heads=s.kda_heads, head_dim=s.kda_head_dim)
+                else:
+                    kin = (self.kda_q, self.kda_k, self.kda_v, self.kda_decay, self.kda_beta)
+                ops.kda_decode_step(lw.kda_state, *kin, scale=s.kda_head_dim ** -0.5,
                                     out_bf16=self.kda_out)
                 h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
             else:
@@ -241,13 +277,19 @@ class HotPathDecoder:
             elif eps is not None:
                 x = eps[li].forward(h)
             else:
-                x, _, _ = moe_forward(h, lw.moe)
+                x, idx, _ = moe_forward(h, lw.moe)
+                if routes is not None:
+                    routes.append(idx)
         return ops.w4a16_dense(x, *self.lm_head)
+
+    @property
+    def launches_per_step(self) -> int:
+        return self._count_launches()
 
     def _count_launches(self) -> int:
         n = 1  # lm_head
         for lw in self.layers:
-            n += 3 if lw.kind == "kda" else 2
+            n += (4 if self.kda_prepare else 3) if lw.kind == "kda" else 2
             n += 2 if lw.dense_mlp is not None else 3
         return n
 
@@ -353,6 +395,9 @@ class HotPathDecoder:
                 out["dense_proj"] += _bytes(p) + _bytes(sc)
             if lw.kda_state is not None:
                 out["kda_state"] += 2 * _bytes(lw.kda_state)
+                if self.kda_prepare:
+                    # conv states read and written, q/k/v in, five fp32 outputs
+                    out["kda_state"] += sum(2 * _bytes(c) for c in lw.conv_state)
             if lw.dense_mlp is not None:
                 (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
                 out["dense_proj"] += sum(_bytes(t) for t in (w1p, w1s, w3p, w3s, w2p, w2s))
@@ -372,22 +417,14 @@ class HotPathDecoder:
         return out
 
     def touched_experts(self, x: torch.Tensor) -> list[int]:
-        """Distinct experts per MoE layer for input x (runs one step eagerly)."""
-        counts = []
-        s = self.shape
-        for lw in self.layers:
-            if lw.kind == "kda":
-                ops.kda_decode_step(lw.kda_state.clone(), self.kda_q, self.kda_k, self.kda_v,
-                                    self.kda_decay, self.kda_beta, scale=s.kda_head_dim ** -0.5,
-                                    out_bf16=self.kda_out)
-                h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
-            else:
-                h = ops.w4a16_dense(self.mla_attn, *lw.o_proj)
-            if lw.dense_mlp is not None:
-                (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
-                act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
-                x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
-            else:
-                x, idx, _ = moe_forward(h, lw.moe)
-                counts.append(int(torch.unique(idx).numel()) + 1)
-        return counts
+        """Distinct experts (routed + shared) per MoE layer for input x: one
+        step run eagerly with every recurrent state put back afterwards."""
+        saved = [(lw.kda_state.clone(), [c.clone() for c in lw.conv_state])
+                 for lw in self.layers if lw.kda_state is not None]
+        routes: list[torch.Tensor] = []
+        self.step(x, routes=routes)
+        for lw, (st, conv) in zip([lw for lw in self.layers if lw.kda_state is not None], saved):
+            lw.kda_state.copy_(st)
+            for c, c0 in zip(lw.conv_state, conv):
+                c.copy_(c0)
+        return [int(torch.unique(idx).numel()) + 1 for idx in routes]

@@ -772,6 +772,52 @@ def kda_decode_step(
 # ---------------------------------------------------------------------------
 
 
+def kda_prepare(q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor,
+                q_state: torch.Tensor, k_state: torch.Tensor, v_state: torch.Tensor,
+                q_weight: torch.Tensor, k_weight: torch.Tensor, v_weight: torch.Tensor,
+                raw_decay: torch.Tensor, dt_bias: torch.Tensor, a_log: torch.Tensor,
+                raw_beta: torch.Tensor, *, num_heads: int, head_dim: int, eps: float = 1e-6):
+    """KDA decode preparation (attention.py:192-230) in one launch: the three
+    width-4 short convolutions (states [B, C, 4] updated in place), then the
+    gates.  Returns fp32 (q, k, v, decay) [B, H, D] and beta [B, H]: the
+    inputs of ``kda_decode_step``.  Projections, states, weights, raw_decay and
+    raw_beta are bf16; dt_bias and a_log fp32 (a_log [H] or [1, 1, H, 1])."""
+    batch = q_in.shape[0]
+    c = num_heads * head_dim
+    bf = (q_in, k_in, v_in, q_state, k_state, v_state, q_weight, k_weight, v_weight, raw_decay,
+          raw_beta)
+    if any(t.dtype != torch.bfloat16 for t in bf):
+        raise TypeError("KDA prepare projections, states, weights and gate inputs must be BF16")
+    if dt_bias.dtype != torch.float32 or a_log.dtype != torch.float32:
+        raise TypeError("dt_bias and A_log must be FP32")
+    _require_cuda(q_in, "KDA prepare")
+    if any(t.device != q_in.device for t in bf + (dt_bias, a_log)):
+        raise ValueError("KDA prepare tensors must share one device")
+    x = [t.reshape(batch, c) for t in (q_in, k_in, v_in)]
+    if any(t.stride(1) != 1 or t.stride(0) != x[0].stride(0) for t in x):
+        x = [t.contiguous() for t in x]
+    states = (q_state, k_state, v_state)
+    if any(tuple(st.shape) != (batch, c, 4) or not st.is_contiguous() for st in states):
+        raise ValueError("each short convolution state must be a contiguous [batch, channels, 4]")
+    weights = [w.reshape(c, 4).contiguous() for w in (q_weight, k_weight, v_weight)]
+    rd = raw_decay.reshape(batch, c).contiguous()
+    rb = raw_beta.reshape(batch, num_heads).contiguous()
+    a = a_log.reshape(num_heads).contiguous()
+    dt = dt_bias.reshape(c).contiguous()
+    outs = [torch.empty((batch, num_heads, head_dim), dtype=torch.float32, device=q_in.device)
+            for _ in range(4)]
+    beta = torch.empty((batch, num_heads), dtype=torch.float32, device=q_in.device)
+    if batch == 0:
+        return (*outs, beta)
+    _lib.call("kb_kda_prepare", _p(x[0]), _p(x[1]), _p(x[2]), c_int64(x[0].stride(0)),
+              _p(q_state), _p(k_state), _p(v_state), _p(weights[0]), _p(weights[1]),
+              _p(weights[2]), _p(rd), c_int64(rd.stride(0)), _p(dt), _p(a), _p(rb),
+              c_int64(rb.stride(0)), c_int64(batch), c_int64(num_heads), c_int64(head_dim),
+              c_float(eps), _p(outs[0]), _p(outs[1]), _p(outs[2]), _p(outs[3]), _p(beta),
+              _stream(q_in.device))
+    return (*outs, beta)
+
+
 def quantise(weight: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
     """On-device quantise of a bf16 [N,K] matrix -> (packed uint8 [N,K/2], bf16 scales).
 

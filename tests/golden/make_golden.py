@@ -6,7 +6,9 @@ REFERENCE_DIR defaults to the KIMI_REFERENCE_DIR environment variable.  The
 script imports the reference's own functions -- the codec
 (engine/quant/w4a16.py), fused_w2_combine_reference
 (engine/kernels/moe_combine.py:209-261), kda_decode_step_reference
-(engine/kernels/kda_step.py:173-196), KLinearRouter (engine/klinear/router.py)
+(engine/kernels/kda_step.py:173-196), fused_short_conv_triple_reference and
+fused_kda_gates_reference (engine/kernels/kda_prepare.py:426-472, 581-615),
+KLinearRouter (engine/klinear/router.py)
 and KLinearMoE's eager expert path with an expert provider returning
 dequantised weights (engine/klinear/moe.py:336-398) -- runs them on seeded
 inputs at the reference group size 32, and writes every input and output to
@@ -29,6 +31,8 @@ OUT = HERE / "reference_g32.pt"
 
 def _load_reference(ref_dir: str):
     sys.path.insert(0, ref_dir)
+    from engine.kernels.kda_prepare import (fused_kda_gates_reference,
+                                            fused_short_conv_triple_reference)
     from engine.kernels.kda_step import kda_decode_step_reference
     from engine.kernels.moe_combine import fused_w2_combine_reference
     from engine.klinear.moe import KLinearMoE
@@ -41,6 +45,8 @@ def _load_reference(ref_dir: str):
         "W4A16Tensor": W4A16Tensor,
         "combine": fused_w2_combine_reference,
         "kda": kda_decode_step_reference,
+        "conv3": fused_short_conv_triple_reference,
+        "gates": fused_kda_gates_reference,
         "router": KLinearRouter,
         "moe": KLinearMoE,
     }
@@ -207,6 +213,32 @@ def main(ref_dir: str) -> None:
         gold[f"moe.{name}_scales"] = torch.stack(
             [experts[e][j].scales for e in range(E2)] + [shared[j].scales]
         )
+
+    # KDA decode preparation: the width-4 short convolutions of q/k/v (states
+    # updated in place) and the gates, bf16 inputs as in the model.
+    gp = torch.Generator().manual_seed(20260729)
+    B, C, NH, HD = 2, 256, 2, 128
+    vals = [torch.randn(B, 1, C, generator=gp).to(torch.bfloat16) for _ in range(3)]
+    states = [torch.randn(B, C, 4, generator=gp).to(torch.bfloat16) for _ in range(3)]
+    weights = [(0.5 * torch.randn(C, 1, 4, generator=gp)).to(torch.bfloat16) for _ in range(3)]
+    for j, name in enumerate("qkv"):
+        gold[f"prep.{name}_in"] = vals[j].clone()
+        gold[f"prep.{name}_state_in"] = states[j].clone()
+        gold[f"prep.{name}_weight"] = weights[j].clone()
+    conv = R["conv3"](*vals, *states, *weights)
+    for j, name in enumerate("qkv"):
+        gold[f"prep.{name}_conv"] = conv[j].clone()
+        gold[f"prep.{name}_state_out"] = states[j].clone()
+    raw_decay = torch.randn(B, 1, NH, HD, generator=gp).to(torch.bfloat16)
+    dt_bias = torch.randn(NH * HD, generator=gp)
+    a_log = torch.log(1.0 + 15.0 * torch.rand(NH, generator=gp)).view(1, 1, NH, 1)
+    raw_beta = torch.randn(B, 1, NH, generator=gp).to(torch.bfloat16)
+    raw_decay[0, 0, 0, :4] = torch.tensor([30.0, -30.0, 0.0, 19.0])   # softplus branches
+    gates = R["gates"](raw_decay, dt_bias, a_log, raw_beta, conv[0], conv[1], num_heads=NH,
+                       head_dim=HD, eps=1e-6)
+    gold.update({"prep.raw_decay": raw_decay, "prep.dt_bias": dt_bias, "prep.a_log": a_log,
+                 "prep.raw_beta": raw_beta, "prep.decay": gates[0], "prep.beta": gates[1],
+                 "prep.q": gates[2], "prep.k": gates[3]})
 
     torch.save(gold, OUT)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(gold)} tensors)")

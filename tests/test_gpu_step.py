@@ -162,7 +162,7 @@ def _small_shape() -> KimiLinearShape:
 
 @pytest.mark.parametrize("batch", [1, 5])
 def test_step_program_matches_per_op_step(cuda, batch):
-    model = HotPathDecoder(batch, shape=_small_shape())
+    model = HotPathDecoder(batch, shape=_small_shape(), kda_prepare=False)
     x = model.x0.clone()
     states = [lw.kda_state.clone() if lw.kda_state is not None else None for lw in model.layers]
     prog, buf = model.build_program(x)
@@ -225,7 +225,7 @@ def test_step_program_matches_oracle_chain(cuda, batch):
     # tolerance.
     from oracle.decode import StepTrace, decode_step
 
-    model = HotPathDecoder(batch, shape=_small_shape(), seed=7)
+    model = HotPathDecoder(batch, shape=_small_shape(), seed=7, kda_prepare=False)
     x = model.x0.clone()
     states = [lw.kda_state.clone() if lw.kda_state is not None else None for lw in model.layers]
     layers = _oracle_model(model, states)
@@ -247,3 +247,38 @@ def test_step_program_matches_oracle_chain(cuda, batch):
         assert torch.equal(idx[:, :-1].cpu(), ref_idx)
         torch.testing.assert_close(wts.cpu(), ref_w, rtol=1e-5, atol=1e-6)
     assert_close(buf["logits"], ref_logits, what=f"program logits vs oracle B={batch}")
+
+
+@pytest.mark.parametrize("batch", [1, 6])
+def test_per_op_step_with_kda_prepare_matches_oracle_chain(cuda, batch):
+    # The per-operation step with the KDA decode preparation (q/k/v from the
+    # layer's projections through the short convolutions and gates) against
+    # the oracle chain: logits, KDA and convolution states.
+    from oracle.decode import StepTrace, decode_step
+
+    model = HotPathDecoder(batch, shape=_small_shape(), seed=11)
+    assert model.kda_prepare
+    x = model.x0.clone()
+    states = [lw.kda_state.clone() if lw.kda_state is not None else None for lw in model.layers]
+    layers = _oracle_model(model, states)
+    for lw, ol in zip(model.layers, layers):
+        if lw.kind == "kda":
+            ol.conv_w = [w.cpu() for w in lw.conv_w]
+            ol.conv_state = [c.cpu().clone() for c in lw.conv_state]
+            ol.dt_bias, ol.a_log = lw.dt_bias.cpu(), lw.a_log.cpu()
+    logits = model.step(x)
+    torch.cuda.synchronize()
+    inputs = {"raw_decay": model.raw_decay.cpu(), "raw_beta": model.raw_beta.cpu(),
+              "mla_latent": model.mla_latent.cpu(), "mla_attn": model.mla_attn.cpu()}
+    trace = StepTrace()
+    ref = decode_step(layers, (model.lm_head[0].cpu(), model.lm_head[1].cpu()), inputs,
+                      x.cpu(), kda_scale=model.shape.kda_head_dim ** -0.5, trace=trace,
+                      prepare=True, heads=model.shape.kda_heads)
+    for lw, ol in zip(model.layers, layers):
+        if lw.kda_state is not None:
+            torch.testing.assert_close(lw.kda_state.cpu(), ol.kda_state, rtol=1e-3, atol=1e-4)
+            # the newest token of each state is the layer's projection output,
+            # itself within one bf16 rounding of the oracle's
+            for c, rc in zip(lw.conv_state, ol.conv_state):
+                assert_close(c, rc, what="conv state")
+    assert_close(logits, ref, what=f"per-op step with KDA preparation B={batch}")

@@ -258,3 +258,59 @@ def test_shape_stable_indices_append_shared_route():
     stable = ops.shape_stable_indices(idx, 8)
     assert torch.equal(stable[:, :-1], idx)
     assert torch.equal(stable[:, -1], torch.full((2,), 8))
+
+
+def test_kda_prepare_matches_reference(golden):
+    # kda_prepare.py:426-472 and 581-615, recorded from the reference.
+    from oracle import kda_prep
+
+    g = golden
+    states = [g[f"prep.{n}_state_in"].clone() for n in "qkv"]
+    conv = kda_prep.short_conv3(*(g[f"prep.{n}_in"] for n in "qkv"), *states,
+                                *(g[f"prep.{n}_weight"] for n in "qkv"))
+    for j, n in enumerate("qkv"):
+        assert torch.equal(conv[j], g[f"prep.{n}_conv"])
+        assert torch.equal(states[j], g[f"prep.{n}_state_out"])
+    decay, beta, q, k = kda_prep.gates(g["prep.raw_decay"], g["prep.dt_bias"], g["prep.a_log"],
+                                       g["prep.raw_beta"], conv[0], conv[1], num_heads=2,
+                                       head_dim=128)
+    assert torch.equal(decay, g["prep.decay"])
+    assert torch.equal(beta, g["prep.beta"])
+    assert torch.equal(q, g["prep.q"])
+    assert torch.equal(k, g["prep.k"])
+
+
+def test_kda_prepare_known_answers():
+    # tests/test_kda_prepare.py:26-123 of the reference (hand-computed cases).
+    import math
+
+    from oracle import kda_prep
+
+    silu = lambda v: v / (1.0 + math.exp(-v))  # noqa: E731
+    states = [torch.tensor([[[1.0, 2.0, 3.0, 4.0]]]), torch.tensor([[[4.0, 3.0, 2.0, 1.0]]]),
+              torch.tensor([[[-1.0, -2.0, -3.0, -4.0]]])]
+    weights = [torch.tensor([[[1.0, 0.0, 0.0, 0.0]]]), torch.tensor([[[0.0, 0.0, 1.0, 0.0]]]),
+               torch.tensor([[[1.0, 1.0, 1.0, 1.0]]])]
+    out = kda_prep.short_conv3(torch.tensor([[[5.0]]]), torch.tensor([[[0.0]]]),
+                               torch.tensor([[[6.0]]]), *states, *weights)
+    for actual, expected in zip(out, (silu(2.0), silu(1.0), silu(-3.0))):
+        torch.testing.assert_close(actual, torch.tensor([[[expected]]]), atol=1e-6, rtol=1e-6)
+    assert torch.equal(states[0], torch.tensor([[[2.0, 3.0, 4.0, 5.0]]]))
+    assert torch.equal(states[2], torch.tensor([[[-2.0, -3.0, -4.0, 6.0]]]))
+    eps = 1e-6
+    decay, beta, q, k = kda_prep.gates(
+        torch.tensor([[[[0.0, 1.0], [-1.0, 2.0]]]]), torch.tensor([0.5, -0.5, 1.0, -1.0]),
+        torch.log(torch.tensor([2.0, 0.5])).view(1, 1, 2, 1),
+        torch.tensor([[[0.0, math.log(3.0)]]]), torch.tensor([[[3.0, 4.0, 0.0, 2.0]]]),
+        torch.tensor([[[5.0, 12.0, 8.0, 15.0]]]), num_heads=2, head_dim=2, eps=eps)
+    sp = lambda v: math.log1p(math.exp(v))  # noqa: E731
+    torch.testing.assert_close(decay, torch.tensor(
+        [[[[-2.0 * sp(0.5), -2.0 * sp(0.5)], [-0.5 * sp(0.0), -0.5 * sp(1.0)]]]]),
+        atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(beta, torch.tensor([[[0.5, 0.75]]]), atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(q, torch.tensor(
+        [[[[3.0 / math.sqrt(25 + eps), 4.0 / math.sqrt(25 + eps)],
+           [0.0, 2.0 / math.sqrt(4 + eps)]]]]), atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(k, torch.tensor(
+        [[[[5.0 / math.sqrt(169 + eps), 12.0 / math.sqrt(169 + eps)],
+           [8.0 / math.sqrt(289 + eps), 15.0 / math.sqrt(289 + eps)]]]]), atol=1e-6, rtol=1e-6)
