@@ -361,6 +361,12 @@ class BatchCpuSample:
         self.decay = -(0.005 + 0.075 * torch.rand((kb, H, D), generator=act))
         self.beta = torch.sigmoid(torch.randn((kb, H), generator=act))
         self.state = 0.05 * torch.randn((kb, H, D, D), generator=gen)
+        self.conv_w = [synth.activations((proj, 4), gen) for _ in range(3)]
+        self.conv_state = [synth.activations((batch, proj, 4), act) for _ in range(3)]
+        self.raw_decay = synth.activations((batch, proj), act)
+        self.raw_beta = synth.activations((batch, H), act)
+        self.dt_bias = torch.randn(proj, generator=gen)
+        self.a_log = torch.log(1.0 + 15.0 * torch.rand(H, generator=gen))
         self.qkv = [q(proj, s.hidden) for _ in range(3)]
         self.kda_o = q(s.hidden, proj)
         self.mla_q = q(s.mla_heads * s.mla_q_head_dim, s.hidden)
@@ -386,16 +392,20 @@ class BatchCpuSample:
         return oref.dense(a, *w2)
 
     def seconds_per_step(self) -> tuple[float, str, int]:
+        from oracle import kda_prep
         from oracle import ops as oref
 
         torch.set_num_threads(os.cpu_count() or 1)
         s, B = self.shape, self.batch
         scale = s.kda_head_dim ** -0.5
         t0 = time.perf_counter()
-        oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
+        qkv = oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
+        kda_prep.prepare(*qkv, *self.conv_state, *self.conv_w, self.raw_decay, self.dt_bias,
+                         self.a_log, self.raw_beta, num_heads=s.kda_heads,
+                         head_dim=s.kda_head_dim)
         t_qkv = time.perf_counter() - t0
         # The KDA state step's cost is linear in the batch: timed at kda_batch
-        # sequences and scaled.
+        # sequences and scaled to the batch.
         st = self.state.clone()
         t0 = time.perf_counter()
         oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
@@ -403,119 +413,6 @@ class BatchCpuSample:
         t0 = time.perf_counter()
         oref.dense(self.kda_in, *self.kda_o)
         t_kda_block = t_qkv + t_state + (time.perf_counter() - t0)
-
-        t0 = time.perf_counter()
-        oref.dense(self.x, *self.mla_q)
-        oref.dense(self.latent, *self.kv_b)
-        h = oref.dense(self.attn, *self.mla_o)
-        omoe.moe_layer(h, banks_mla)
-        t_mla = time.perf_counter() - t0
-
-        t0 = time.perf_counter()
-        d = self.dense
-        a = oref.swiglu(self.x, torch.zeros((B, 1), dtype=torch.long), d[0], d[1], d[2], d[3])
-        oref.dense(a.view(B, -1), d[4], d[5])
-        t_dense = time.perf_counter() - t0
-
-        t0 = time.perf_counter()
-        oref.dense(self.x, *self.lm_head)
-        t_head = (time.perf_counter() - t0) * self.LM_HEAD_FRACTION
-
-        total = t_kda * self.n_kda + t_mla * self.n_mla + t_dense + t_head
-        sample = (f"oracle (torch CPU, {torch.get_num_threads()} threads) on 1 KDA+MoE layer, "
-                  f"1 MLA+MoE layer, the dense layer 0 and 1/{self.LM_HEAD_FRACTION} of the "
-                  f"lm_head rows at batch {B}; per-step time extrapolated to {self.n_kda} "
-                  f"KDA+MoE + {self.n_mla} MLA+MoE layers + layer 0 + the full lm_head")
-        return total, sample, torch.get_num_threads()
-
-
-class BatchCpuSample:
-    """The oracle (torch CPU, all cores) on a bounded sample of the batch decode
-    step: one KDA attention block, one MLA attention block, one MoE layer, the
-    dense MLP of layer 0 and 1/8 of the lm_head rows, at ``batch`` tokens.
-
-    The MoE layer routes all tokens but computes the routed experts for only
-    ``expert_sample`` of the experts it touches (each with its own tokens),
-    scaled by the number touched; the shared expert runs on every token.  The
-    KDA state step runs at ``kda_batch`` sequences and is scaled by
-    batch / kda_batch (its cost is linear in the batch).  Weights are seeded
-    synthetic values with the real shapes (the timing does not depend on the
-    values); the per-step time is extrapolated to the 27-layer step.
-    """
-
-    LM_HEAD_FRACTION = 8
-
-    def __init__(self, batch: int, group: int, seed: int = 0, expert_sample: int = 8,
-                 kda_batch: int = 32) -> None:
-        from local_kimi_b200.decode import KimiLinearShape
-        from oracle import synth
-
-        s = KimiLinearShape()
-        self.shape, self.batch, self.group = s, batch, group
-        self.expert_sample = expert_sample
-        self.kda_batch = min(kda_batch, batch)
-        gen = synth.generator(seed)
-        act = synth.generator(seed + 1)
-        H, D = s.kda_heads, s.kda_head_dim
-        proj = H * D
-        q = lambda n, k: synth.quantised(n, k, group, gen)  # noqa: E731
-        self.x = synth.activations((batch, s.hidden), act)
-        self.attn = synth.activations((batch, s.mla_heads * s.mla_v_head_dim), act)
-        self.latent = synth.activations((batch, s.kv_lora_rank), act)
-        self.kda_in = synth.activations((batch, proj), act)
-        kb = self.kda_batch
-        self.q = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
-        self.k = torch.nn.functional.normalize(torch.randn((kb, H, D), generator=act), dim=-1)
-        self.v = 0.2 * torch.randn((kb, H, D), generator=act)
-        self.decay = -(0.005 + 0.075 * torch.rand((kb, H, D), generator=act))
-        self.beta = torch.sigmoid(torch.randn((kb, H), generator=act))
-        self.state = 0.05 * torch.randn((kb, H, D, D), generator=gen)
-        self.qkv = [q(proj, s.hidden) for _ in range(3)]
-        self.kda_o = q(s.hidden, proj)
-        self.mla_q = q(s.mla_heads * s.mla_q_head_dim, s.hidden)
-        self.kv_b = q(s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
-        self.mla_o = q(s.hidden, s.mla_heads * s.mla_v_head_dim)
-        self.router = synth.weight((s.experts, s.hidden), gen)
-        self.experts = [(q(s.moe_intermediate, s.hidden), q(s.moe_intermediate, s.hidden),
-                         q(s.hidden, s.moe_intermediate)) for _ in range(expert_sample + 1)]
-        w1, w3 = q(s.dense_intermediate, s.hidden), q(s.dense_intermediate, s.hidden)
-        w2 = q(s.hidden, s.dense_intermediate)
-        self.dense = (w1, w3, w2)
-        self.lm_head = q(s.vocab_size // self.LM_HEAD_FRACTION, s.hidden)
-        self.n_kda = sum(1 for i in range(s.layers) if not s.is_mla(i))
-        self.n_mla = s.layers - self.n_kda
-        self.n_moe = s.layers - s.first_k_dense
-
-    @staticmethod
-    def _ffn(x: torch.Tensor, w1, w3, w2) -> torch.Tensor:
-        from oracle import ops as oref
-
-        idx = torch.zeros((x.shape[0], 1), dtype=torch.long)
-        a = oref.swiglu(x, idx, w1[0][None], w1[1][None], w3[0][None], w3[1][None])[:, 0]
-        return oref.dense(a, *w2)
-
-    def seconds_per_step(self) -> tuple[float, str, int]:
-        from oracle import ops as oref
-
-        torch.set_num_threads(os.cpu_count() or 1)
-        s, B = self.shape, self.batch
-        scale = s.kda_head_dim ** -0.5
-        t0 = time.perf_counter()
-        oref.fused_qkv(self.x, *self.qkv[0], *self.qkv[1], *self.qkv[2])
-        st = self.state.clone()
-        oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
-        t_kda_state = time.perf_counter() - t0
-        t1 = time.perf_counter()
-        oref.dense(self.kda_in, *self.kda_o)
-        t_kda = (time.perf_counter() - t1) + t_kda_state * 0  # o_proj
-        t_kda += t_kda_state
-        t_kda_scaled = t_kda + (t_kda_state - 0) * 0
-        # KDA state step cost scales with the batch: measure it alone and scale.
-        t2 = time.perf_counter()
-        st = self.state.clone()
-        oref.kda_step(st, self.q, self.k, self.v, self.decay, self.beta, scale=scale)
-        t_state = time.perf_counter() - t2
-        t_kda_block = t_kda_scaled - t_state + t_state * (B / self.kda_batch)
 
         t0 = time.perf_counter()
         oref.dense(self.x, *self.mla_q)
@@ -548,7 +445,7 @@ class BatchCpuSample:
         total = (self.n_kda * t_kda_block + self.n_mla * t_mla + self.n_moe * t_moe + t_dense
                  + t_head)
         desc = (f"oracle (torch CPU, {torch.get_num_threads()} threads) at batch {B}: one KDA "
-                f"block (q/k/v, state step at {self.kda_batch} sequences scaled x"
+                f"block (q/k/v, preparation, state step at {self.kda_batch} sequences scaled x"
                 f"{B / self.kda_batch:g}, o_proj), one MLA block (q_proj, kv_b, o_proj), one "
                 f"MoE layer (router, shared expert, {len(sample)} of the {touched.numel()} "
                 f"touched routed experts scaled to all), the layer-0 dense MLP and "
@@ -824,6 +721,69 @@ def _batch_record(base, batch: int, args) -> dict:
     }
 
 
+def _moe_layers_record(base, args) -> dict:
+    """Configs C1 (1 token) and C3 (64 tokens, expert popularity skewed
+    ~Zipf(1.1) by the router bias of a seeded expert permutation): the MoE
+    layer (router -> gate/up + SwiGLU -> down + combine) of every MoE layer of
+    the model back to back in one CUDA graph; bytes = router + the touched
+    experts' three matrices."""
+    import copy
+
+    from local_kimi_b200.moe import moe_forward
+
+    peak, _ = _peak_hbm()
+    moes = [lw.moe for lw in base.layers if lw.moe is not None]
+    experts = moes[0].num_experts
+    per_expert = sum(t[0].numel() * t.element_size() for t in (
+        moes[0].w1_packed, moes[0].w1_scales, moes[0].w2_packed, moes[0].w2_scales,
+        moes[0].w3_packed, moes[0].w3_scales))
+    router_bytes = moes[0].router_weight.numel() * 2
+    out = {}
+    for name, tokens, zipf in (("C1", 1, 0.0), ("C3", 64, 1.1)):
+        layers = moes
+        if zipf > 0:
+            g = torch.Generator().manual_seed(7)
+            perm = torch.randperm(experts, generator=g)
+            bias = torch.empty(experts)
+            bias[perm] = 0.25 * torch.arange(1, experts + 1, dtype=torch.float32).pow(-zipf)
+            layers = []
+            for m in moes:
+                mm = copy.copy(m)
+                mm.router_bias = bias.to(m.router_weight.device)
+                layers.append(mm)
+        gx = torch.Generator(device="cuda")
+        gx.manual_seed(5 + tokens)
+        x = torch.randn((tokens, base.shape.hidden), generator=gx, device="cuda").to(
+            torch.bfloat16)
+        touched, loads = [], []
+        for m in layers:
+            _, idx, _ = moe_forward(x, m)
+            cnt = torch.bincount(idx.reshape(-1), minlength=experts)
+            loads.append(int(cnt.max()))
+            touched.append(int((cnt > 0).sum()) + 1)
+        nbytes = sum(t * per_expert + router_bytes for t in touched)
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for m in layers:
+                moe_forward(x, m)
+            with torch.cuda.graph(graph, stream=side):
+                for m in layers:
+                    moe_forward(x, m)
+        torch.cuda.current_stream().wait_stream(side)
+        t = _time_graph(graph, max(5, args.steps), 3)
+        del graph
+        gbs = nbytes / t / 1e9
+        out[name] = {"tokens": tokens, "zipf": zipf, "layers": len(layers),
+                     "us_per_layer": round(t * 1e6 / len(layers), 2),
+                     "touched_experts_mean": round(sum(touched) / len(touched), 1),
+                     "max_tokens_per_expert": max(loads),
+                     "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+    out["timing"] = "CUDA graph of the model's MoE layers back to back, replayed"
+    return out
+
+
 def _sweep_record(args) -> dict:
     """The C2 dense sweep at M 1, 16 and 64 through the registry op (engine or
     tensor-core path by shape): time, HBM GB/s and fraction of the peak."""
@@ -902,6 +862,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         records["bs32"] = _batch_record(base, 32, args)
         if not args.no_sweep:
             records["dense_sweep"] = _sweep_record(args)
+            records["moe_layers"] = _moe_layers_record(base, args)
     _progress(rank, "weights built; sub-records done; sharding experts")
     model.enable_expert_parallel(group)
     static_x = model.x0.clone()

@@ -31,37 +31,37 @@ constexpr int EP_THREADS = 256;
 constexpr int EP_MAX_PAIRS = 8192;   // tokens * top_k per call
 constexpr int EP_MAX_RANKS = 64;
 
-// Stable per-destination positions of all pairs, by one warp: pos[a] and the
-// per-destination counts cnt[d].  Every CTA computes the same table.
+// Stable per-destination positions of all pairs: pos[a] and the counts
+// cnt[d].  All threads first stage every pair's destination in shared memory
+// (coalesced loads); then warp w scans the pairs for destinations d = w, w+8,
+// ...: a ballot per 32 pairs gives each match its rank among the earlier
+// matches.  Every CTA computes the same table.
 __device__ void ep_positions(const int64_t* idx, int64_t istride, int T, int k, int per_rank,
-                             int world, int* cnt, int* pos, uint32_t* err) {
-  const int tid = threadIdx.x;
-  for (int d = tid; d < world; d += EP_THREADS) cnt[d] = 0;
+                             int world, int* cnt, int* pos, uint8_t* dest, uint32_t* err) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int pairs = T * k;
+  for (int a = tid; a < pairs; a += EP_THREADS) {
+    const int t = a / k, r = a - t * k;
+    const int64_t e = idx[(size_t)t * istride + r];
+    int d = 0;
+    if (e < 0 || e >= (int64_t)per_rank * world) {
+      atomicOr(err, 1u);
+    } else {
+      d = (int)(e / per_rank);
+    }
+    dest[a] = (uint8_t)d;
+  }
   __syncthreads();
-  if (tid < 32) {
-    const int lane = tid;
-    const int pairs = T * k;
+  for (int d = warp; d < world; d += EP_THREADS / 32) {
+    int running = 0;
     for (int base = 0; base < pairs; base += 32) {
       const int a = base + lane;
-      int d = -1 - lane;
-      if (a < pairs) {
-        const int t = a / k, r = a - t * k;
-        const int64_t e = idx[(size_t)t * istride + r];
-        if (e < 0 || e >= (int64_t)per_rank * world) {
-          atomicOr(err, 1u);
-          d = 0;
-        } else {
-          d = (int)(e / per_rank);
-        }
-      }
-      const unsigned peers = __match_any_sync(0xffffffffu, d);
-      if (a < pairs) {
-        pos[a] = cnt[d] + __popc(peers & ((1u << lane) - 1u));
-      }
-      __syncwarp();
-      if (a < pairs && lane == __ffs(peers) - 1) cnt[d] += __popc(peers);
-      __syncwarp();
+      const bool mine = a < pairs && dest[a] == d;
+      const unsigned m = __ballot_sync(0xffffffffu, mine);
+      if (mine) pos[a] = running + __popc(m & ((1u << lane) - 1u));
+      running += __popc(m);
     }
+    if (lane == 0) cnt[d] = running;
   }
   __syncthreads();
 }
@@ -72,9 +72,10 @@ __global__ void __launch_bounds__(EP_THREADS)
                        int world, int capacity, uint16_t* __restrict__ send_rows,
                        int* __restrict__ slots, uint32_t* err) {
   __shared__ int cnt[EP_MAX_RANKS];
-  extern __shared__ int pos[];
+  extern __shared__ int pos[];                 // [pairs], then the destinations as bytes
   pdl_wait();
-  ep_positions(idx, istride, T, k, per_rank, world, cnt, pos, err);
+  ep_positions(idx, istride, T, k, per_rank, world, cnt, pos,
+               reinterpret_cast<uint8_t*>(pos + T * k), err);
   const int pairs = T * k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (EP_THREADS / 32) + warp, nw = gridDim.x * (EP_THREADS / 32);
@@ -181,11 +182,11 @@ extern "C" int kb_ep_dispatch(const uint16_t* hidden, int64_t h_stride, int64_t 
   KB_REQUIRE(err != nullptr, KB_ERR_LAUNCH, "device error word unavailable");
   const int sms = kb::num_sms(dev);
   const int grid = std::max(1, std::min<int>(sms, (int)((T * k + 7) / 8)));
-  const size_t smem = (size_t)(T * k) * sizeof(int);
+  const size_t smem = (size_t)(T * k) * (sizeof(int) + 1);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kb::ep_dispatch_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(kb::EP_MAX_PAIRS * sizeof(int)));
+                                         (int)(kb::EP_MAX_PAIRS * (sizeof(int) + 1)));
     KB_REQUIRE(e == cudaSuccess, KB_ERR_DEVICE, "dispatch: shared-memory limit: %s",
                cudaGetErrorString(e));
   }

@@ -272,7 +272,10 @@ class HotPathDecoder:
                 h = ops.w4a16_dense(self.mla_attn, *lw.o_proj)
             if lw.dense_mlp is not None:
                 (w1p, w1s), (w3p, w3s), (w2p, w2s) = lw.dense_mlp
-                act = ops.w4a16_swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
+                tokens, hid = h.shape
+                tc = ops.prefer_tc(tokens, w1p.shape[1], hid, hid // w1s.shape[2])
+                swiglu = ops.w4a16_swiglu_tc if tc else ops.w4a16_swiglu
+                act = swiglu(h, self.dense_idx, w1p, w1s, w3p, w3s)
                 x = ops.w4a16_dense(act.view(h.shape[0], -1), w2p, w2s)
             elif eps is not None:
                 x = eps[li].forward(h)
