@@ -16,6 +16,9 @@
 // of the reference expression so the result tracks it closely.
 #include "kb_common.cuh"
 
+#include <algorithm>
+#include <mutex>
+
 namespace kb {
 
 constexpr int KDA_WARPS = 16;
@@ -100,6 +103,245 @@ __global__ void __launch_bounds__(KDA_WARPS * 32)
   }
 }
 
+// Streaming form for Dk = Dv = 128 (the model's shape) with contiguous state
+// rows, used when there are enough (batch, head) pairs to fill the GPU.  One
+// persistent CTA per SM walks the heads u = blockIdx.x + n * gridDim.x; each
+// head's state (64 KB, contiguous) and its q, k, decay and v rows arrive by
+// bulk asynchronous copies into one of three shared-memory stages, two heads
+// ahead of the one being updated, and the updated state leaves by one bulk
+// store.  So every SM keeps about 130 KB of reads and one 64 KB write in
+// flight with no thread waiting on them, and the registers hold one head's
+// slice at a time: lane l owns columns 4l .. 4l+3, warp w the rows w, w+8, ...
+// Column sums go through shared memory in warp order.
+constexpr int KS_THREADS = 256;
+constexpr int KS_WARPS = KS_THREADS / 32;
+constexpr int KS_DIM = 128;
+constexpr int KS_ROWS = KS_DIM / KS_WARPS;
+constexpr int KS_STAGES = 3;
+constexpr int KS_HEAD = KS_DIM * KS_DIM;                 // floats of one head's state
+constexpr int KS_STAGE = KS_HEAD + 4 * KS_DIM;           // + q, k, decay, v
+constexpr size_t KS_SMEM = (size_t)KS_STAGES * KS_STAGE * 4 + 4 * KS_DIM * 4 +
+                           2 * KS_WARPS * 32 * 16 + KS_STAGES * 8 + 16;
+constexpr long long KS_WAIT_NS = 2000000000LL;
+
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_addr(src)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ long long ks_now() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void __launch_bounds__(KS_THREADS, 1)
+    kda_stream_kernel(float* __restrict__ state, int64_t sb, int64_t sh,
+                      const float* __restrict__ q, const float* __restrict__ k,
+                      const float* __restrict__ v, const float* __restrict__ decay,
+                      const float* __restrict__ beta, int H, int BH, float scale,
+                      float* __restrict__ out, uint16_t* __restrict__ out_bf16,
+                      uint32_t* __restrict__ err) {
+  extern __shared__ __align__(128) uint8_t ks_smem[];
+  float* stage = reinterpret_cast<float*>(ks_smem);
+  float* s_ed = stage + KS_STAGES * KS_STAGE;
+  float* s_k = s_ed + KS_DIM;
+  float* s_bk = s_k + KS_DIM;
+  float* s_q = s_bk + KS_DIM;
+  float4* s_red = reinterpret_cast<float4*>(s_q + KS_DIM);    // [2][KS_WARPS][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + 2 * KS_WARPS * 32);
+  int* s_ok = reinterpret_cast<int*>(full + KS_STAGES);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+
+  if (tid == 0) {
+    for (int i = 0; i < KS_STAGES; ++i) mbar_init(&full[i], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const uint64_t pol = l2_evict_first_policy();
+  auto head_state = [&](int u) {
+    const int b = u / H, h = u - b * H;
+    return state + (size_t)b * sb + (size_t)h * sh;
+  };
+  auto issue = [&](int u, int s) {
+    float* st = stage + (size_t)s * KS_STAGE;
+    const size_t vec = (size_t)u * KS_DIM;
+    mbar_arrive_expect_tx(&full[s], KS_STAGE * 4);
+    bulk_g2s(st, head_state(u), KS_HEAD * 4, &full[s], pol);
+    bulk_g2s(st + KS_HEAD, q + vec, KS_DIM * 4, &full[s], pol);
+    bulk_g2s(st + KS_HEAD + KS_DIM, k + vec, KS_DIM * 4, &full[s], pol);
+    bulk_g2s(st + KS_HEAD + 2 * KS_DIM, decay + vec, KS_DIM * 4, &full[s], pol);
+    bulk_g2s(st + KS_HEAD + 3 * KS_DIM, v + vec, KS_DIM * 4, &full[s], pol);
+  };
+  if (tid == 0)
+    for (int n = 0; n < KS_STAGES - 1; ++n)
+      if (blockIdx.x + n * G < BH) issue(blockIdx.x + n * G, n);
+
+  float bt = tid < KS_DIM ? beta[blockIdx.x] : 0.f;
+  int s = 0;
+  uint32_t ph = 0;
+  int issued = min(KS_STAGES - 1, (BH - (int)blockIdx.x + G - 1) / G);
+  int done = 0;
+  for (int u = blockIdx.x; u < BH; u += G, ++done) {
+    // One thread waits (bounded); the verdict is shared so that every thread
+    // leaves the loop together on a timeout.
+    if (tid == 0) {
+      int ok = 1;
+      const long long t0 = ks_now();
+      while (!mbar_try_wait(&full[s], ph)) {
+        if (ks_now() - t0 > KS_WAIT_NS) {
+          atomicOr(err, 2u);
+          ok = 0;
+          break;
+        }
+      }
+      *s_ok = ok;
+    }
+    __syncthreads();
+    if (!*s_ok) break;
+    while (!mbar_try_wait(&full[s], ph)) {
+    }
+    float* st = stage + (size_t)s * KS_STAGE;
+    const float* sq = st + KS_HEAD;
+    if (tid < KS_DIM) {
+      const float kv = sq[KS_DIM + tid];
+      s_ed[tid] = expf(sq[2 * KS_DIM + tid]);
+      s_k[tid] = kv;
+      s_bk[tid] = __fmul_rn(bt, kv);
+      s_q[tid] = __fmul_rn(sq[tid], scale);
+      bt = u + G < BH ? beta[u + G] : 0.f;   // next head's, consumed next pass
+    }
+    const float4 vv = reinterpret_cast<const float4*>(sq + 3 * KS_DIM)[lane];
+    __syncthreads();
+
+    float4 c[KS_ROWS];
+    float4 part = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < KS_ROWS; ++j) {
+      const int i = warp + KS_WARPS * j;
+      const float ed = s_ed[i], kk = s_k[i];
+      c[j] = reinterpret_cast<const float4*>(st + i * KS_DIM)[lane];
+      c[j].x = __fmul_rn(c[j].x, ed);
+      c[j].y = __fmul_rn(c[j].y, ed);
+      c[j].z = __fmul_rn(c[j].z, ed);
+      c[j].w = __fmul_rn(c[j].w, ed);
+      part.x = fmaf(c[j].x, kk, part.x);
+      part.y = fmaf(c[j].y, kk, part.y);
+      part.z = fmaf(c[j].z, kk, part.z);
+      part.w = fmaf(c[j].w, kk, part.w);
+    }
+    s_red[warp * 32 + lane] = part;
+    __syncthreads();
+    float4 pred = s_red[lane];
+#pragma unroll
+    for (int w = 1; w < KS_WARPS; ++w) {
+      const float4 p = s_red[w * 32 + lane];
+      pred.x += p.x;
+      pred.y += p.y;
+      pred.z += p.z;
+      pred.w += p.w;
+    }
+    const float4 d = make_float4(__fsub_rn(vv.x, pred.x), __fsub_rn(vv.y, pred.y),
+                                 __fsub_rn(vv.z, pred.z), __fsub_rn(vv.w, pred.w));
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < KS_ROWS; ++j) {
+      const int i = warp + KS_WARPS * j;
+      const float bk = s_bk[i], qq = s_q[i];
+      c[j].x = __fadd_rn(c[j].x, __fmul_rn(bk, d.x));
+      c[j].y = __fadd_rn(c[j].y, __fmul_rn(bk, d.y));
+      c[j].z = __fadd_rn(c[j].z, __fmul_rn(bk, d.z));
+      c[j].w = __fadd_rn(c[j].w, __fmul_rn(bk, d.w));
+      reinterpret_cast<float4*>(st + i * KS_DIM)[lane] = c[j];
+      o.x = fmaf(c[j].x, qq, o.x);
+      o.y = fmaf(c[j].y, qq, o.y);
+      o.z = fmaf(c[j].z, qq, o.z);
+      o.w = fmaf(c[j].w, qq, o.w);
+    }
+    s_red[(KS_WARPS + warp) * 32 + lane] = o;
+    // The updated rows become visible to the bulk-copy engine, then one
+    // thread sends the head back and refills the stage used two heads ago.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      bulk_s2g(head_state(u), st, KS_HEAD * 4);
+      const int un = u + (KS_STAGES - 1) * G;
+      if (un < BH) {
+        int sn = s + KS_STAGES - 1;
+        if (sn >= KS_STAGES) sn -= KS_STAGES;
+        bulk_wait_read_1();   // that stage's store has left shared memory
+        issue(un, sn);
+        ++issued;
+      }
+    }
+    if (warp == 0) {
+      float4 r = s_red[KS_WARPS * 32 + lane];
+#pragma unroll
+      for (int w = 1; w < KS_WARPS; ++w) {
+        const float4 p = s_red[(KS_WARPS + w) * 32 + lane];
+        r.x += p.x;
+        r.y += p.y;
+        r.z += p.z;
+        r.w += p.w;
+      }
+      const size_t vec = (size_t)u * KS_DIM;
+      reinterpret_cast<float4*>(out + vec)[lane] = r;
+      if (out_bf16) {
+        const uint32_t lo = (uint32_t)float_to_bf16_bits(r.x) |
+                            ((uint32_t)float_to_bf16_bits(r.y) << 16);
+        const uint32_t hi = (uint32_t)float_to_bf16_bits(r.z) |
+                            ((uint32_t)float_to_bf16_bits(r.w) << 16);
+        reinterpret_cast<uint2*>(out_bf16 + vec)[lane] = make_uint2(lo, hi);
+      }
+    }
+    if (++s == KS_STAGES) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+  if (tid == 0) {
+    // Loads still in flight after a timeout land before the CTA exits
+    // (bounded); every store has completed.
+    for (int n = done; n < issued; ++n) {
+      const int sn = n % KS_STAGES;
+      const uint32_t pn = (uint32_t)(n / KS_STAGES) & 1u;
+      const long long t0 = ks_now();
+      while (!mbar_try_wait(&full[sn], pn))
+        if (ks_now() - t0 > KS_WAIT_NS / 10) break;
+    }
+    bulk_wait_all();
+  }
+}
+
+static std::mutex g_ks_attr_mu;
+static bool g_ks_attr_done[64] = {};
+
+static int kda_stream_attr(int dev) {
+  KB_REQUIRE(dev >= 0 && dev < 64, KB_ERR_DEVICE, "KDA step: no usable current device");
+  std::lock_guard<std::mutex> lock(g_ks_attr_mu);
+  if (g_ks_attr_done[dev]) return KB_OK;
+  const cudaError_t e = cudaFuncSetAttribute(
+      kda_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KS_SMEM);
+  KB_REQUIRE(e == cudaSuccess, KB_ERR_DEVICE, "KDA step: setting the shared-memory limit failed: %s",
+             cudaGetErrorString(e));
+  g_ks_attr_done[dev] = true;
+  return KB_OK;
+}
+
 }  // namespace kb
 
 extern "C" int kb_kda_decode_step(float* state, int64_t sb, int64_t sh, int64_t sk,
@@ -118,6 +360,20 @@ extern "C" int kb_kda_decode_step(float* state, int64_t sb, int64_t sh, int64_t 
   KB_REQUIRE(sk >= Dv && sh >= Dk * sk && sb >= H * sh, KB_ERR_BAD_SHAPE,
              "state strides (%lld, %lld, %lld) overlap rows", (long long)sb, (long long)sh,
              (long long)sk);
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (Dk == kb::KS_DIM && Dv == kb::KS_DIM && sk == kb::KS_DIM && sh % 4 == 0 && sb % 4 == 0 &&
+      B * H >= 2 * 148 && a16(state) && a16(q) && a16(k) && a16(v) && a16(decay) && a16(out) &&
+      (out_bf16 == nullptr || (reinterpret_cast<uintptr_t>(out_bf16) & 7) == 0)) {
+    const int dev = kb::bind_stream_device(stream);
+    const int attr = kb::kda_stream_attr(dev);
+    if (attr != KB_OK) return attr;
+    uint32_t* err = kb::device_error_word(dev);
+    KB_REQUIRE(err != nullptr, KB_ERR_LAUNCH, "device error word unavailable");
+    const int grid = (int)std::min<int64_t>(B * H, kb::num_sms(dev));
+    return kb::launch(kb::kda_stream_kernel, dim3((unsigned)grid), dim3(kb::KS_THREADS),
+                      kb::KS_SMEM, stream, state, sb, sh, q, k, v, decay, beta, (int)H,
+                      (int)(B * H), scale, out, out_bf16, err);
+  }
   const dim3 grid((unsigned)(B * H), (unsigned)((Dv + kb::KDA_COLS - 1) / kb::KDA_COLS));
   const dim3 block(kb::KDA_WARPS * 32);
   if (Dk <= 128)

@@ -110,6 +110,7 @@ struct Args {
   int splits;             // reduction-axis splits per tile (1: no split)
   float* ws;              // splits > 1: fp32 partials [tile][split][2][NT][BM]
   int* counters;          // splits > 1: arrival counter per tile (zero between launches)
+  int x_tma;              // dense: activations by tensor copies of the map tmx
   uint32_t* err;
 };
 
@@ -503,7 +504,7 @@ struct Bars {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-              const Args A) {
+              const __grid_constant__ CUtensorMap tmx, const Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&B->a_empty[i], 1);
     }
     for (int i = 0; i < A.sx; ++i) {
-      mbar_init(&B->x_full[i], NXTHREADS);
+      mbar_init(&B->x_full[i], A.x_tma ? 1 : NXTHREADS);
       mbar_init(&B->x_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -621,6 +622,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = first; i < it; ++i) drain_phase(&B->w_full[i % A.sw], (i / A.sw) & 1);
       for (int k = max(0, uc - 2); k < uc; ++k) drain_phase(&B->sc_full[k & 1], (k >> 1) & 1);
     }
+  } else if (A.x_tma && (warp == X_WARP0 || warp == X_WARP1)) {
+    // ------------------------------------- activation loader (dense: tensor copies)
+    // One 2-D tensor copy per k-chunk: NT token rows x 128 bytes, written by
+    // the copy engine in the 128-byte-swizzled K-major layout the MMA reads
+    // (rows past the last token are zero-filled).  Asynchronous-proxy writes,
+    // so the MMA issuer needs no proxy fence.
+    if (warp == X_WARP0 && lane == 0) {
+      const uint64_t pol = l2_evict_last_policy();
+      Ring xr(A.sx);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit U = unit_of(A, P, u);
+        for (int si = 0; si < U.s1 - U.s0; ++si, ++it, xr.next()) {
+          const int s = chunk_of(U, si);
+          if (!xr.first && !wait_phase(&B->x_empty[xr.st], xr.ph ^ 1u, abort_f, A.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&B->x_full[xr.st], (uint32_t)(NT * 128));
+          tma_load_2d(ring_x + (size_t)xr.st * NT * 128, &tmx, s * KC, U.tok0, &B->x_full[xr.st],
+                      pol);
+        }
+      }
+      const int first = max(0, it - A.sx);
+      for (int i = first; i < it; ++i) drain_phase(&B->x_full[i % A.sx], (i / A.sx) & 1);
+    }
   } else if (warp == X_WARP0 || warp == X_WARP1) {
     // ------------------------------------------------------ activation loader
     const int xt = (warp == X_WARP0 ? 0 : 32) + lane;
@@ -673,7 +701,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ok = false;
             break;
           }
-          fence_proxy_async();
+          if (!A.x_tma) fence_proxy_async();   // cp.async (generic-proxy) writes
           tc_fence_after();
           // Descriptors and TMEM addresses of the stage, then four k-steps of
           // both tiles with immediate offsets (one instruction chain per MMA
@@ -900,6 +928,24 @@ static int make_map(CUtensorMap* map, const uint8_t* w, int64_t rows, int64_t K)
   return KB_OK;
 }
 
+// 2-D map over bf16 activations [T, K] (row stride xs elements), box NT rows x
+// 64 elements with the 128-byte swizzle the tensor cores read.
+static int make_x_map(CUtensorMap* map, const uint16_t* x, int64_t T, int64_t K, int64_t xs,
+                      int nt) {
+  EncodeFn enc = encode_fn();
+  KB_REQUIRE(enc != nullptr, KB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)(xs * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)nt};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_DEVICE, "activation tensor map encoding failed (%d)",
+             (int)r);
+  return KB_OK;
+}
+
 static std::mutex g_attr_mu;
 static bool g_attr_done[64] = {};
 
@@ -971,18 +1017,24 @@ static int launch_tc(Args& A, const uint8_t* w0, const uint8_t* w1, int64_t rows
                      void* stream) {
   int st = smem_limit();
   if (st != KB_OK) return st;
-  CUtensorMap m0, m1;
+  CUtensorMap m0, m1, mx;
   st = make_map(&m0, w0, rows, A.K);
   if (st != KB_OK) return st;
   st = make_map(&m1, w1 ? w1 : w0, rows, A.K);
   if (st != KB_OK) return st;
+  if (A.x_tma) {
+    st = make_x_map(&mx, A.x, A.T, A.K, A.xs, A.nt);
+    if (st != KB_OK) return st;
+  } else {
+    mx = m0;   // unused
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   A.err = device_error_word(dev);
   KB_REQUIRE(A.err != nullptr, KB_ERR_LAUNCH, "device error word unavailable");
   const int sms = num_sms(dev);
   const int grid = std::max(1, std::min(sms, units_hint));
-  return launch(tc_kernel, dim3(grid), dim3(NTHREADS), (size_t)MAX_SMEM, stream, m0, m1, A);
+  return launch(tc_kernel, dim3(grid), dim3(NTHREADS), (size_t)MAX_SMEM, stream, m0, m1, mx, A);
 }
 
 }  // namespace tc
@@ -1052,6 +1104,7 @@ extern "C" int kb_w4a16_dense_tc(const uint16_t* x, int64_t x_stride, int64_t M,
              need, workspace_bytes);
   Args A = {};
   A.mode = kb::tc::DENSE;
+  A.x_tma = 1;
   A.x = x;
   A.xs = x_stride;
   A.T = (int)M;

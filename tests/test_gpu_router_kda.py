@@ -131,7 +131,9 @@ def _real_inputs(batch: int, seed: int = 20260729):
     return state, q, k, v, decay, beta
 
 
-@pytest.mark.parametrize("batch", [1, 32])
+# batch 1 runs the column-slice kernel, 13 and 32 (416 and 1024 heads) the
+# streaming kernel (uneven and several passes per CTA over its three stages).
+@pytest.mark.parametrize("batch", [1, 13, 32])
 def test_kda_real_shape_single_step(cuda, batch):
     state, q, k, v, decay, beta = _real_inputs(batch)
     dev = [t.to(cuda) for t in (state, q, k, v, decay, beta)]
@@ -161,6 +163,29 @@ def test_kda_256_recurrent_steps(cuda):
         ref = oref.kda_step(st_ref, q, k, v, decay, beta, scale=128 ** -0.5)
     torch.testing.assert_close(st_gpu.cpu(), st_ref, atol=RECURRENT_TOL, rtol=RECURRENT_TOL)
     torch.testing.assert_close(out.cpu(), ref, atol=RECURRENT_TOL, rtol=RECURRENT_TOL)
+
+
+def test_kda_streaming_recurrent_steps_strided_heads(cuda):
+    # 24 sequences (768 heads) whose states are every other head of a larger
+    # buffer: the streaming kernel with head and batch strides, 8 steps.
+    state, *_ = _real_inputs(24)
+    big = torch.zeros(24, 64, 128, 128, device=cuda)
+    view = big[:, ::2]
+    view.copy_(state.to(cuda))
+    st_ref = state.clone()
+    g = torch.Generator().manual_seed(7)
+    for _ in range(8):
+        q = F.normalize(torch.randn(24, 32, 128, generator=g), dim=-1)
+        k = F.normalize(torch.randn(24, 32, 128, generator=g), dim=-1)
+        v = 0.2 * torch.randn(24, 32, 128, generator=g)
+        decay = -(0.005 + 0.075 * torch.rand(24, 32, 128, generator=g))
+        beta = torch.sigmoid(torch.randn(24, 32, generator=g))
+        out = ops.kda_decode_step(view, q.to(cuda), k.to(cuda), v.to(cuda), decay.to(cuda),
+                                  beta.to(cuda), scale=128 ** -0.5)
+        ref = oref.kda_step(st_ref, q, k, v, decay, beta, scale=128 ** -0.5)
+    torch.testing.assert_close(view.cpu(), st_ref, atol=RECURRENT_TOL, rtol=RECURRENT_TOL)
+    torch.testing.assert_close(out.cpu(), ref, atol=RECURRENT_TOL, rtol=RECURRENT_TOL)
+    assert float(big[:, 1::2].abs().max()) == 0.0
 
 
 def test_kda_noncontiguous_state_is_updated_in_place(cuda):

@@ -20,6 +20,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("m,n,k,group", [
+    (1, 512, 1024, 128),      # fewer token rows than one activation copy box
+    (5, 1024, 2304, 128),
     (16, 4096, 2304, 128),
     (32, 4096, 2304, 128),
     (64, 2304, 4096, 128),
