@@ -148,7 +148,7 @@ KB_API int kb_w4a16_swiglu(const uint16_t* x, int64_t x_stride, int64_t T, int64
 /* as kb_w4a16_dense / kb_w4a16_grouped / kb_w4a16_swiglu (decoded weights     */
 /* bf16(code*scale), fp32 accumulation, bf16 outputs); the reduction order     */
 /* inside the tensor core differs, so outputs agree within rounding.           */
-/* Limits: K % 64 == 0, N % 8 == 0, x row stride % 8 == 0, 16-byte aligned     */
+/* Limits: K % 128 == 0, N % 8 == 0, x row stride % 8 == 0, 16-byte aligned    */
 /* pointers, K/group small enough for the per-CTA scale buffers (at most 81    */
 /* groups per row), grouped T*R <= KB_MAX_ASSIGNMENTS and E <= 520; outside    */
 /* them the call returns KB_ERR_UNSUPPORTED without launching.  y of the       */

@@ -14,26 +14,28 @@
 // 128-row weight tiles -- rows [256 rt, 256 rt + 256) of one matrix (dense and
 // grouped modes) or the same 128 rows of the gate and up matrices (SwiGLU
 // mode) -- times up to 64 token rows (one expert's rows in the grouped modes),
-// over the reduction axis (or one split of it) in 64-wide k-chunks:
+// over the reduction axis (or one split of it) in 128-wide k-chunks (each
+// pipeline hand-off carries a whole chunk, so the fixed cost of the barrier
+// hand-offs is paid once per 32 KB of decoded weights):
 //
 //   warp 0 (lane 0): TMA producer.  Packed codes of both tiles, one 2-D tiled
-//     bulk tensor copy of 128 rows x 32 bytes per tile and k-chunk (plain, no
-//     multicast, L2 evict-first), into a ring of SW shared-memory stages; the
-//     unit's bf16 scales (rows contiguous) with one bulk copy per tile into a
-//     double buffer.
-//   warps 1, 3: activation loaders.  16-byte cp.async pieces of the unit's
-//     token rows (gathered through the expert plan in the grouped modes),
-//     written straight into the 128-byte-swizzled K-major layout the tensor
-//     core reads as its B operand, into a ring of SX stages; each stage is
-//     signalled by the copies' own completion (cp.async.mbarrier.arrive).
+//     bulk tensor copy of 128 rows x 64 bytes per tile and k-chunk (64-byte
+//     swizzle, plain, no multicast, L2 evict-first), into a ring of SW
+//     shared-memory stages; the unit's bf16 scales (rows contiguous) with one
+//     bulk copy per tile into a double buffer.
+//   warps 1, 3: activation loaders.  Dense mode: two 2-D tensor copies per
+//     chunk (lane 0 of warp 1).  Grouped modes: 16-byte cp.async pieces of the
+//     unit's token rows gathered through the expert plan.  Both write the
+//     128-byte-swizzled K-major layout the tensor core reads as its B operand
+//     (two 64-element halves per chunk), into a ring of SX stages.
 //   warps 8-23: decoders, four per TMEM lane quarter (a warp reaches only the
-//     32 lanes of its quarter).  A thread turns 16 packed bytes of its row into
-//     32 weights bf16(code * scale) in k order (17 instructions per 8 weights:
+//     32 lanes of its quarter).  A thread turns 32 packed bytes of its row into
+//     64 weights bf16(code * scale) in k order (17 instructions per 8 weights:
 //     one shift, four byte permutes, four LOP3s, four exact bf16x2
 //     subtractions and four bf16x2 multiplies -- the one rounding of the
-//     reference) and writes them with one tcgen05.st into a ring of four
-//     decoded-weight stages held in tensor memory.
-//   warp 2 (lane 0): MMA issuer.  Per k-chunk, four tcgen05.mma per tile with
+//     reference) and writes them with two tcgen05.st into a ring of two or
+//     three decoded-weight stages held in tensor memory.
+//   warp 2 (lane 0): MMA issuer.  Per k-chunk, eight tcgen05.mma per tile with
 //     A (the decoded weights) read from TMEM and B (the activations) from
 //     shared memory: M 128, N = tokens rounded up to 16, K 16, bf16 x bf16 ->
 //     fp32 into a TMEM accumulator; tcgen05.commit frees each stage and, after
@@ -63,12 +65,12 @@ namespace kb {
 namespace tc {
 
 constexpr int BM = 128;                 // weight rows per tile (MMA M)
-constexpr int KC = 64;                  // reduction elements per chunk (one 128-byte swizzle row)
-constexpr int W_TILE = BM * KC / 2;     // packed bytes per tile and chunk
+constexpr int KC = 128;                 // reduction elements per chunk (two 128-byte swizzle rows)
+constexpr int W_TILE = BM * KC / 2;     // packed bytes per tile and chunk (64 per row)
 constexpr int A_COLS = KC / 2;          // TMEM columns of one decoded tile chunk (bf16 pairs)
 constexpr int NT_MAX = 64;              // token rows per unit (MMA N bound)
-constexpr int TMEM_COLS = 512;          // accumulators [2 buffers][2 tiles][NT_MAX], then the A ring
-constexpr int A_BASE = 4 * NT_MAX;      // first TMEM column of the decoded-weight ring
+constexpr int TMEM_COLS = 512;          // accumulators [2 buffers][2 tiles][NT], then the A ring
+constexpr int SA_MAX = 3;               // decoded-weight stages in TMEM (2 at NT 64, 3 at NT 32)
 constexpr int W_WARP = 0;
 constexpr int X_WARP0 = 1;
 constexpr int MMA_WARP = 2;
@@ -80,7 +82,6 @@ constexpr int NWARPS = DEC_WARP0 + NDEC_WARPS;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int NXTHREADS = 64;
 constexpr int MAX_SMEM = 226 * 1024;   // dynamic; the static plan counters take a few bytes
-constexpr int SA = (TMEM_COLS - A_BASE) / (2 * A_COLS);   // decoded-weight stages in TMEM (4)
 constexpr int MAX_SX = 12;
 constexpr int MAX_SW = 16;
 constexpr int MAX_ASSIGN = 4096;        // grouped modes: T * R
@@ -111,6 +112,7 @@ struct Args {
   float* ws;              // splits > 1: fp32 partials [tile][split][2][NT][BM]
   int* counters;          // splits > 1: arrival counter per tile (zero between launches)
   int x_tma;              // dense: activations by tensor copies of the map tmx
+  int sa, a_base;         // decoded-weight stages in TMEM and the first column of their ring
   uint32_t* err;
 };
 
@@ -492,7 +494,7 @@ __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
 // ---------------------------------------------------------------------------
 struct Bars {
   uint64_t w_full[MAX_SW], w_empty[MAX_SW];
-  uint64_t a_full[SA], a_empty[SA];
+  uint64_t a_full[SA_MAX], a_empty[SA_MAX];
   uint64_t x_full[MAX_SX], x_empty[MAX_SX];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t sc_full[2], sc_empty[2];
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&B->w_full[i], 1);
       mbar_init(&B->w_empty[i], NDEC_WARPS);
     }
-    for (int i = 0; i < SA; ++i) {
+    for (int i = 0; i < A.sa; ++i) {
       mbar_init(&B->a_full[i], NDEC_WARPS);
       mbar_init(&B->a_empty[i], 1);
     }
@@ -567,8 +569,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   P.units *= A.splits;
   const int units = P.units;
-  uint8_t* ring_x = smem + A.off_x;                 // [sx][NT * 128]
+  uint8_t* ring_x = smem + A.off_x;                 // [sx][2][NT * 128]
   uint8_t* ring_w = smem + A.off_w;                 // [sw][2][W_TILE]
+  const int x_stage = NT * KC * 2;                  // bytes of one activation stage
   uint16_t* scl = reinterpret_cast<uint16_t*>(smem + A.off_sc);  // [2][2][BM * ng]
   const int ng = A.ng;
 
@@ -624,10 +627,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (A.x_tma && (warp == X_WARP0 || warp == X_WARP1)) {
     // ------------------------------------- activation loader (dense: tensor copies)
-    // One 2-D tensor copy per k-chunk: NT token rows x 128 bytes, written by
-    // the copy engine in the 128-byte-swizzled K-major layout the MMA reads
-    // (rows past the last token are zero-filled).  Asynchronous-proxy writes,
-    // so the MMA issuer needs no proxy fence.
+    // Two 2-D tensor copies per k-chunk, one per 64-element half: NT token
+    // rows x 128 bytes each, written by the copy engine in the 128-byte-
+    // swizzled K-major layout the MMA reads (rows past the last token are
+    // zero-filled).  Asynchronous-proxy writes, so the MMA issuer needs no
+    // proxy fence.
     if (warp == X_WARP0 && lane == 0) {
       const uint64_t pol = l2_evict_last_policy();
       Ring xr(A.sx);
@@ -641,9 +645,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&B->x_full[xr.st], (uint32_t)(NT * 128));
-          tma_load_2d(ring_x + (size_t)xr.st * NT * 128, &tmx, s * KC, U.tok0, &B->x_full[xr.st],
-                      pol);
+          uint8_t* dst = ring_x + (size_t)xr.st * x_stage;
+          mbar_arrive_expect_tx(&B->x_full[xr.st], (uint32_t)x_stage);
+          tma_load_2d(dst, &tmx, s * KC, U.tok0, &B->x_full[xr.st], pol);
+          tma_load_2d(dst + NT * 128, &tmx, s * KC + KC / 2, U.tok0, &B->x_full[xr.st], pol);
         }
       }
       const int first = max(0, it - A.sx);
@@ -662,12 +667,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        uint8_t* dst = ring_x + (size_t)xr.st * NT * 128;
-        for (int p = xt; p < U.nt * 8; p += NXTHREADS) {
-          const int i = p >> 3, c = p & 7;
+        // Sixteen 16-byte pieces per token row: pieces 0-7 go to the first
+        // 64-element half, 8-15 to the second, each half in the swizzled layout.
+        uint8_t* dst = ring_x + (size_t)xr.st * x_stage;
+        for (int p = xt; p < U.nt * 16; p += NXTHREADS) {
+          const int i = p >> 4, c = p & 15;
           int xrow, yrow;
           rows_of(A, P, U, i, xrow, yrow);
-          cp_async16(dst + sw128_off(i, c), A.x + (size_t)xrow * A.xs + s * KC + c * 8);
+          cp_async16(dst + (c >> 3) * NT * 128 + sw128_off(i, c & 7),
+                     A.x + (size_t)xrow * A.xs + s * KC + c * 8);
         }
         // The stage's arrival is made by the copies' completion (no wait here),
         // so several stages are in flight per thread.
@@ -681,9 +689,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       int uc = 0;
       bool ok = true;
-      Ring ar(SA), xr(A.sx);
+      Ring ar(A.sa), xr(A.sx);
       const uint64_t xdesc0 = sw128_desc(smem_addr(ring_x));
-      const uint64_t xstride = (uint64_t)((NT * 128) >> 4);
+      const uint64_t xstride = (uint64_t)(x_stage >> 4);
+      const uint64_t xhalf = (uint64_t)((NT * 128) >> 4);
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
         const Unit U = unit_of(A, P, u);
         const int b = uc & 1, use_acc = uc >> 1;
@@ -706,15 +715,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // Descriptors and TMEM addresses of the stage, then four k-steps of
           // both tiles with immediate offsets (one instruction chain per MMA
           // as short as possible: the single issuing thread is the limit).
+          // k-step kk reads activation half kk / 4 at byte offset 32 (kk % 4).
           const uint64_t bd = xdesc0 + (uint64_t)xr.st * xstride;
-          const uint32_t ta = tmem + (uint32_t)(A_BASE + ar.st * 2 * A_COLS);
+          const uint64_t bd1 = bd + xhalf;
+          const uint32_t ta = tmem + (uint32_t)(A.a_base + ar.st * 2 * A_COLS);
           const uint32_t acc0 = si > 0 ? 1u : 0u;
           umma_ts(d0, ta, bd, idesc, acc0);
           umma_ts(d1, ta + A_COLS, bd, idesc, acc0);
 #pragma unroll
-          for (int kk = 1; kk < KC / 16; ++kk) {
+          for (int kk = 1; kk < 4; ++kk) {
             umma_ts(d0, ta + kk * 8, bd + (uint64_t)(kk * 2), idesc, 1u);
             umma_ts(d1, ta + A_COLS + kk * 8, bd + (uint64_t)(kk * 2), idesc, 1u);
+          }
+#pragma unroll
+          for (int kk = 4; kk < KC / 16; ++kk) {
+            umma_ts(d0, ta + kk * 8, bd1 + (uint64_t)((kk - 4) * 2), idesc, 1u);
+            umma_ts(d1, ta + A_COLS + kk * 8, bd1 + (uint64_t)((kk - 4) * 2), idesc, 1u);
           }
           umma_commit(&B->a_empty[ar.st]);
           umma_commit(&B->x_empty[xr.st]);
@@ -834,7 +850,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // -------------------------------------------------------------- decoders
     // Warp w may only reach TMEM lanes 32 (w % 4) .. + 31, so the four lane
     // quarters each get four decoder warps: one per (tile, half of the
-    // 64-wide chunk).  A thread decodes 32 weights of its row per chunk.
+    // 128-wide chunk).  A thread decodes 64 weights of its row per chunk: the
+    // two 16-byte pieces of its half of the row's 64 packed bytes, which the
+    // copy engine wrote with the 64-byte swizzle (piece p of row r at
+    // p ^ ((r >> 1) & 3)), so the lanes of a quarter-warp read distinct banks.
     const int dw = warp - DEC_WARP0;
     const int quarter = warp & 3;
     const int m = (dw >> 2) >> 1, h = (dw >> 2) & 1;
@@ -842,7 +861,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_bits = (uint32_t)(quarter * 32) << 16;
     int uc = 0;
     bool ok = true;
-    Ring wr(A.sw), ar(SA);
+    Ring wr(A.sw), ar(A.sa);
+    const int swz = (r >> 1) & 3;
+    const uint32_t wrow = (uint32_t)(m * W_TILE + r * 64);
+    const uint32_t piece0 = (uint32_t)(((2 * h) ^ swz) << 4);
+    const uint32_t piece1 = (uint32_t)(((2 * h + 1) ^ swz) << 4);
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
       const Unit U = unit_of(A, P, u);
       const int sb = uc & 1;
@@ -857,21 +880,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        const uint4 q4 = lds_v4(ring_w + (size_t)(wst * 2 + m) * W_TILE + r * 32 + h * 16);
-        const uint32_t sc =
-            rv ? (uint32_t)srow[(s * KC + h * 32) >> (5 + A.gshift)] : 0u;
-        const uint32_t sc2 = sc | (sc << 16);
-        const uint32_t words[4] = {q4.x, q4.y, q4.z, q4.w};
-        uint32_t o[16];
+        const uint8_t* wsrc = ring_w + (size_t)wst * 2 * W_TILE + wrow;
+        const uint4 qa = lds_v4(wsrc + piece0);
+        const uint4 qb = lds_v4(wsrc + piece1);
+        const int k0 = s * KC + h * 64;   // reduction index of this thread's first weight
+        const uint32_t sa = rv ? (uint32_t)srow[k0 >> (5 + A.gshift)] : 0u;
+        const uint32_t sbv = rv ? (uint32_t)srow[(k0 + 32) >> (5 + A.gshift)] : 0u;
+        const uint32_t col = tmem + lane_bits + (uint32_t)(A.a_base + (ast * 2 + m) * A_COLS + h * 32);
+        {
+          const uint32_t sc2 = sa | (sa << 16);
+          const uint32_t words[4] = {qa.x, qa.y, qa.z, qa.w};
+          uint32_t o[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 v = decode_word_ordered(words[i], sc2);
-          o[4 * i + 0] = v.x;
-          o[4 * i + 1] = v.y;
-          o[4 * i + 2] = v.z;
-          o[4 * i + 3] = v.w;
+          for (int i = 0; i < 4; ++i) {
+            const uint4 v = decode_word_ordered(words[i], sc2);
+            o[4 * i + 0] = v.x;
+            o[4 * i + 1] = v.y;
+            o[4 * i + 2] = v.z;
+            o[4 * i + 3] = v.w;
+          }
+          tmem_st16(col, o);
         }
-        tmem_st16(tmem + lane_bits + (uint32_t)(A_BASE + (ast * 2 + m) * A_COLS + h * 16), o);
+        {
+          const uint32_t sc2 = sbv | (sbv << 16);
+          const uint32_t words[4] = {qb.x, qb.y, qb.z, qb.w};
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 v = decode_word_ordered(words[i], sc2);
+            o[4 * i + 0] = v.x;
+            o[4 * i + 1] = v.y;
+            o[4 * i + 2] = v.z;
+            o[4 * i + 3] = v.w;
+          }
+          tmem_st16(col + 16, o);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -913,7 +956,9 @@ static EncodeFn encode_fn() {
   return fn;
 }
 
-// 2-D map over packed codes viewed as [rows, K/2] bytes, box 128 rows x 32 bytes.
+// 2-D map over packed codes viewed as [rows, K/2] bytes, box 128 rows x 64
+// bytes (one k-chunk of a tile), written to shared memory with the 64-byte
+// swizzle.
 static int make_map(CUtensorMap* map, const uint8_t* w, int64_t rows, int64_t K) {
   EncodeFn enc = encode_fn();
   KB_REQUIRE(enc != nullptr, KB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
@@ -922,21 +967,22 @@ static int make_map(CUtensorMap* map, const uint8_t* w, int64_t rows, int64_t K)
   cuuint32_t box[2] = {(cuuint32_t)(KC / 2), (cuuint32_t)BM};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   KB_REQUIRE(r == CUDA_SUCCESS, KB_ERR_DEVICE, "tensor map encoding failed (%d)", (int)r);
   return KB_OK;
 }
 
 // 2-D map over bf16 activations [T, K] (row stride xs elements), box NT rows x
-// 64 elements with the 128-byte swizzle the tensor cores read.
+// 64 elements (one 128-byte swizzle row) with the swizzle the tensor cores
+// read; a k-chunk takes two copies.
 static int make_x_map(CUtensorMap* map, const uint16_t* x, int64_t T, int64_t K, int64_t xs,
                       int nt) {
   EncodeFn enc = encode_fn();
   KB_REQUIRE(enc != nullptr, KB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
   cuuint64_t strides[1] = {(cuuint64_t)(xs * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)nt};
+  cuuint32_t box[2] = {(cuuint32_t)(KC / 2), (cuuint32_t)nt};   // one 64-element half
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -970,7 +1016,11 @@ static int smem_limit() {
 // Shared-memory layout and ring depths for a problem; KB_ERR_UNSUPPORTED when
 // the scale buffers and plan leave no room for two stages of each ring.
 static int layout(Args& A, int plan_ints) {
-  const int x_stage = A.nt * 128;
+  const int x_stage = A.nt * KC * 2;
+  // TMEM: accumulators [2 buffers][2 tiles][nt] columns, then the decoded-weight
+  // ring (2 tiles x A_COLS columns per stage).
+  A.a_base = 4 * A.nt;
+  A.sa = std::min(SA_MAX, (TMEM_COLS - A.a_base) / (2 * A_COLS));
   const int sc_bytes = (2 * 2 * BM * A.ng * 2 + 1023) / 1024 * 1024;
   const int plan_bytes = (plan_ints * 4 + 127) / 128 * 128;
   const int bar_bytes = (int)((sizeof(Bars) + 127) / 128 * 128);
@@ -1048,9 +1098,11 @@ namespace tc {
 constexpr int TARGET_CTAS = 148;
 
 // Tiles of a dense problem and the reduction-axis split that brings them to
-// about one CTA per SM (each split keeps at least three 64-wide k-chunks).
+// about one CTA per SM (each split keeps at least four 128-wide k-chunks).
 static void dense_split(int64_t M, int64_t K, int64_t N, int* nt, int* tiles, int* splits) {
-  *nt = NT_MAX;
+  // Token rows per unit: all of M up to 64 (rounded to the MMA's 16), so a
+  // small batch keeps TMEM for a third decoded-weight stage.
+  *nt = (int)std::min<int64_t>(NT_MAX, (M + 15) / 16 * 16);
   const int n_rt = (int)((N + 2 * BM - 1) / (2 * BM));
   *tiles = n_rt * (int)((M + *nt - 1) / *nt);
   const int ks = (int)(K / KC);
@@ -1172,7 +1224,10 @@ static int grouped_tc(int mode, const uint16_t* x, int64_t x_stride, int64_t T, 
   A.ys = N;
   const int rows_per_unit = (mode == kb::tc::SWIGLU) ? kb::tc::BM : 2 * kb::tc::BM;
   A.n_rt = (int)((N + rows_per_unit - 1) / rows_per_unit);
-  A.nt = kb::tc::NT_MAX;
+  // Token rows per unit: 32 when experts average fewer than 48 rows (batched
+  // decode spreads T * R rows over many experts; TMEM then holds three
+  // decoded-weight stages), else 64 (one expert taking many rows).
+  A.nt = (T * R >= 48 * E) ? kb::tc::NT_MAX : 32;
   A.splits = 1;
   const int plan_ints = (int)(4 * E + 2 + T * R);
   st = kb::tc::layout(A, plan_ints);

@@ -131,13 +131,13 @@ def _validate_dense(
     return m, output_size, reduction, group
 
 
-# Tensor-core (tcgen05) limits: K a multiple of 64, N of 8, at most 81 scale
+# Tensor-core (tcgen05) limits: K a multiple of 128, N of 8, at most 81 scale
 # groups per row (the per-CTA scale buffers).
 TC_MAX_GROUPS_PER_ROW = 81
 
 
 def tc_supported(m: int, n: int, k: int, group: int) -> bool:
-    return k % 64 == 0 and n % 8 == 0 and k // group <= TC_MAX_GROUPS_PER_ROW and m > 0
+    return k % 128 == 0 and n % 8 == 0 and k // group <= TC_MAX_GROUPS_PER_ROW and m > 0
 
 
 def prefer_tc(m: int, n: int, k: int, group: int) -> bool:
