@@ -35,12 +35,15 @@
 //     subtractions and four bf16x2 multiplies -- the one rounding of the
 //     reference) and writes them with two tcgen05.st into a ring of two or
 //     three decoded-weight stages held in tensor memory.
-//   warp 2 (lane 0): MMA issuer.  Per k-chunk, eight tcgen05.mma per tile with
+//   warp 2 (lanes 0, 1): MMA issuers, one per tile (a tcgen05.mma costs
+//     its issuing thread ~110 cycles at these shapes, measured, so one thread
+//     cannot keep the tensor core busy).  Per k-chunk, eight tcgen05.mma with
 //     A (the decoded weights) read from TMEM and B (the activations) from
 //     shared memory: M 128, N = tokens rounded up to 16, K 16, bf16 x bf16 ->
-//     fp32 into a TMEM accumulator; tcgen05.commit frees each stage and, after
-//     the unit's last chunk, publishes the accumulator (two accumulator
-//     buffers, so the next unit's products overlap this unit's epilogue).
+//     fp32 into the tile's TMEM accumulator; each issuer's tcgen05.commit
+//     frees its share of each stage and, after the unit's last chunk,
+//     publishes its accumulator (two accumulator buffers, so the next unit's
+//     products overlap this unit's epilogue).
 //   warps 4-7: epilogue.  tcgen05.ld of their 32 TMEM lanes (one weight row per
 //     thread), bf16 rounding (or the SwiGLU contract of the gate/up pair) and
 //     stores to the output rows; with a split reduction axis, fp32 partials to
@@ -72,8 +75,8 @@ constexpr int NT_MAX = 64;              // token rows per unit (MMA N bound)
 constexpr int TMEM_COLS = 512;          // accumulators [2 buffers][2 tiles][NT], then the A ring
 constexpr int SA_MAX = 3;               // decoded-weight stages in TMEM (2 at NT 64, 3 at NT 32)
 constexpr int W_WARP = 0;
-constexpr int X_WARP0 = 1;
-constexpr int MMA_WARP = 2;
+constexpr int X_WARP0 = 1;              // activation loaders (warps 1 and 3)
+constexpr int MMA_WARP = 2;             // MMA issuer of tile 0
 constexpr int X_WARP1 = 3;              // also allocates the TMEM
 constexpr int EPI_WARP0 = 4;            // warps 4..7: TMEM lane quarters 0..3
 constexpr int DEC_WARP0 = 8;
@@ -81,6 +84,7 @@ constexpr int NDEC_WARPS = 16;
 constexpr int NWARPS = DEC_WARP0 + NDEC_WARPS;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int NXTHREADS = 64;
+constexpr int NISSUERS = 2;             // MMA-issuing threads (one per tile)
 constexpr int MAX_SMEM = 226 * 1024;   // dynamic; the static plan counters take a few bytes
 constexpr int MAX_SX = 12;
 constexpr int MAX_SW = 16;
@@ -407,20 +411,59 @@ __device__ __forceinline__ void rows_of(const Args& A, const Plan& P, const Unit
 }
 
 // Expert-major plan of the grouped modes, built by all threads of the CTA.
+// Every CTA builds the same plan (the token blocks of an expert with more
+// rows than one unit takes must be the same rows in every CTA): assignments
+// of an expert in ascending order.  The expert ids are staged in shared
+// memory once; PLAN_WARPS warps then each take a contiguous segment of the
+// assignments, count it per expert, and -- after a scan over experts and over
+// the warps -- scatter it, each warp's segment after the earlier warps'.
+constexpr int PLAN_WARPS = 8;
+
+// Ints of shared memory the plan takes for E experts and TR assignments.
+__host__ __device__ constexpr int plan_ints_for(int E, int TR) {
+  return 4 * E + 2 + TR + (TR + 1) / 2 + (PLAN_WARPS * E + 1) / 2;
+}
+
 __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
   __shared__ int s_nslots, s_units;
   const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int TR = A.T * A.R;
   const int E = A.E;
-  for (int e = tid; e < E; e += NTHREADS) cnt[e] = 0;
-  __syncthreads();
+  int16_t* eid = reinterpret_cast<int16_t*>(P.assign + TR);      // [TR]
+  int16_t* wcnt = eid + ((TR + 1) & ~1);                         // [PLAN_WARPS][E]
+  const int seg = ((TR + PLAN_WARPS - 1) / PLAN_WARPS + 31) & ~31;
   for (int a = tid; a < TR; a += NTHREADS) {
     const int64_t v = A.idx[a];
-    if (v != EXPERT_NONE) atomicAdd(&cnt[clamp_expert(v, E, A.err)], 1);
+    eid[a] = (int16_t)(v == EXPERT_NONE ? -1 : clamp_expert(v, E, A.err));
+  }
+  for (int i = tid; i < PLAN_WARPS * E; i += NTHREADS) wcnt[i] = 0;
+  __syncthreads();
+  // Per-warp counts of each expert over the warp's segment.
+  if (warp < PLAN_WARPS) {
+    int16_t* wc = wcnt + warp * E;
+    const int a_end = min(TR, (warp + 1) * seg);
+    for (int base = warp * seg; base < a_end; base += 32) {
+      const int a = base + lane;
+      const int e = a < a_end ? (int)eid[a] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e < 0 ? -1 - lane : e);
+      if (e >= 0 && lane == __ffs(peers) - 1) wc[e] = (int16_t)(wc[e] + __popc(peers));
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // Expert totals; each warp's count becomes its offset within the expert.
+  for (int e = tid; e < E; e += NTHREADS) {
+    int run = 0;
+    for (int w = 0; w < PLAN_WARPS; ++w) {
+      const int c = wcnt[w * E + e];
+      wcnt[w * E + e] = (int16_t)run;
+      run += c;
+    }
+    cnt[e] = run;
   }
   __syncthreads();
   if (tid < 32) {
-    const int lane = tid;
     const int per = (E + 31) / 32;
     const int e0 = min(E, lane * per), e1 = min(E, e0 + per);
     int tot = 0, used = 0, un = 0;
@@ -452,7 +495,7 @@ __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
         ++rank;
         urun += ((c + A.nt - 1) / A.nt) * A.n_rt;
       }
-      cnt[e] = run;  // becomes the scatter cursor
+      cnt[e] = run;  // the expert's first position
       run += c;
     }
     if (lane == 31) {
@@ -463,24 +506,20 @@ __device__ void build_plan(const Args& A, int* cnt, Plan& P) {
     }
   }
   __syncthreads();
-  // Stable scatter (ascending assignment id within an expert) by one warp:
-  // every CTA builds the same order, so the token blocks of an expert with
-  // more rows than one unit takes are the same rows in every CTA.
-  if (tid < 32) {
-    const int lane = tid;
-    for (int base = 0; base < TR; base += 32) {
+  // Stable scatter: position = expert start + earlier warps' count + this
+  // warp's running count + the lane's rank among equal experts of the chunk.
+  if (warp < PLAN_WARPS) {
+    int16_t* wc = wcnt + warp * E;
+    const int a_end = min(TR, (warp + 1) * seg);
+    for (int base = warp * seg; base < a_end; base += 32) {
       const int a = base + lane;
-      const int64_t v = a < TR ? A.idx[a] : EXPERT_NONE;
-      const bool valid = v != EXPERT_NONE;
-      int e = -1 - lane;
-      if (valid) e = (v < 0 || v >= E) ? 0 : (int)v;
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
-      const int pos = valid ? cnt[e] + __popc(peers & ((1u << lane) - 1u)) : 0;
-      __syncwarp();
-      if (valid) {
-        P.assign[pos] = a;
-        if (lane == __ffs(peers) - 1) cnt[e] += __popc(peers);
+      const int e = a < a_end ? (int)eid[a] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e < 0 ? -1 - lane : e);
+      if (e >= 0) {
+        P.assign[cnt[e] + wc[e] + __popc(peers & ((1u << lane) - 1u))] = a;
       }
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(peers) - 1) wc[e] = (int16_t)(wc[e] + __popc(peers));
       __syncwarp();
     }
   }
@@ -523,19 +562,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int i = 0; i < A.sa; ++i) {
       mbar_init(&B->a_full[i], NDEC_WARPS);
-      mbar_init(&B->a_empty[i], 1);
+      mbar_init(&B->a_empty[i], NISSUERS);
     }
     for (int i = 0; i < A.sx; ++i) {
       mbar_init(&B->x_full[i], A.x_tma ? 1 : NXTHREADS);
-      mbar_init(&B->x_empty[i], 1);
+      mbar_init(&B->x_empty[i], NISSUERS);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&B->acc_full[i], 1);
+      mbar_init(&B->acc_full[i], NISSUERS);
       mbar_init(&B->acc_empty[i], 4);
       mbar_init(&B->sc_full[i], 1);
       mbar_init(&B->sc_empty[i], NDEC_WARPS);
     }
-    mbar_init(&B->drain, 1);
+    mbar_init(&B->drain, NISSUERS);
     B->abort_flag = 0;
     mbar_fence_init();
   }
@@ -685,8 +724,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     cp_async_wait_all();
   } else if (warp == MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ----------------------------------------------------------- MMA issuers
+    // One thread per tile: a tcgen05.mma costs its issuing thread about a
+    // hundred cycles whatever its size at these shapes, so two issuers with
+    // their own accumulators double the rate at which the tensor core is fed.
+    // Each commits its own products to the stage barriers (count two).
+    if (lane < NISSUERS) {
+      const int mt = lane;
       int uc = 0;
       bool ok = true;
       Ring ar(A.sa), xr(A.sx);
@@ -702,7 +746,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tc_fence_after();
         const uint32_t idesc = idesc_bf16((U.nt + 15) & ~15);
-        const uint32_t d0 = tmem + (uint32_t)(b * 2 * NT), d1 = d0 + (uint32_t)NT;
+        const uint32_t dm = tmem + (uint32_t)((b * 2 + mt) * NT);
         const int nks = U.s1 - U.s0;
         for (int si = 0; si < nks; ++si, ar.next(), xr.next()) {
           if (!wait_phase(&B->a_full[ar.st], ar.ph, abort_f, A.err) ||
@@ -712,26 +756,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           if (!A.x_tma) fence_proxy_async();   // cp.async (generic-proxy) writes
           tc_fence_after();
-          // Descriptors and TMEM addresses of the stage, then four k-steps of
-          // both tiles with immediate offsets (one instruction chain per MMA
-          // as short as possible: the single issuing thread is the limit).
-          // k-step kk reads activation half kk / 4 at byte offset 32 (kk % 4).
+          // Descriptors and TMEM addresses of the stage, then the eight
+          // k-steps of this issuer's tile with immediate offsets.  k-step kk
+          // reads activation half kk / 4 at byte offset 32 (kk % 4).
           const uint64_t bd = xdesc0 + (uint64_t)xr.st * xstride;
           const uint64_t bd1 = bd + xhalf;
-          const uint32_t ta = tmem + (uint32_t)(A.a_base + ar.st * 2 * A_COLS);
+          const uint32_t ta =
+              tmem + (uint32_t)(A.a_base + (ar.st * 2 + mt) * A_COLS);
           const uint32_t acc0 = si > 0 ? 1u : 0u;
-          umma_ts(d0, ta, bd, idesc, acc0);
-          umma_ts(d1, ta + A_COLS, bd, idesc, acc0);
+          umma_ts(dm, ta, bd, idesc, acc0);
 #pragma unroll
-          for (int kk = 1; kk < 4; ++kk) {
-            umma_ts(d0, ta + kk * 8, bd + (uint64_t)(kk * 2), idesc, 1u);
-            umma_ts(d1, ta + A_COLS + kk * 8, bd + (uint64_t)(kk * 2), idesc, 1u);
-          }
+          for (int kk = 1; kk < 4; ++kk)
+            umma_ts(dm, ta + kk * 8, bd + (uint64_t)(kk * 2), idesc, 1u);
 #pragma unroll
-          for (int kk = 4; kk < KC / 16; ++kk) {
-            umma_ts(d0, ta + kk * 8, bd1 + (uint64_t)((kk - 4) * 2), idesc, 1u);
-            umma_ts(d1, ta + A_COLS + kk * 8, bd1 + (uint64_t)((kk - 4) * 2), idesc, 1u);
-          }
+          for (int kk = 4; kk < KC / 16; ++kk)
+            umma_ts(dm, ta + kk * 8, bd1 + (uint64_t)((kk - 4) * 2), idesc, 1u);
           umma_commit(&B->a_empty[ar.st]);
           umma_commit(&B->x_empty[xr.st]);
         }
@@ -846,7 +885,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
     }
-  } else if (warp >= DEC_WARP0) {
+  } else if (warp >= DEC_WARP0 && warp < DEC_WARP0 + NDEC_WARPS) {
     // -------------------------------------------------------------- decoders
     // Warp w may only reach TMEM lanes 32 (w % 4) .. + 31, so the four lane
     // quarters each get four decoder warps: one per (tile, half of the
@@ -1229,7 +1268,7 @@ static int grouped_tc(int mode, const uint16_t* x, int64_t x_stride, int64_t T, 
   // decoded-weight stages), else 64 (one expert taking many rows).
   A.nt = (T * R >= 48 * E) ? kb::tc::NT_MAX : 32;
   A.splits = 1;
-  const int plan_ints = (int)(4 * E + 2 + T * R);
+  const int plan_ints = kb::tc::plan_ints_for((int)E, (int)(T * R));
   st = kb::tc::layout(A, plan_ints);
   if (st != KB_OK) return st;
   return kb::tc::launch_tc(A, w0, w1, E * N, 1 << 30, stream);
