@@ -35,7 +35,8 @@
 //     subtractions and four bf16x2 multiplies -- the one rounding of the
 //     reference) and writes them with two tcgen05.st into a ring of two or
 //     three decoded-weight stages held in tensor memory.
-//   warp 2 (lanes 0, 1): MMA issuers, one per tile (a tcgen05.mma costs
+//   MMA issuers, one per tile (lane 0 of warps 2 and 3 in dense mode, lanes
+//     0 and 1 of warp 2 in the grouped modes; a tcgen05.mma costs
 //     its issuing thread ~110 cycles at these shapes, measured, so one thread
 //     cannot keep the tensor core busy).  Per k-chunk, eight tcgen05.mma with
 //     A (the decoded weights) read from TMEM and B (the activations) from
@@ -664,7 +665,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = first; i < it; ++i) drain_phase(&B->w_full[i % A.sw], (i / A.sw) & 1);
       for (int k = max(0, uc - 2); k < uc; ++k) drain_phase(&B->sc_full[k & 1], (k >> 1) & 1);
     }
-  } else if (A.x_tma && (warp == X_WARP0 || warp == X_WARP1)) {
+  } else if (A.x_tma && warp == X_WARP0) {
     // ------------------------------------- activation loader (dense: tensor copies)
     // Two 2-D tensor copies per k-chunk, one per 64-element half: NT token
     // rows x 128 bytes each, written by the copy engine in the 128-byte-
@@ -693,7 +694,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int first = max(0, it - A.sx);
       for (int i = first; i < it; ++i) drain_phase(&B->x_full[i % A.sx], (i / A.sx) & 1);
     }
-  } else if (warp == X_WARP0 || warp == X_WARP1) {
+  } else if (!A.x_tma && (warp == X_WARP0 || warp == X_WARP1)) {
     // ------------------------------------------------------ activation loader
     const int xt = (warp == X_WARP0 ? 0 : 32) + lane;
     Ring xr(A.sx);
@@ -723,14 +724,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!ok) break;
     }
     cp_async_wait_all();
-  } else if (warp == MMA_WARP) {
+  } else if (warp == MMA_WARP || (A.x_tma && warp == X_WARP1)) {
     // ----------------------------------------------------------- MMA issuers
     // One thread per tile: a tcgen05.mma costs its issuing thread about a
     // hundred cycles whatever its size at these shapes, so two issuers with
     // their own accumulators double the rate at which the tensor core is fed.
     // Each commits its own products to the stage barriers (count two).
-    if (lane < NISSUERS) {
-      const int mt = lane;
+    // Dense mode (activations by tensor copies, warp 3 free): lane 0 of warps
+    // 2 and 3, which issue independently.  Grouped modes (warps 1 and 3 gather
+    // activations): lanes 0 and 1 of warp 2, which still issue faster than one.
+    const bool issuer = A.x_tma ? lane == 0 : lane < NISSUERS;
+    if (issuer) {
+      const int mt = A.x_tma ? (warp == MMA_WARP ? 0 : 1) : lane;
       int uc = 0;
       bool ok = true;
       Ring ar(A.sa), xr(A.sx);
