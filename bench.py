@@ -627,12 +627,14 @@ def _ep_launches(model) -> int:
     n = 1  # lm_head
     for lw in model.layers:
         if lw.kind == "kda":
-            n += (3 if tc(proj, s.hidden) else 1) + (3 if model.kda_prepare else 2)
+            n += 1 + (3 if model.kda_prepare else 2)   # q/k/v: one launch on either path
         else:
             both = tc(s.mla_heads * s.mla_q_head_dim, s.hidden) and tc(
                 s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)
             n += (2 if both else 1) + 1
-        n += 2 if lw.dense_mlp is not None else 7
+        # MoE: router, dispatch, expert gate/up and down (the shared expert's
+        # rows ride in the same two launches), combine.
+        n += 2 if lw.dense_mlp is not None else 5
     return n
 
 

@@ -9,10 +9,11 @@
 // chosen experts, renormalised by (sum + 1e-20) and multiplied by the scaling
 // factor.
 //
-// Phase 1: CTA (expert block, token block) computes 4 experts x up to 8 tokens
-// of logits, one warp per expert, with a fixed reduction order (each lane sums
-// its strided 16-byte pieces in order, then a xor butterfly), so logits are
-// identical run to run.  Phase 2: the CTA that completes a token block
+// Phase 1: CTA (expert block, token block) computes 32 experts x up to 8
+// tokens of logits, each warp 4 experts x 4 tokens per pass (every 16-byte
+// piece it loads feeds four sums), with a fixed reduction order (each lane
+// sums its strided 16-byte pieces in order, then a xor butterfly), so logits
+// are identical run to run.  Phase 2: the CTA that completes a token block
 // (arrival counter, one publishing thread) selects the top_k of its tokens,
 // one warp per token, and resets the counter.  For E <= 256 every lane sorts
 // its eight candidates once with a sorting network and each pick is two
@@ -25,8 +26,11 @@
 
 namespace kb {
 
-constexpr int RT_WARPS = 4;  // experts per CTA
-constexpr int RT_TOK = 8;    // tokens per CTA
+constexpr int RT_WARPS = 8;               // warps per CTA
+constexpr int RT_EW = 4;                  // experts per warp
+constexpr int RT_EXP = RT_WARPS * RT_EW;  // experts per CTA
+constexpr int RT_TOK = 8;                 // tokens per CTA
+constexpr int RT_TQ = 4;                  // tokens per pass of a warp
 
 __global__ void __launch_bounds__(RT_WARPS * 32)
     router_kernel(const uint16_t* __restrict__ hidden, int64_t hs, int T, int K,
@@ -45,56 +49,71 @@ __global__ void __launch_bounds__(RT_WARPS * 32)
 
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint16_t* hsm = reinterpret_cast<uint16_t*>(smem_raw);  // [nt][K]
-  const int expert = blockIdx.x * RT_WARPS + warp;
-  const uint16_t* wrow = weight + (size_t)min(expert, E - 1) * K;
-  // The first eight 16-byte pieces of this warp's router row are requested
-  // before the hidden states are staged, so both fetches overlap.
-  uint4 wv[8];
+  // Warp w computes experts ebase .. ebase + 3 for the CTA's tokens, four
+  // tokens per pass: each 16-byte piece of a router row (from L2) and of a
+  // staged hidden row (from shared memory) feeds four (token, expert) sums.
+  // Every sum keeps the stated order: lane l takes pieces l, l + 32, ... in
+  // order (router_word_fma), then router_lane_sum and the xor butterfly.
+  const int ebase = blockIdx.x * RT_EXP + warp * RT_EW;
+  const uint16_t* wrow[RT_EW];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int w = u * 32 + lane;
-    wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
-  }
+  for (int i = 0; i < RT_EW; ++i) wrow[i] = weight + (size_t)min(ebase + i, E - 1) * K;
+  // The warp's first pieces are requested before the hidden states are
+  // staged, so both fetches overlap.
+  uint4 wv[RT_EW];
+#pragma unroll
+  for (int i = 0; i < RT_EW; ++i)
+    wv[i] = lane < words ? ldg_stream_v4(wrow[i] + (size_t)lane * 8) : make_uint4(0, 0, 0, 0);
   for (int e = threadIdx.x; e < nt * words; e += RT_WARPS * 32) {
     const int m = e / words, w = e - m * words;
     reinterpret_cast<uint4*>(hsm + (size_t)m * K)[w] =
         __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)(t0 + m) * hs) + w);
   }
   __syncthreads();
-  if (expert < E) {
-    float acc[RT_TOK][4];
+  if (ebase < E) {
+    for (int tq = 0; tq < nt; tq += RT_TQ) {
+      float acc[RT_TQ][RT_EW][4];
 #pragma unroll
-    for (int m = 0; m < RT_TOK; ++m)
+      for (int t = 0; t < RT_TQ; ++t)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
-    for (int w0 = 0; w0 < words; w0 += 32 * 8) {
-      if (w0 > 0) {
+        for (int i = 0; i < RT_EW; ++i)
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int w = w0 + u * 32 + lane;
-          wv[u] = (w < words) ? ldg_stream_v4(wrow + (size_t)w * 8) : make_uint4(0, 0, 0, 0);
-        }
+          for (int j = 0; j < 4; ++j) acc[t][i][j] = 0.f;
+      if (tq > 0) {
+#pragma unroll
+        for (int i = 0; i < RT_EW; ++i)
+          wv[i] = lane < words ? ldg_stream_v4(wrow[i] + (size_t)lane * 8) : make_uint4(0, 0, 0, 0);
       }
+      for (int w = lane; w < words; w += 32) {
+        // Next pieces of the router rows, requested before these are used.
+        uint4 wn[RT_EW];
+        const int wnext = w + 32;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int w = w0 + u * 32 + lane;
-        if (w < words) {
+        for (int i = 0; i < RT_EW; ++i)
+          wn[i] = wnext < words ? ldg_stream_v4(wrow[i] + (size_t)wnext * 8)
+                                : make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int m = 0; m < RT_TOK; ++m) {
-            if (m < nt) {
-              const uint4 hv = reinterpret_cast<const uint4*>(hsm + (size_t)m * K)[w];
-              router_word_fma(wv[u], hv, acc[m]);
-            }
+        for (int t = 0; t < RT_TQ; ++t) {
+          if (tq + t < nt) {
+            const uint4 hv = reinterpret_cast<const uint4*>(hsm + (size_t)(tq + t) * K)[w];
+#pragma unroll
+            for (int i = 0; i < RT_EW; ++i) router_word_fma(wv[i], hv, acc[t][i]);
           }
         }
+#pragma unroll
+        for (int i = 0; i < RT_EW; ++i) wv[i] = wn[i];
       }
-    }
 #pragma unroll
-    for (int m = 0; m < RT_TOK; ++m) {
-      float v = router_lane_sum(acc[m]);
+      for (int t = 0; t < RT_TQ; ++t) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0 && m < nt) logits[(size_t)(t0 + m) * E + expert] = v;
+        for (int i = 0; i < RT_EW; ++i) {
+          float v = router_lane_sum(acc[t][i]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0 && tq + t < nt && ebase + i < E)
+            logits[(size_t)(t0 + tq + t) * E + ebase + i] = v;
+        }
+      }
     }
   }
 
@@ -242,7 +261,7 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
   float* logits = reinterpret_cast<float*>(workspace);
   const size_t lbytes = ((size_t)T * E * sizeof(float) + 255) / 256 * 256;
   int* counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + lbytes);
-  const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
+  const dim3 grid((unsigned)((E + kb::RT_EXP - 1) / kb::RT_EXP),
                   (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
   const size_t smem = (size_t)std::min<int64_t>(T, kb::RT_TOK) * K * sizeof(uint16_t);
   const int attr = kb::router_smem_limit();
@@ -366,7 +385,7 @@ extern "C" int kb_router_topk_static(const uint16_t* hidden, int64_t h_stride, i
   int* counters = reinterpret_cast<int*>(scratch);
   float* logits =
       reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kb::RT_STATIC_COUNTER_BYTES);
-  const dim3 grid((unsigned)((E + kb::RT_WARPS - 1) / kb::RT_WARPS),
+  const dim3 grid((unsigned)((E + kb::RT_EXP - 1) / kb::RT_EXP),
                   (unsigned)((T + kb::RT_TOK - 1) / kb::RT_TOK));
   const size_t smem = (size_t)std::min<int64_t>(T, kb::RT_TOK) * K * sizeof(uint16_t);
   return kb::launch(kb::router_kernel, grid, dim3(kb::RT_WARPS * 32), smem, stream, hidden,

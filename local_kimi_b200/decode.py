@@ -65,7 +65,11 @@ class KimiLinearShape:
 @dataclass
 class LayerWeights:
     kind: str                       # "kda" or "mla"
-    qkv: list[tuple[torch.Tensor, torch.Tensor]] | None = None   # KDA q, k, v
+    qkv: list[tuple[torch.Tensor, torch.Tensor]] | None = None   # KDA q, k, v (views)
+    # The three KDA projections stored as one [3 * C, K/2] matrix (q rows, then
+    # k, then v); ``qkv`` holds row views of it.  Many-token steps project all
+    # three in one tensor-core launch.
+    qkv_fused: tuple[torch.Tensor, torch.Tensor] | None = None
     q_proj: tuple[torch.Tensor, torch.Tensor] | None = None      # MLA
     kv_b: tuple[torch.Tensor, torch.Tensor] | None = None        # MLA
     o_proj: tuple[torch.Tensor, torch.Tensor] | None = None
@@ -142,9 +146,14 @@ class HotPathDecoder:
             )
         else:
             proj = s.kda_heads * s.kda_head_dim
+            parts = [self._quant(proj, s.hidden) for _ in range(3)]
+            fused = (torch.cat([pk for pk, _ in parts]), torch.cat([sc for _, sc in parts]))
+            del parts
             lw = LayerWeights(
                 kind="kda",
-                qkv=[self._quant(proj, s.hidden) for _ in range(3)],
+                qkv=[(fused[0][i * proj:(i + 1) * proj], fused[1][i * proj:(i + 1) * proj])
+                     for i in range(3)],
+                qkv_fused=fused,
                 o_proj=self._quant(s.hidden, proj),
                 kda_state=0.05 * torch.randn((B, s.kda_heads, s.kda_head_dim, s.kda_head_dim),
                                              generator=self._gen, device=self.device),
@@ -255,8 +264,15 @@ class HotPathDecoder:
         eps = getattr(self, "ep_layers", None)
         for li, lw in enumerate(self.layers):
             if lw.kind == "kda":
-                q_in, k_in, v_in = ops.w4a16_dense_multi(
-                    [(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])])
+                probs = [(x, *lw.qkv[0]), (x, *lw.qkv[1]), (x, *lw.qkv[2])]
+                if lw.qkv_fused is not None and ops.multi_prefers_tc(probs):
+                    # One launch over the three stacked matrices: enough row
+                    # tiles to fill the GPU, then column views (one row stride).
+                    n = lw.qkv[0][0].shape[0]
+                    y = ops.w4a16_dense_tc(x, *lw.qkv_fused)
+                    q_in, k_in, v_in = y[:, :n], y[:, n:2 * n], y[:, 2 * n:]
+                else:
+                    q_in, k_in, v_in = ops.w4a16_dense_multi(probs)
                 if self.kda_prepare:
                     kin = ops.kda_prepare(q_in, k_in, v_in, *lw.conv_state, *lw.conv_w,
                                           self.raw_decay, lw.dt_bias, lw.a_log, self.raw_beta,

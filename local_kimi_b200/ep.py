@@ -86,8 +86,10 @@ class CudaExperts:
 
     def dispatch(self, hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
                  capacity: int):
-        """(payload bf16 [world*capacity, H+8], slots int32 [T*k])."""
-        return ops.ep_dispatch(hidden, routed, per_rank, world, capacity)
+        """(payload bf16 [world*capacity + T, H+8], slots int32 [T*k]); the last
+        T rows are room for the rank's own rows for the shared expert."""
+        return ops.ep_dispatch(hidden, routed, per_rank, world, capacity,
+                               extra_rows=hidden.shape[0])
 
     def experts(self, payload: torch.Tensor, bank: LocalExpertBank) -> torch.Tensor:
         """Down(SwiGLU(gate/up)) of each payload row with its local expert, bf16 [n, H];
@@ -166,7 +168,8 @@ class ExpertParallelMoE:
         if self.last_received is None:
             return 0
         ids = ops.payload_ids(self.last_received)[:, 0]
-        return int(torch.unique(ids[ids >= 0]).numel())
+        routed = ids[(ids >= 0) & (ids < self.bank.per_rank)]
+        return int(torch.unique(routed).numel())
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
         """hidden bf16 [T, H] (this rank's tokens) -> bf16 [T, H]."""
@@ -176,10 +179,21 @@ class ExpertParallelMoE:
         stable, weights = be.route(hidden, layer)
         routed = stable[:, :k].contiguous()
         capacity = max(1, tokens * k)
+        n = self.world * capacity
         payload, slots = be.dispatch(hidden, routed, bank.per_rank, self.world, capacity)
-        received = self._exchange(payload)
-        self.last_payload, self.last_received = payload, received
-        y_recv = be.experts(received, bank)
-        y_back = self._exchange(y_recv)
-        y_shared = be.shared(hidden, bank)
-        return be.combine(y_back, slots, weights, y_shared)
+        # The received rows, then this rank's own rows for the shared expert
+        # (local bank slot per_rank): one gate/up and one down launch serve
+        # both, so the shared expert's few row tiles do not run as launches of
+        # their own on a fraction of the GPU.
+        if self.world == 1:
+            received = payload if payload.shape[0] >= n + tokens else torch.cat(
+                (payload[:n], payload.new_empty((tokens, payload.shape[1]))))
+        else:
+            received = payload.new_empty((n + tokens, payload.shape[1]))
+            dist.all_to_all_single(received[:n], payload[:n].contiguous(), group=self.group)
+        received[n:, :width].copy_(hidden)
+        ops.payload_ids(received[n:]).fill_(bank.per_rank)
+        self.last_payload, self.last_received = payload[:n], received
+        y_all = be.experts(received, bank)
+        y_back = self._exchange(y_all[:n])
+        return be.combine(y_back, slots, weights, y_all[n:])

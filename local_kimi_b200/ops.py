@@ -190,6 +190,11 @@ def w4a16_dense_engine(
     return out
 
 
+def multi_prefers_tc(problems: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]) -> bool:
+    """Whether ``w4a16_dense_multi`` runs these problems on the tensor-core path."""
+    return bool(problems) and all(prefer_tc(*_validate_dense(*pr)) for pr in problems)
+
+
 def w4a16_dense_multi(
     problems: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
 ) -> list[torch.Tensor]:
@@ -197,7 +202,7 @@ def w4a16_dense_multi(
     launch each when ``prefer_tc`` picks that path for every problem)."""
     if len(problems) > _lib.MAX_DENSE_PROBLEMS:
         raise ValueError(f"at most {_lib.MAX_DENSE_PROBLEMS} problems per launch")
-    if problems and all(prefer_tc(*_validate_dense(*pr)) for pr in problems):
+    if multi_prefers_tc(problems):
         return [w4a16_dense_tc(*pr) for pr in problems]
     arr = (_lib.DenseProblem * max(1, len(problems)))()
     outs: list[torch.Tensor] = []
@@ -580,14 +585,15 @@ def moe_combine_routes(routes: torch.Tensor, weights: torch.Tensor) -> torch.Ten
 
 
 def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
-                capacity: int) -> tuple[torch.Tensor, torch.Tensor]:
+                capacity: int, extra_rows: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
     """Pack each routed (token, route) pair's hidden row for its expert's rank.
 
     hidden bf16 [T, H]; routed int64 [T, k] global expert ids.  Returns
     (payload bf16 [world*capacity, H+8]: per slot the row, then the
     owner-local expert id as an int64 in the next four bf16 -- -1 for an
     unused slot; slots int32 [T*k]: the payload slot of each pair).
-    capacity must be at least T*k.
+    capacity must be at least T*k.  ``extra_rows`` more rows are allocated
+    after the slots and left unwritten (room for rows the caller appends).
     """
     if hidden.dtype != torch.bfloat16 or hidden.ndim != 2:
         raise TypeError("hidden must be BF16 [T, H]")
@@ -600,11 +606,11 @@ def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world
     k = routed.shape[1]
     if capacity < t * k:
         raise ValueError("capacity must be at least tokens * top_k")
-    payload = torch.empty((world * capacity, h + 8), dtype=torch.bfloat16,
+    payload = torch.empty((world * capacity + extra_rows, h + 8), dtype=torch.bfloat16,
                           device=hidden.device)
     slots = torch.empty((t * k,), dtype=torch.int32, device=hidden.device)
     if t == 0:
-        payload_ids(payload).fill_(-1)
+        payload_ids(payload[:world * capacity]).fill_(-1)
         return payload, slots
     x = _rows_16b(hidden)
     r = routed if routed.stride(1) == 1 else routed.contiguous()
