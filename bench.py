@@ -78,7 +78,7 @@ def _args() -> argparse.Namespace:
                          "per-op: the registry-level launches captured in a CUDA graph")
     ap.add_argument("--case",
                     choices=("step", "lm_head", "moe", "eager", "program", "dense_sweep",
-                             "ep_moe", "moe_layers"),
+                             "ep_moe", "moe_layers", "kda", "experts"),
                     default="step",
                     help="step = the benchmark; the others run one op family eagerly for "
                          "profiling (lm_head: the INT4 lm_head GEMV; moe: router + experts + "
@@ -88,7 +88,11 @@ def _args() -> argparse.Namespace:
                          "ep_moe: one MoE layer with its experts sharded over the torchrun "
                          "ranks, --batch tokens in total split over them (NCCL all-to-all); "
                          "moe_layers: router + gate/up + down/combine of distinct MoE layers "
-                         "back to back in one graph (--zipf S skews the expert popularity)")
+                         "back to back in one graph (--zipf S skews the expert popularity); "
+                         "kda: the KDA state step of --batch sequences (32 heads of 128x128); "
+                         "experts: the routed-expert gate/up+SwiGLU and down tensor-core "
+                         "launches of one MoE layer for --batch tokens (top-8 of 256 experts, "
+                         "uniform random routes, as the expert-parallel step at one GPU)")
     ap.add_argument("--wide-sweep", action="store_true",
                     help="dense_sweep: also the MLA and dense-MLP shapes, both paths at every M")
     ap.add_argument("--zipf", type=float, default=0.0,
@@ -1163,6 +1167,42 @@ def run_case(args) -> dict:
         fn = lambda: moe_forward(x, layer)  # noqa: E731
         nbytes = None
         per_step = 3
+    elif args.case == "kda":
+        H, D = s.kda_heads, s.kda_head_dim
+        st = 0.05 * torch.randn((args.batch, H, D, D), generator=gen, device="cuda")
+        q = torch.nn.functional.normalize(
+            torch.randn((args.batch, H, D), generator=gen, device="cuda"), dim=-1)
+        k = torch.nn.functional.normalize(
+            torch.randn((args.batch, H, D), generator=gen, device="cuda"), dim=-1)
+        v = 0.2 * torch.randn((args.batch, H, D), generator=gen, device="cuda")
+        dec = -(0.005 + 0.075 * torch.rand((args.batch, H, D), generator=gen, device="cuda"))
+        beta = torch.sigmoid(torch.randn((args.batch, H), generator=gen, device="cuda"))
+        ob = torch.empty((args.batch, H, D), dtype=torch.bfloat16, device="cuda")
+        fn = lambda: ops.kda_decode_step(st, q, k, v, dec, beta, scale=D ** -0.5,  # noqa: E731
+                                         out_bf16=ob)
+        nbytes = 2 * st.numel() * 4 + 5 * q.numel() * 4
+        per_step = 1
+    elif args.case == "experts":
+        E, I, top_k = s.experts, s.moe_intermediate, s.top_k
+        q = lambda n, kk: ops.quantise(  # noqa: E731
+            (0.02 * torch.randn((E * n, kk), generator=gen, device="cuda")).to(torch.bfloat16),
+            args.group)
+        w1, w3, w2 = q(I, s.hidden), q(I, s.hidden), q(s.hidden, I)
+        w1p, w1s = w1[0].view(E, I, -1), w1[1].view(E, I, -1)
+        w3p, w3s = w3[0].view(E, I, -1), w3[1].view(E, I, -1)
+        w2p, w2s = w2[0].view(E, s.hidden, -1), w2[1].view(E, s.hidden, -1)
+        rows = args.batch * top_k
+        idx = torch.randint(0, E, (rows, 1), generator=gen, device="cuda")
+        xr = torch.randn((rows, s.hidden), generator=gen, device="cuda").to(torch.bfloat16)
+
+        def fn():
+            act = ops.w4a16_swiglu_tc(xr, idx, w1p, w1s, w3p, w3s)
+            ops.w4a16_grouped_tc(act[:, 0], idx, w2p, w2s)
+
+        touched = int(torch.unique(idx).numel())
+        per_expert = sum(t[0].numel() * t.element_size() for t in (w1p, w1s, w3p, w3s, w2p, w2s))
+        nbytes = touched * per_expert
+        per_step = 2
     elif args.case == "program":
         model = HotPathDecoder(args.batch, group=args.group, layers=args.layers)
         prog, _ = model.build_program(model.x0.clone())

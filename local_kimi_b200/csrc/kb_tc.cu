@@ -92,6 +92,7 @@ constexpr int MAX_SW = 16;
 constexpr int MAX_ASSIGN = 4096;        // grouped modes: T * R
 constexpr int MAX_SLOTS = 520;          // grouped modes: experts in the bank
 constexpr int MAX_SPLITS = 4;           // reduction-axis splits per tile
+constexpr int MAX_RED = 16;             // split tiles one CTA may finish (deferred reductions)
 constexpr long long WAIT_NS = 2000000000LL;
 constexpr long long DRAIN_NS = 200000000LL;
 
@@ -542,7 +543,68 @@ struct Bars {
   uint32_t tmem_base;
   int abort_flag;
   int epi_last;
+  // Split tiles whose last partial this CTA wrote: reduced by all threads at
+  // the end of the kernel.
+  int red_n;
+  int red_unit[MAX_RED];
 };
+
+// Deferred split-K reduction (dense mode): for each split tile this CTA
+// finished last, every thread sums 16-byte pieces (four rows of one token of
+// one tile) over the splits in split order -- the same additions, in the same
+// order, as a per-row sum -- and stores four bf16 outputs; then the tile's
+// arrival counter is reset for the next launch.
+__device__ __forceinline__ void reduce_splits(const Args& A, const Plan& P, Bars* B) {
+  const int NT = A.nt;
+  for (int li = 0; li < B->red_n; ++li) {
+    const Unit U = unit_of(A, P, B->red_unit[li]);
+    __threadfence();
+    const int items = 2 * U.nt * (BM / 4);
+    const size_t split_stride = (size_t)2 * NT * BM;
+    const float* base = A.ws + (size_t)U.tile * A.splits * split_stride;
+    for (int e0 = threadIdx.x; e0 < items; e0 += 2 * NTHREADS) {
+      float4 p[2][MAX_SPLITS];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = min(e0 + i * NTHREADS, items - 1);
+        const int m = e / (U.nt * (BM / 4));
+        const int rem = e - m * U.nt * (BM / 4);
+        const int j = rem / (BM / 4), r4 = rem - j * (BM / 4);
+        const float* src = base + (size_t)m * NT * BM + (size_t)j * BM + r4 * 4;
+#pragma unroll
+        for (int k = 0; k < MAX_SPLITS; ++k)
+          p[i][k] = k < A.splits ? __ldcg(reinterpret_cast<const float4*>(src + k * split_stride))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = e0 + i * NTHREADS;
+        if (e >= items) break;
+        const int m = e / (U.nt * (BM / 4));
+        const int rem = e - m * U.nt * (BM / 4);
+        const int j = rem / (BM / 4), r4 = rem - j * (BM / 4);
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < MAX_SPLITS; ++k) {
+          if (k < A.splits) {
+            t.x += p[i][k].x;
+            t.y += p[i][k].y;
+            t.z += p[i][k].z;
+            t.w += p[i][k].w;
+          }
+        }
+        const int row = tile_row(A, U.rt, m) + r4 * 4;
+        uint16_t* y = A.y + (size_t)(U.tok0 + j) * A.ys + row;
+        const float v[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (row + c < A.N) y[c] = float_to_bf16_bits(v[c]);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) A.counters[U.tile] = 0;
+  }
+}
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
@@ -577,6 +639,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     mbar_init(&B->drain, NISSUERS);
     B->abort_flag = 0;
+    B->red_n = 0;
     mbar_fence_init();
   }
   if (warp == X_WARP1) {
@@ -842,52 +905,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           B->epi_last = (old == A.splits - 1);
         }
         named_barrier(1, 128);
-        if (B->epi_last) {
-          __threadfence();
-          const float* base = A.ws + (size_t)U.tile * A.splits * 2 * NT * BM + r;
-          // Two tokens at a time: all splits' partials of both tiles are
-          // requested before any is summed (the loads are independent; the
-          // sums then run in split order).
-          for (int j0 = 0; j0 < U.nt; j0 += 2) {
-            float pg[MAX_SPLITS][2], ph[MAX_SPLITS][2];
-#pragma unroll
-            for (int k = 0; k < MAX_SPLITS; ++k) {
-              if (k < A.splits) {
-                const float* pk = base + (size_t)k * 2 * NT * BM;
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                  const int j = min(j0 + jj, U.nt - 1);
-                  pg[k][jj] = __ldcg(pk + (size_t)j * BM);
-                  ph[k][jj] = __ldcg(pk + (size_t)(NT + j) * BM);
-                }
-              }
-            }
-#pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-              const int j = j0 + jj;
-              if (j >= U.nt) break;
-              float g = 0.f, h = 0.f;
-#pragma unroll
-              for (int k = 0; k < MAX_SPLITS; ++k) {
-                if (k < A.splits) {
-                  g += pg[k][jj];
-                  h += ph[k][jj];
-                }
-              }
-              int xr, yr;
-              rows_of(A, P, U, j, xr, yr);
-              uint16_t* yrow = A.y + (size_t)yr * A.ys;
-              if (A.mode == SWIGLU) {
-                if (v0) yrow[row0 + r] = float_to_bf16_bits(swiglu_contract(g, h));
-              } else {
-                if (v0) yrow[row0 + r] = float_to_bf16_bits(g);
-                if (v1) yrow[row1 + r] = float_to_bf16_bits(h);
-              }
-            }
+        if (B->epi_last && q == 0 && lane == 0) {
+          // The sums run after the roles finish, on all threads (more loads
+          // in flight than the four epilogue warps can keep).
+          if (B->red_n < MAX_RED) {
+            B->red_unit[B->red_n++] = u;
+          } else {
+            *abort_f = 1;
+            atomicOr(A.err, ERR_TIMEOUT);
           }
-          named_barrier(1, 128);
-          if (q == 0 && lane == 0) A.counters[U.tile] = 0;
         }
+        named_barrier(1, 128);
       }
     }
   } else if (warp >= DEC_WARP0 && warp < DEC_WARP0 + NDEC_WARPS) {
@@ -979,6 +1007,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                  "r"(tmem_cols)
                  : "memory");
   }
+  if (B->red_n > 0) reduce_splits(A, P, B);
 }
 
 // ---------------------------------------------------------------------------
