@@ -244,6 +244,10 @@ KB_API int kb_kda_prepare(const uint16_t* q_in, const uint16_t* k_in, const uint
 /* travel in one exchange; unused slots carry id -1 (the grouped kernels skip  */
 /* them).  slots[t * k + r] = d * capacity + p, int32 [T * k].                 */
 /* capacity >= T * k (then nothing can overflow); T * k <= 8192, world <= 64.  */
+/* shared_id >= 0: send_rows has T more rows after the world * capacity slots */
+/* and row world * capacity + t receives hidden[t] with id shared_id (the     */
+/* rank's own rows for its shared expert, processed with the received rows);  */
+/* -1: no extra rows.                                                          */
 /*                                                                             */
 /* kb_ep_combine: out[t] = bf16( bf16(sum_{r<k} float(y[slots[t*k+r]]) *       */
 /* weights[t, r]) + shared[t] ), fp32 sum in route order (the combine of       */
@@ -251,7 +255,8 @@ KB_API int kb_kda_prepare(const uint16_t* q_in, const uint16_t* k_in, const uint
 /* ------------------------------------------------------------------------- */
 KB_API int kb_ep_dispatch(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t H,
                           const int64_t* idx, int64_t idx_stride, int64_t k, int64_t per_rank,
-                          int64_t world, int64_t capacity, uint16_t* send_rows,
+                          int64_t world, int64_t capacity,
+                          int64_t shared_id, uint16_t* send_rows,
                           int32_t* slots, void* stream);
 KB_API int kb_ep_combine(const uint16_t* y, const int32_t* slots, int64_t T, int64_t k,
                          int64_t H, const float* weights, int64_t w_stride,

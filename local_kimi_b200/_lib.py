@@ -109,7 +109,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kb_ep_dispatch": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
-         c_int64, c_void_p, c_void_p, c_void_p],
+         c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     ),
     "kb_ep_combine": (
         c_int,

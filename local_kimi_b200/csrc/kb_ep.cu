@@ -69,8 +69,8 @@ __device__ void ep_positions(const int64_t* idx, int64_t istride, int T, int k, 
 __global__ void __launch_bounds__(EP_THREADS)
     ep_dispatch_kernel(const uint16_t* __restrict__ hidden, int64_t hs, int T, int H,
                        const int64_t* __restrict__ idx, int64_t istride, int k, int per_rank,
-                       int world, int capacity, uint16_t* __restrict__ send_rows,
-                       int* __restrict__ slots, uint32_t* err) {
+                       int world, int capacity, int64_t shared_id,
+                       uint16_t* __restrict__ send_rows, int* __restrict__ slots, uint32_t* err) {
   __shared__ int cnt[EP_MAX_RANKS];
   extern __shared__ int pos[];                 // [pairs], then the destinations as bytes
   pdl_wait();
@@ -81,8 +81,20 @@ __global__ void __launch_bounds__(EP_THREADS)
   const int gw = blockIdx.x * (EP_THREADS / 32) + warp, nw = gridDim.x * (EP_THREADS / 32);
   const int vecs = H >> 3;
   const int64_t ps = (int64_t)H + 8;  // payload row stride (elements)
-  // Rows of the routed pairs: one warp per pair.
-  for (int a = gw; a < pairs; a += nw) {
+  // Rows of the routed pairs, one warp per pair; with shared_id >= 0 also
+  // every token's row once more after the world * capacity slots (the rank's
+  // own rows for the shared expert, which are not exchanged).
+  const int extra = shared_id >= 0 ? T : 0;
+  for (int a = gw; a < pairs + extra; a += nw) {
+    if (a >= pairs) {
+      const int t = a - pairs;
+      const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * hs);
+      uint4* dst = reinterpret_cast<uint4*>(send_rows + ((size_t)world * capacity + t) * ps);
+      for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+      if (lane == 0)
+        dst[vecs] = make_uint4((uint32_t)shared_id, (uint32_t)((uint64_t)shared_id >> 32), 0u, 0u);
+      continue;
+    }
     const int t = a / k, r = a - t * k;
     const int64_t e = idx[(size_t)t * istride + r];
     const bool ok = e >= 0 && e < (int64_t)per_rank * world;
@@ -160,7 +172,8 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 extern "C" int kb_ep_dispatch(const uint16_t* hidden, int64_t h_stride, int64_t T, int64_t H,
                               const int64_t* idx, int64_t idx_stride, int64_t k,
                               int64_t per_rank, int64_t world, int64_t capacity,
-                              uint16_t* send_rows, int32_t* slots, void* stream) {
+                              int64_t shared_id, uint16_t* send_rows, int32_t* slots,
+                              void* stream) {
   kb::clear_error();
   KB_REQUIRE(T >= 0 && H > 0 && k > 0 && per_rank > 0 && world > 0 && capacity > 0,
              KB_ERR_BAD_SHAPE, "dispatch: bad shape");
@@ -192,7 +205,7 @@ extern "C" int kb_ep_dispatch(const uint16_t* hidden, int64_t h_stride, int64_t 
   }
   return kb::launch(kb::ep_dispatch_kernel, dim3(grid), dim3(kb::EP_THREADS), smem, stream,
                     hidden, h_stride, (int)T, (int)H, idx, idx_stride, (int)k, (int)per_rank,
-                    (int)world, (int)capacity, send_rows, slots, err);
+                    (int)world, (int)capacity, shared_id, send_rows, slots, err);
 }
 
 extern "C" int kb_ep_combine(const uint16_t* y, const int32_t* slots, int64_t T, int64_t k,

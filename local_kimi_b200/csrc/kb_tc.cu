@@ -302,6 +302,22 @@ __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Shared-memory loads by 32-bit shared address (ordered after the barrier
+// waits like the other volatile instructions).
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major tile.
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4));
@@ -610,8 +626,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
               const __grid_constant__ CUtensorMap tmx, const Args A) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // Aligned to 1024 bytes by pointer arithmetic on the shared array, so the
+  // compiler keeps the shared state space and emits shared-memory loads and
+  // stores (not generic ones) for everything placed in it.
+  uint8_t* smem =
+      smem_raw + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) &
+                  1023u);
   Bars* B = reinterpret_cast<Bars*>(smem + A.off_bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NT = A.nt;
@@ -935,7 +955,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     Ring wr(A.sw), ar(A.sa);
     const int swz = (r >> 1) & 3;
-    const uint32_t wrow = (uint32_t)(m * W_TILE + r * 64);
+    const uint32_t wrow = smem_addr(ring_w) + (uint32_t)(m * W_TILE + r * 64);
     const uint32_t piece0 = (uint32_t)(((2 * h) ^ swz) << 4);
     const uint32_t piece1 = (uint32_t)(((2 * h + 1) ^ swz) << 4);
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
@@ -943,7 +963,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int sb = uc & 1;
       if (!wait_phase(&B->sc_full[sb], (uc >> 1) & 1, abort_f, A.err)) break;
       const bool rv = r < valid_rows(A, U.rt, m);
-      const uint16_t* srow = scl + (size_t)(sb * 2 + m) * BM * ng + (size_t)r * ng;
+      const uint32_t srow = smem_addr(scl + (size_t)(sb * 2 + m) * BM * ng + (size_t)r * ng);
       for (int si = 0; si < U.s1 - U.s0; ++si, wr.next(), ar.next()) {
         const int s = chunk_of(U, si);
         const int wst = wr.st, ast = ar.st;
@@ -952,12 +972,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        const uint8_t* wsrc = ring_w + (size_t)wst * 2 * W_TILE + wrow;
-        const uint4 qa = lds_v4(wsrc + piece0);
-        const uint4 qb = lds_v4(wsrc + piece1);
+        const uint32_t wsrc = wrow + (uint32_t)(wst * 2 * W_TILE);
+        const uint4 qa = ld_shared_v4(wsrc + piece0);
+        const uint4 qb = ld_shared_v4(wsrc + piece1);
         const int k0 = s * KC + h * 64;   // reduction index of this thread's first weight
-        const uint32_t sa = rv ? (uint32_t)srow[k0 >> (5 + A.gshift)] : 0u;
-        const uint32_t sbv = rv ? (uint32_t)srow[(k0 + 32) >> (5 + A.gshift)] : 0u;
+        const uint32_t sa = rv ? ld_shared_u16(srow + 2u * (uint32_t)(k0 >> (5 + A.gshift))) : 0u;
+        const uint32_t sbv =
+            rv ? ld_shared_u16(srow + 2u * (uint32_t)((k0 + 32) >> (5 + A.gshift))) : 0u;
         const uint32_t col = tmem + lane_bits + (uint32_t)(A.a_base + (ast * 2 + m) * A_COLS + h * 32);
         {
           const uint32_t sc2 = sa | (sa << 16);

@@ -87,9 +87,8 @@ class CudaExperts:
     def dispatch(self, hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
                  capacity: int):
         """(payload bf16 [world*capacity + T, H+8], slots int32 [T*k]); the last
-        T rows are room for the rank's own rows for the shared expert."""
-        return ops.ep_dispatch(hidden, routed, per_rank, world, capacity,
-                               extra_rows=hidden.shape[0])
+        T rows are the rank's own rows with the shared expert's local id."""
+        return ops.ep_dispatch(hidden, routed, per_rank, world, capacity, shared_id=per_rank)
 
     def experts(self, payload: torch.Tensor, bank: LocalExpertBank) -> torch.Tensor:
         """Down(SwiGLU(gate/up)) of each payload row with its local expert, bf16 [n, H];
@@ -177,7 +176,7 @@ class ExpertParallelMoE:
         tokens, width = hidden.shape
         k = layer.top_k
         stable, weights = be.route(hidden, layer)
-        routed = stable[:, :k].contiguous()
+        routed = stable[:, :k]   # row-strided view; the dispatch kernel takes the stride
         capacity = max(1, tokens * k)
         n = self.world * capacity
         payload, slots = be.dispatch(hidden, routed, bank.per_rank, self.world, capacity)
@@ -185,14 +184,20 @@ class ExpertParallelMoE:
         # (local bank slot per_rank): one gate/up and one down launch serve
         # both, so the shared expert's few row tiles do not run as launches of
         # their own on a fraction of the GPU.
+        # A dispatch that already wrote the shared rows (after the slots)
+        # returns n + tokens rows; otherwise they are appended here.
+        own = payload.shape[0] >= n + tokens
         if self.world == 1:
-            received = payload if payload.shape[0] >= n + tokens else torch.cat(
+            received = payload if own else torch.cat(
                 (payload[:n], payload.new_empty((tokens, payload.shape[1]))))
         else:
             received = payload.new_empty((n + tokens, payload.shape[1]))
             dist.all_to_all_single(received[:n], payload[:n].contiguous(), group=self.group)
-        received[n:, :width].copy_(hidden)
-        ops.payload_ids(received[n:]).fill_(bank.per_rank)
+            if own:
+                received[n:].copy_(payload[n:])
+        if not own:
+            received[n:, :width].copy_(hidden)
+            ops.payload_ids(received[n:]).fill_(bank.per_rank)
         self.last_payload, self.last_received = payload[:n], received
         y_all = be.experts(received, bank)
         y_back = self._exchange(y_all[:n])

@@ -585,15 +585,16 @@ def moe_combine_routes(routes: torch.Tensor, weights: torch.Tensor) -> torch.Ten
 
 
 def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world: int,
-                capacity: int, extra_rows: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+                capacity: int, shared_id: int = -1) -> tuple[torch.Tensor, torch.Tensor]:
     """Pack each routed (token, route) pair's hidden row for its expert's rank.
 
     hidden bf16 [T, H]; routed int64 [T, k] global expert ids.  Returns
     (payload bf16 [world*capacity, H+8]: per slot the row, then the
     owner-local expert id as an int64 in the next four bf16 -- -1 for an
     unused slot; slots int32 [T*k]: the payload slot of each pair).
-    capacity must be at least T*k.  ``extra_rows`` more rows are allocated
-    after the slots and left unwritten (room for rows the caller appends).
+    capacity must be at least T*k.  With ``shared_id`` >= 0 the payload has T
+    more rows after the slots: row world*capacity + t is hidden[t] with id
+    ``shared_id`` (the rank's own rows for its shared expert, not exchanged).
     """
     if hidden.dtype != torch.bfloat16 or hidden.ndim != 2:
         raise TypeError("hidden must be BF16 [T, H]")
@@ -606,7 +607,8 @@ def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world
     k = routed.shape[1]
     if capacity < t * k:
         raise ValueError("capacity must be at least tokens * top_k")
-    payload = torch.empty((world * capacity + extra_rows, h + 8), dtype=torch.bfloat16,
+    extra = t if shared_id >= 0 else 0
+    payload = torch.empty((world * capacity + extra, h + 8), dtype=torch.bfloat16,
                           device=hidden.device)
     slots = torch.empty((t * k,), dtype=torch.int32, device=hidden.device)
     if t == 0:
@@ -616,7 +618,7 @@ def ep_dispatch(hidden: torch.Tensor, routed: torch.Tensor, per_rank: int, world
     r = routed if routed.stride(1) == 1 else routed.contiguous()
     _lib.call("kb_ep_dispatch", _p(x), c_int64(x.stride(0)), c_int64(t), c_int64(h), _p(r),
               c_int64(r.stride(0)), c_int64(k), c_int64(per_rank), c_int64(world),
-              c_int64(capacity), _p(payload), _p(slots), _stream(x.device))
+              c_int64(capacity), c_int64(shared_id), _p(payload), _p(slots), _stream(x.device))
     return payload, slots
 
 

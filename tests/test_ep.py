@@ -237,6 +237,17 @@ def test_dispatch_and_combine_kernels_match_cpu_restatement(cuda, world, tokens)
     shared = torch.randn((tokens, h), generator=g).to(torch.bfloat16)
     out = ops.ep_combine(y.to(cuda), slots, w.to(cuda), shared.to(cuda))
     assert_close(out, OracleExperts().combine(y, ref_slots, w, shared), what="ep combine")
+    # With a shared-expert id the same slots, then every token's row once more
+    # with that id.
+    p2, s2 = ops.ep_dispatch(hidden.to(cuda), routed.to(cuda), per_rank, world, cap,
+                             shared_id=per_rank)
+    assert p2.shape[0] == world * cap + tokens
+    assert torch.equal(s2.cpu(), ref_slots)
+    ids2 = ops.payload_ids(p2).cpu()
+    assert torch.equal(ids2[:world * cap], ops.payload_ids(ref_payload))
+    assert bool((ids2[world * cap:, 0] == per_rank).all())
+    assert torch.equal(p2.cpu()[world * cap:, :h], hidden)
+    assert torch.equal(p2.cpu()[used, :h], ref_payload[used, :h])
 
 
 @pytest.mark.gpu
