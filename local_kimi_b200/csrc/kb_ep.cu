@@ -40,16 +40,32 @@ __device__ void ep_positions(const int64_t* idx, int64_t istride, int T, int k, 
                              int world, int* cnt, int* pos, uint8_t* dest, uint32_t* err) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pairs = T * k;
-  for (int a = tid; a < pairs; a += EP_THREADS) {
-    const int t = a / k, r = a - t * k;
-    const int64_t e = idx[(size_t)t * istride + r];
-    int d = 0;
-    if (e < 0 || e >= (int64_t)per_rank * world) {
-      atomicOr(err, 1u);
-    } else {
-      d = (int)(e / per_rank);
+  // Eight ids per thread are requested before any is used (the loads are
+  // independent; one round trip instead of eight).
+  for (int a0 = tid; a0 < pairs; a0 += 8 * EP_THREADS) {
+    int64_t ev[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int a = a0 + i * EP_THREADS;
+      if (a < pairs) {
+        const int t = a / k, r = a - t * k;
+        ev[i] = idx[(size_t)t * istride + r];
+      }
     }
-    dest[a] = (uint8_t)d;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int a = a0 + i * EP_THREADS;
+      if (a < pairs) {
+        const int64_t e = ev[i];
+        int d = 0;
+        if (e < 0 || e >= (int64_t)per_rank * world) {
+          atomicOr(err, 1u);
+        } else {
+          d = (int)(e / per_rank);
+        }
+        dest[a] = (uint8_t)d;
+      }
+    }
   }
   __syncthreads();
   for (int d = warp; d < world; d += EP_THREADS / 32) {
@@ -64,6 +80,27 @@ __device__ void ep_positions(const int64_t* idx, int64_t istride, int T, int k, 
     if (lane == 0) cnt[d] = running;
   }
   __syncthreads();
+}
+
+// Copy of one row of `vecs` 16-byte pieces by a warp: eight pieces per lane
+// are requested before any is stored, so a row costs one memory round trip
+// per 4 KB instead of one per 512 bytes.
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst,
+                                              const uint4* __restrict__ src, int vecs,
+                                              int lane) {
+  for (int v0 = 0; v0 < vecs; v0 += 32 * 8) {
+    uint4 t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int v = v0 + i * 32 + lane;
+      if (v < vecs) t[i] = src[v];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int v = v0 + i * 32 + lane;
+      if (v < vecs) dst[v] = t[i];
+    }
+  }
 }
 
 __global__ void __launch_bounds__(EP_THREADS)
@@ -90,7 +127,7 @@ __global__ void __launch_bounds__(EP_THREADS)
       const int t = a - pairs;
       const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * hs);
       uint4* dst = reinterpret_cast<uint4*>(send_rows + ((size_t)world * capacity + t) * ps);
-      for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+      warp_copy_row(dst, src, vecs, lane);
       if (lane == 0)
         dst[vecs] = make_uint4((uint32_t)shared_id, (uint32_t)((uint64_t)shared_id >> 32), 0u, 0u);
       continue;
@@ -107,7 +144,7 @@ __global__ void __launch_bounds__(EP_THREADS)
     const int slot = d * capacity + p;
     const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * hs);
     uint4* dst = reinterpret_cast<uint4*>(send_rows + (size_t)slot * ps);
-    for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+    warp_copy_row(dst, src, vecs, lane);
     if (lane == 0) {
       const int64_t id = ok ? e - (int64_t)d * per_rank : 0;
       dst[vecs] = make_uint4((uint32_t)id, (uint32_t)((uint64_t)id >> 32), 0u, 0u);
@@ -137,15 +174,32 @@ __global__ void __launch_bounds__(EP_THREADS)
        u += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(u / words), wd = (int)(u - (int64_t)t * words);
     float accum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < k; ++r) {
-      const int slot = slots[t * k + r];
-      const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)slot * H + (size_t)wd * 8);
-      const float wr = w[(size_t)t * wstride + r];
-      const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
+    // Up to eight routes' slots, weights and rows are requested before any is
+    // summed; the sums then run in route order.
+    for (int r0 = 0; r0 < k; r0 += 8) {
+      int sl[8];
+      float wr[8];
+      uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        accum[2 * j] += bf16_bits_to_float((uint16_t)(pv[j] & 0xffffu)) * wr;
-        accum[2 * j + 1] += bf16_bits_to_float((uint16_t)(pv[j] >> 16)) * wr;
+      for (int i = 0; i < 8; ++i)
+        if (r0 + i < k) {
+          sl[i] = slots[t * k + r0 + i];
+          wr[i] = w[(size_t)t * wstride + r0 + i];
+        }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (r0 + i < k)
+          v[i] = *reinterpret_cast<const uint4*>(y + (size_t)sl[i] * H + (size_t)wd * 8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (r0 + i < k) {
+          const uint32_t pv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            accum[2 * j] += bf16_bits_to_float((uint16_t)(pv[j] & 0xffffu)) * wr[i];
+            accum[2 * j + 1] += bf16_bits_to_float((uint16_t)(pv[j] >> 16)) * wr[i];
+          }
+        }
       }
     }
     const uint4 s = *reinterpret_cast<const uint4*>(shared + (size_t)t * ss + (size_t)wd * 8);
