@@ -72,7 +72,8 @@ constexpr int BM = 128;                 // weight rows per tile (MMA M)
 constexpr int KC = 128;                 // reduction elements per chunk (two 128-byte swizzle rows)
 constexpr int W_TILE = BM * KC / 2;     // packed bytes per tile and chunk (64 per row)
 constexpr int A_COLS = KC / 2;          // TMEM columns of one decoded tile chunk (bf16 pairs)
-constexpr int NT_MAX = 64;              // token rows per unit (MMA N bound)
+constexpr int NT_MAX = 64;              // token rows per unit with two accumulator buffers
+constexpr int NT_DENSE_MAX = 128;       // dense units of more rows: one accumulator buffer
 constexpr int TMEM_COLS = 512;          // accumulators [2 buffers][2 tiles][NT], then the A ring
 constexpr int SA_MAX = 3;               // decoded-weight stages in TMEM (2 at NT 64, 3 at NT 32)
 constexpr int W_WARP = 0;
@@ -119,6 +120,7 @@ struct Args {
   int* counters;          // splits > 1: arrival counter per tile (zero between launches)
   int x_tma;              // dense: activations by tensor copies of the map tmx
   int sa, a_base;         // decoded-weight stages in TMEM and the first column of their ring
+  int nbuf;               // accumulator buffers (2: a unit's epilogue overlaps the next unit)
   uint32_t* err;
 };
 
@@ -827,7 +829,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint64_t xhalf = (uint64_t)((NT * 128) >> 4);
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
         const Unit U = unit_of(A, P, u);
-        const int b = uc & 1, use_acc = uc >> 1;
+        const int b = A.nbuf == 2 ? (uc & 1) : 0;
+        const int use_acc = A.nbuf == 2 ? (uc >> 1) : uc;
         if (use_acc > 0 && !wait_phase(&B->acc_empty[b], (use_acc - 1) & 1, abort_f, A.err)) {
           ok = false;
           break;
@@ -874,8 +877,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int uc = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
       const Unit U = unit_of(A, P, u);
-      const int b = uc & 1;
-      if (!wait_phase(&B->acc_full[b], (uc >> 1) & 1, abort_f, A.err)) break;
+      const int b = A.nbuf == 2 ? (uc & 1) : 0;
+      const int use_acc = A.nbuf == 2 ? (uc >> 1) : uc;
+      if (!wait_phase(&B->acc_full[b], use_acc & 1, abort_f, A.err)) break;
       tc_fence_after();
       const int r = q * 32 + lane;
       const int row0 = tile_row(A, U.rt, 0), row1 = tile_row(A, U.rt, 1);
@@ -1111,9 +1115,9 @@ static int smem_limit() {
 // the scale buffers and plan leave no room for two stages of each ring.
 static int layout(Args& A, int plan_ints) {
   const int x_stage = A.nt * KC * 2;
-  // TMEM: accumulators [2 buffers][2 tiles][nt] columns, then the decoded-weight
+  // TMEM: accumulators [nbuf][2 tiles][nt] columns, then the decoded-weight
   // ring (2 tiles x A_COLS columns per stage).
-  A.a_base = 4 * A.nt;
+  A.a_base = 2 * A.nbuf * A.nt;
   A.sa = std::min(SA_MAX, (TMEM_COLS - A.a_base) / (2 * A_COLS));
   const int sc_bytes = (2 * 2 * BM * A.ng * 2 + 1023) / 1024 * 1024;
   const int plan_bytes = (plan_ints * 4 + 127) / 128 * 128;
@@ -1193,20 +1197,40 @@ constexpr int TARGET_CTAS = 148;
 
 // Tiles of a dense problem and the reduction-axis split that brings them to
 // about one CTA per SM (each split keeps at least four 128-wide k-chunks).
-static void dense_split(int64_t M, int64_t K, int64_t N, int* nt, int* tiles, int* splits) {
-  // Token rows per unit: all of M up to 64 (rounded to the MMA's 16), so a
-  // small batch keeps TMEM for a third decoded-weight stage.
-  *nt = (int)std::min<int64_t>(NT_MAX, (M + 15) / 16 * 16);
+static void dense_split_for(int64_t M, int64_t K, int64_t N, int nt, int* tiles, int* splits) {
   const int n_rt = (int)((N + 2 * BM - 1) / (2 * BM));
-  *tiles = n_rt * (int)((M + *nt - 1) / *nt);
+  *tiles = n_rt * (int)((M + nt - 1) / nt);
   const int ks = (int)(K / KC);
   // Splitting pays only when the tiles leave most SMs idle: each split adds
-  // an fp32 partial round trip through L2 and a reduction by the tile's last
-  // CTA.
+  // an fp32 partial round trip through L2 and the deferred reduction.
   int sp = 1;
   if (*tiles * 3 <= TARGET_CTAS)
     sp = std::max(1, std::min(std::min(TARGET_CTAS / *tiles, MAX_SPLITS), ks / 4));
   *splits = sp;
+}
+
+// Token rows per unit and the split: all of M up to 64 (rounded to the
+// MMA's 16), or 128 (each weight decoded once per 128 tokens, one
+// accumulator buffer) when that lowers the most k-chunks any CTA walks (a
+// split counts four chunks for its reduction).
+static void dense_split(int64_t M, int64_t K, int64_t N, int* nt, int* tiles, int* splits) {
+  const int ks = (int)(K / KC);
+  auto cost = [&](int n, int t, int sp) {
+    const int waves = (t * sp + TARGET_CTAS - 1) / TARGET_CTAS;
+    return waves * ((ks + sp - 1) / sp) + (sp > 1 ? 4 : 0);
+  };
+  const int small = (int)std::min<int64_t>(NT_MAX, (M + 15) / 16 * 16);
+  dense_split_for(M, K, N, small, tiles, splits);
+  *nt = small;
+  if (M > NT_MAX) {
+    int t2, s2;
+    dense_split_for(M, K, N, NT_DENSE_MAX, &t2, &s2);
+    if (cost(NT_DENSE_MAX, t2, s2) < cost(small, *tiles, *splits)) {
+      *nt = NT_DENSE_MAX;
+      *tiles = t2;
+      *splits = s2;
+    }
+  }
 }
 
 static size_t split_ws_bytes(int tiles, int splits, int nt) {
@@ -1267,6 +1291,7 @@ extern "C" int kb_w4a16_dense_tc(const uint16_t* x, int64_t x_stride, int64_t M,
   A.ys = y_stride;
   A.n_rt = (int)((N + 2 * kb::tc::BM - 1) / (2 * kb::tc::BM));
   A.nt = nt;
+  A.nbuf = nt > kb::tc::NT_MAX ? 1 : 2;
   A.splits = splits;
   if (splits > 1) {
     const size_t part = (size_t)tiles * splits * 2 * nt * kb::tc::BM * sizeof(float);
@@ -1322,6 +1347,7 @@ static int grouped_tc(int mode, const uint16_t* x, int64_t x_stride, int64_t T, 
   // decode spreads T * R rows over many experts; TMEM then holds three
   // decoded-weight stages), else 64 (one expert taking many rows).
   A.nt = (T * R >= 48 * E) ? kb::tc::NT_MAX : 32;
+  A.nbuf = 2;
   A.splits = 1;
   const int plan_ints = kb::tc::plan_ints_for((int)E, (int)(T * R));
   st = kb::tc::layout(A, plan_ints);
