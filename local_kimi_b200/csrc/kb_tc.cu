@@ -23,9 +23,9 @@
 //     swizzle, plain, no multicast, L2 evict-first), into a ring of SW
 //     shared-memory stages; the unit's bf16 scales (rows contiguous) with one
 //     bulk copy per tile into a double buffer.
-//   warps 1, 3: activation loaders.  Dense mode: two 2-D tensor copies per
-//     chunk (lane 0 of warp 1).  Grouped modes: 16-byte cp.async pieces of the
-//     unit's token rows gathered through the expert plan.  Both write the
+//   warp 1: activation loader.  Dense mode: two 2-D tensor copies per chunk
+//     (lane 0).  Grouped modes: 16-byte cp.async pieces of the unit's token
+//     rows gathered through the expert plan.  Both write the
 //     128-byte-swizzled K-major layout the tensor core reads as its B operand
 //     (two 64-element halves per chunk), into a ring of SX stages.
 //   warps 8-23: decoders, four per TMEM lane quarter (a warp reaches only the
@@ -35,8 +35,7 @@
 //     subtractions and four bf16x2 multiplies -- the one rounding of the
 //     reference) and writes them with two tcgen05.st into a ring of two or
 //     three decoded-weight stages held in tensor memory.
-//   MMA issuers, one per tile (lane 0 of warps 2 and 3 in dense mode, lanes
-//     0 and 1 of warp 2 in the grouped modes; a tcgen05.mma costs
+//   warps 2 and 3 (lane 0): MMA issuers, one per tile (a tcgen05.mma costs
 //     its issuing thread ~110 cycles at these shapes, measured, so one thread
 //     cannot keep the tensor core busy).  Per k-chunk, eight tcgen05.mma with
 //     A (the decoded weights) read from TMEM and B (the activations) from
@@ -85,7 +84,7 @@ constexpr int DEC_WARP0 = 8;
 constexpr int NDEC_WARPS = 16;
 constexpr int NWARPS = DEC_WARP0 + NDEC_WARPS;
 constexpr int NTHREADS = NWARPS * 32;
-constexpr int NXTHREADS = 64;
+constexpr int NXTHREADS = 32;
 constexpr int NISSUERS = 2;             // MMA-issuing threads (one per tile)
 constexpr int MAX_SMEM = 226 * 1024;   // dynamic; the static plan counters take a few bytes
 constexpr int MAX_SX = 12;
@@ -565,6 +564,7 @@ struct Bars {
   // the end of the kernel.
   int red_n;
   int red_unit[MAX_RED];
+  int xoff[NT_MAX];       // grouped modes: the current unit's activation row offsets
 };
 
 // Deferred split-K reduction (dense mode): for each split tile this CTA
@@ -779,12 +779,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int first = max(0, it - A.sx);
       for (int i = first; i < it; ++i) drain_phase(&B->x_full[i % A.sx], (i / A.sx) & 1);
     }
-  } else if (!A.x_tma && (warp == X_WARP0 || warp == X_WARP1)) {
+  } else if (!A.x_tma && warp == X_WARP0) {
     // ------------------------------------------------------ activation loader
-    const int xt = (warp == X_WARP0 ? 0 : 32) + lane;
+    const int xt = lane;
     Ring xr(A.sx);
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit U = unit_of(A, P, u);
+      // The unit's source rows once (the plan lookup and the division by R),
+      // then every chunk's pieces read them from shared memory.
+      __syncwarp();
+      for (int i = lane; i < U.nt; i += 32) {
+        int xrow, yrow;
+        rows_of(A, P, U, i, xrow, yrow);
+        B->xoff[i] = xrow * (int)A.xs;
+      }
+      __syncwarp();
       bool ok = true;
       for (int si = 0; si < U.s1 - U.s0; ++si, xr.next()) {
         const int s = chunk_of(U, si);
@@ -795,12 +804,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // Sixteen 16-byte pieces per token row: pieces 0-7 go to the first
         // 64-element half, 8-15 to the second, each half in the swizzled layout.
         uint8_t* dst = ring_x + (size_t)xr.st * x_stage;
+        const uint16_t* xs = A.x + s * KC;
         for (int p = xt; p < U.nt * 16; p += NXTHREADS) {
           const int i = p >> 4, c = p & 15;
-          int xrow, yrow;
-          rows_of(A, P, U, i, xrow, yrow);
-          cp_async16(dst + (c >> 3) * NT * 128 + sw128_off(i, c & 7),
-                     A.x + (size_t)xrow * A.xs + s * KC + c * 8);
+          cp_async16(dst + (c >> 3) * NT * 128 + sw128_off(i, c & 7), xs + B->xoff[i] + c * 8);
         }
         // The stage's arrival is made by the copies' completion (no wait here),
         // so several stages are in flight per thread.
@@ -809,18 +816,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!ok) break;
     }
     cp_async_wait_all();
-  } else if (warp == MMA_WARP || (A.x_tma && warp == X_WARP1)) {
+  } else if (warp == MMA_WARP || warp == X_WARP1) {
     // ----------------------------------------------------------- MMA issuers
     // One thread per tile: a tcgen05.mma costs its issuing thread about a
     // hundred cycles whatever its size at these shapes, so two issuers with
     // their own accumulators double the rate at which the tensor core is fed.
     // Each commits its own products to the stage barriers (count two).
-    // Dense mode (activations by tensor copies, warp 3 free): lane 0 of warps
-    // 2 and 3, which issue independently.  Grouped modes (warps 1 and 3 gather
-    // activations): lanes 0 and 1 of warp 2, which still issue faster than one.
-    const bool issuer = A.x_tma ? lane == 0 : lane < NISSUERS;
-    if (issuer) {
-      const int mt = A.x_tma ? (warp == MMA_WARP ? 0 : 1) : lane;
+    // Lane 0 of warps 2 and 3: issuers in different warps issue independently
+    // (lanes of one warp share its instruction stream).
+    if (lane == 0) {
+      const int mt = warp == MMA_WARP ? 0 : 1;
       int uc = 0;
       bool ok = true;
       Ring ar(A.sa), xr(A.sx);
@@ -1324,6 +1329,8 @@ static int grouped_tc(int mode, const uint16_t* x, int64_t x_stride, int64_t T, 
                  (mode != kb::tc::SWIGLU || (kb::aligned(w1, 16) && kb::aligned(s1, 16))),
              KB_ERR_ALIGNMENT, "packed weights and scales must be 16-byte aligned");
   KB_REQUIRE(E * N <= (int64_t)1 << 31, KB_ERR_UNSUPPORTED, "grouped (tcgen05): bank too large");
+  KB_REQUIRE(T * x_stride < (int64_t)1 << 31, KB_ERR_UNSUPPORTED,
+             "grouped (tcgen05): activations too large for 32-bit row offsets");
   Args A = {};
   A.mode = mode;
   A.x = x;
