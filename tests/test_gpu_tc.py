@@ -120,3 +120,22 @@ def test_tc_reports_no_device_errors(cuda):
     ops.w4a16_dense_tc(x, packed, scales)
     torch.cuda.synchronize()
     assert _lib.device_errors() == 0
+
+
+def test_single_expert_swiglu_and_down(cuda):
+    # One expert and 300 rows (a dense MLP through the grouped modes): SwiGLU,
+    # then the down projection on its output, in token blocks of 64 rows.
+    gen = cuda_gen(500)
+    w1 = quant_bank(1, 1024, 2304, 128, gen)
+    w3 = quant_bank(1, 1024, 2304, 128, gen)
+    w2 = quant_bank(1, 2304, 1024, 128, gen)
+    x = rand_act((300, 2304), gen)
+    idx = torch.zeros((300, 1), dtype=torch.long, device=cuda)
+    act = ops.w4a16_swiglu_tc(x, idx, *w1, *w3)
+    y = ops.w4a16_grouped_tc(act[:, 0], idx, *w2)
+    torch.cuda.synchronize()
+    ref_act = oref.swiglu(x.cpu(), idx.cpu(), w1[0].cpu(), w1[1].cpu(), w3[0].cpu(),
+                          w3[1].cpu())
+    assert_close(act, ref_act, what="swiglu, one expert, 300 rows")
+    ref = oref.dense(act[:, 0].cpu(), w2[0][0].cpu(), w2[1][0].cpu())
+    assert_close(y[:, 0], ref, what="down, one expert, 300 rows")
