@@ -631,7 +631,7 @@ def _ep_launches(model) -> int:
     n = 1  # lm_head
     for lw in model.layers:
         if lw.kind == "kda":
-            n += 1 + (3 if model.kda_prepare else 2)   # q/k/v: one launch on either path
+            n += 3   # q/k/v (one launch on either path), preparation + KDA step, o_proj
         else:
             both = tc(s.mla_heads * s.mla_q_head_dim, s.hidden) and tc(
                 s.mla_heads * s.mla_kv_head_dim, s.kv_lora_rank)

@@ -229,6 +229,23 @@ KB_API int kb_kda_prepare(const uint16_t* q_in, const uint16_t* k_in, const uint
                           int64_t H, int64_t D, float eps, float* q_out, float* k_out,
                           float* v_out, float* decay_out, float* beta_out, void* stream);
 
+/* KDA decode preparation and step in one launch, for head_dim 128 with       */
+/* contiguous state rows (state strides sb, sh, sk = 128): the arguments of   */
+/* kb_kda_prepare (inputs, convolution states updated in place, gates, eps)  */
+/* followed by kb_kda_decode_step's state, scale and outputs.  Each head's    */
+/* preparation runs the operations of kb_kda_prepare in its order, so state, */
+/* convolution states and outputs equal the two calls' bit for bit.          */
+KB_API int kb_kda_prepare_step(const uint16_t* q_in, const uint16_t* k_in, const uint16_t* v_in,
+                               int64_t in_stride, uint16_t* q_state, uint16_t* k_state,
+                               uint16_t* v_state, const uint16_t* q_weight,
+                               const uint16_t* k_weight, const uint16_t* v_weight,
+                               const uint16_t* raw_decay, int64_t raw_decay_stride,
+                               const float* dt_bias, const float* a_log,
+                               const uint16_t* raw_beta, int64_t raw_beta_stride, float eps,
+                               float* state, int64_t sb, int64_t sh, int64_t sk, int64_t B,
+                               int64_t H, int64_t D, float scale, float* out, uint16_t* out_bf16,
+                               void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Expert-parallel data plane (the layer of engine/klinear/moe.py:278-334 with */
 /* its experts sharded over ranks: expert e on rank e / per_rank).  Fixed-     */

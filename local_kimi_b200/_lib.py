@@ -106,6 +106,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p],
     ),
+    "kb_kda_prepare_step": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_float,
+         c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
+         c_void_p, c_void_p],
+    ),
     "kb_ep_dispatch": (
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,

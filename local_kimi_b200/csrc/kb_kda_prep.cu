@@ -15,36 +15,21 @@
 // of the head: the convolution outputs never leave the SM.  Memory-bound
 // elementwise work: bytes = the three projections in, the three states read
 // and written, decay/beta inputs, the fp32 outputs.
-#include "kb_common.cuh"
+#include "kb_kda_prep.cuh"
 
 namespace kb {
 
 constexpr int KP_MAX_DIM = 256;
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-
-__device__ __forceinline__ float softplus_f(float x) {
-  return x > 20.0f ? x : log1pf(expf(x));
-}
-
-// Convolution of one channel: returns the bf16-rounded output as float and
-// writes the shifted state back.
+// Convolution of one channel in memory: returns the bf16-rounded output as
+// float and writes the shifted state back.
 __device__ __forceinline__ float conv_channel(const uint16_t* in, uint16_t* state,
                                               const uint16_t* w) {
-  const uint2 st = *reinterpret_cast<const uint2*>(state);   // 4 bf16
-  const uint2 wv = *reinterpret_cast<const uint2*>(w);
-  const uint16_t tok = *in;
-  const float s1 = bf16_bits_to_float((uint16_t)(st.x >> 16));
-  const float s2 = bf16_bits_to_float((uint16_t)(st.y & 0xffffu));
-  const float s3 = bf16_bits_to_float((uint16_t)(st.y >> 16));
-  const float t = bf16_bits_to_float(tok);
-  float acc = s1 * bf16_bits_to_float((uint16_t)(wv.x & 0xffffu));
-  acc += s2 * bf16_bits_to_float((uint16_t)(wv.x >> 16));
-  acc += s3 * bf16_bits_to_float((uint16_t)(wv.y & 0xffffu));
-  acc += t * bf16_bits_to_float((uint16_t)(wv.y >> 16));
-  *reinterpret_cast<uint2*>(state) = make_uint2(st.x >> 16 | (st.y << 16),
-                                                (st.y >> 16) | ((uint32_t)tok << 16));
-  return round_bf16(silu_f(acc));
+  uint2 ns;
+  const float y = conv_regs(*reinterpret_cast<const uint2*>(state),
+                            *reinterpret_cast<const uint2*>(w), *in, ns);
+  *reinterpret_cast<uint2*>(state) = ns;
+  return y;
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red, int D) {
@@ -83,19 +68,15 @@ __global__ void kda_prepare_kernel(const uint16_t* __restrict__ q_in,
   const float q = conv_channel(q_in + ii, q_state + si, q_w + (size_t)c * 4);
   const float k = conv_channel(k_in + ii, k_state + si, k_w + (size_t)c * 4);
   const float v = conv_channel(v_in + ii, v_state + si, v_w + (size_t)c * 4);
-  const float rate = expf(a_log[h]);
-  const float biased =
-      bf16_bits_to_float(raw_decay[(size_t)b * rd_stride + c]) + dt_bias[c];
   const size_t oi = (size_t)b * C + c;
-  decay_out[oi] = -rate * softplus_f(biased);
+  decay_out[oi] = kda_decay(a_log[h], raw_decay[(size_t)b * rd_stride + c], dt_bias[c]);
   v_out[oi] = v;
   const float qs = rsqrtf(block_sum(q * q, red, D) + eps);
   const float ks = rsqrtf(block_sum(k * k, red, D) + eps);
   q_out[oi] = q * qs;
   k_out[oi] = k * ks;
   if (d == 0) {
-    const float rb = bf16_bits_to_float(raw_beta[(size_t)b * rb_stride + h]);
-    beta_out[(size_t)b * H + h] = 1.0f / (1.0f + expf(-rb));
+    beta_out[(size_t)b * H + h] = kda_beta(raw_beta[(size_t)b * rb_stride + h]);
   }
   pdl_launch_dependents();
 }

@@ -273,14 +273,26 @@ class HotPathDecoder:
                     q_in, k_in, v_in = y[:, :n], y[:, n:2 * n], y[:, 2 * n:]
                 else:
                     q_in, k_in, v_in = ops.w4a16_dense_multi(probs)
-                if self.kda_prepare:
-                    kin = ops.kda_prepare(q_in, k_in, v_in, *lw.conv_state, *lw.conv_w,
-                                          self.raw_decay, lw.dt_bias, lw.a_log, self.raw_beta,
-                                          num_heads=s.kda_heads, head_dim=s.kda_head_dim)
+                fused = self.kda_prepare and ops.kda_prepare_step_supported(
+                    lw.kda_state, s.kda_head_dim)
+                if fused:
+                    # Preparation and state step in one launch.
+                    ops.kda_prepare_step(lw.kda_state, q_in, k_in, v_in, *lw.conv_state,
+                                         *lw.conv_w, self.raw_decay, lw.dt_bias, lw.a_log,
+                                         self.raw_beta, num_heads=s.kda_heads,
+                                         head_dim=s.kda_head_dim,
+                                         scale=s.kda_head_dim ** -0.5, out_bf16=self.kda_out)
                 else:
-                    kin = (self.kda_q, self.kda_k, self.kda_v, self.kda_decay, self.kda_beta)
-                ops.kda_decode_step(lw.kda_state, *kin, scale=s.kda_head_dim ** -0.5,
-                                    out_bf16=self.kda_out)
+                    if self.kda_prepare:
+                        kin = ops.kda_prepare(q_in, k_in, v_in, *lw.conv_state, *lw.conv_w,
+                                              self.raw_decay, lw.dt_bias, lw.a_log,
+                                              self.raw_beta, num_heads=s.kda_heads,
+                                              head_dim=s.kda_head_dim)
+                    else:
+                        kin = (self.kda_q, self.kda_k, self.kda_v, self.kda_decay,
+                               self.kda_beta)
+                    ops.kda_decode_step(lw.kda_state, *kin, scale=s.kda_head_dim ** -0.5,
+                                        out_bf16=self.kda_out)
                 h = ops.w4a16_dense(self.kda_out, *lw.o_proj)
             else:
                 # q_proj and kv_b feed the attention, whose output feeds o_proj.
@@ -308,7 +320,7 @@ class HotPathDecoder:
     def _count_launches(self) -> int:
         n = 1  # lm_head
         for lw in self.layers:
-            n += (4 if self.kda_prepare else 3) if lw.kind == "kda" else 2
+            n += 3 if lw.kind == "kda" else 2   # q/k/v, (preparation +) KDA step, o_proj
             n += 2 if lw.dense_mlp is not None else 3
         return n
 

@@ -791,6 +791,29 @@ def kda_prepare(q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor,
     inputs of ``kda_decode_step``.  Projections, states, weights, raw_decay and
     raw_beta are bf16; dt_bias and a_log fp32 (a_log [H] or [1, 1, H, 1])."""
     batch = q_in.shape[0]
+    x, weights, rd, rb, a, dt = _kda_prep_args(
+        q_in, k_in, v_in, q_state, k_state, v_state, q_weight, k_weight, v_weight, raw_decay,
+        dt_bias, a_log, raw_beta, num_heads, head_dim)
+    outs = [torch.empty((batch, num_heads, head_dim), dtype=torch.float32, device=q_in.device)
+            for _ in range(4)]
+    beta = torch.empty((batch, num_heads), dtype=torch.float32, device=q_in.device)
+    if batch == 0:
+        return (*outs, beta)
+    _lib.call("kb_kda_prepare", _p(x[0]), _p(x[1]), _p(x[2]), c_int64(x[0].stride(0)),
+              _p(q_state), _p(k_state), _p(v_state), _p(weights[0]), _p(weights[1]),
+              _p(weights[2]), _p(rd), c_int64(rd.stride(0)), _p(dt), _p(a), _p(rb),
+              c_int64(rb.stride(0)), c_int64(batch), c_int64(num_heads), c_int64(head_dim),
+              c_float(eps), _p(outs[0]), _p(outs[1]), _p(outs[2]), _p(outs[3]), _p(beta),
+              _stream(q_in.device))
+    return (*outs, beta)
+
+
+def _kda_prep_args(q_in, k_in, v_in, q_state, k_state, v_state, q_weight, k_weight, v_weight,
+                   raw_decay, dt_bias, a_log, raw_beta, num_heads, head_dim):
+    """Validated, flattened preparation inputs: (q/k/v rows [B, C] sharing one
+    row stride, weights [C, 4], raw_decay [B, C], raw_beta [B, H], a_log [H],
+    dt_bias [C])."""
+    batch = q_in.shape[0]
     c = num_heads * head_dim
     bf = (q_in, k_in, v_in, q_state, k_state, v_state, q_weight, k_weight, v_weight, raw_decay,
           raw_beta)
@@ -812,18 +835,53 @@ def kda_prepare(q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor,
     rb = raw_beta.reshape(batch, num_heads).contiguous()
     a = a_log.reshape(num_heads).contiguous()
     dt = dt_bias.reshape(c).contiguous()
-    outs = [torch.empty((batch, num_heads, head_dim), dtype=torch.float32, device=q_in.device)
-            for _ in range(4)]
-    beta = torch.empty((batch, num_heads), dtype=torch.float32, device=q_in.device)
+    return x, weights, rd, rb, a, dt
+
+
+def kda_prepare_step_supported(state: torch.Tensor, head_dim: int) -> bool:
+    """Whether ``kda_prepare_step`` takes this state: head_dim 128, fp32 CUDA
+    state [B, H, 128, 128] with contiguous 16-byte aligned rows."""
+    return (head_dim == 128 and state.is_cuda and state.dtype == torch.float32
+            and state.ndim == 4 and state.shape[2] == 128 and state.shape[3] == 128
+            and state.stride(3) == 1 and state.stride(2) == 128 and state.stride(1) % 4 == 0
+            and state.stride(0) % 4 == 0 and state.data_ptr() % 16 == 0)
+
+
+def kda_prepare_step(state: torch.Tensor, q_in: torch.Tensor, k_in: torch.Tensor,
+                     v_in: torch.Tensor, q_state: torch.Tensor, k_state: torch.Tensor,
+                     v_state: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                     v_weight: torch.Tensor, raw_decay: torch.Tensor, dt_bias: torch.Tensor,
+                     a_log: torch.Tensor, raw_beta: torch.Tensor, *, num_heads: int,
+                     head_dim: int, scale: float, eps: float = 1e-6,
+                     out_bf16: torch.Tensor | None = None) -> torch.Tensor:
+    """``kda_prepare`` then ``kda_decode_step`` in one launch (same results):
+    the convolution states and the KDA state are updated in place; returns
+    the fp32 output [B, H, D] (and fills ``out_bf16`` if given)."""
+    if not kda_prepare_step_supported(state, head_dim):
+        raise ValueError("kda_prepare_step needs head_dim 128 and a state with contiguous rows")
+    batch = q_in.shape[0]
+    if tuple(state.shape[:2]) != (batch, num_heads):
+        raise ValueError("state must have shape [batch, heads, 128, 128]")
+    x, weights, rd, rb, a, dt = _kda_prep_args(
+        q_in, k_in, v_in, q_state, k_state, v_state, q_weight, k_weight, v_weight, raw_decay,
+        dt_bias, a_log, raw_beta, num_heads, head_dim)
+    if state.device != q_in.device:
+        raise ValueError("the KDA state must be on the device of the inputs")
+    out = torch.empty((batch, num_heads, head_dim), dtype=torch.float32, device=q_in.device)
+    if out_bf16 is not None and (out_bf16.dtype != torch.bfloat16 or
+                                 out_bf16.numel() != out.numel() or
+                                 not out_bf16.is_contiguous()):
+        raise ValueError("out_bf16 must be a contiguous BF16 tensor with B*H*D elements")
     if batch == 0:
-        return (*outs, beta)
-    _lib.call("kb_kda_prepare", _p(x[0]), _p(x[1]), _p(x[2]), c_int64(x[0].stride(0)),
+        return out
+    _lib.call("kb_kda_prepare_step", _p(x[0]), _p(x[1]), _p(x[2]), c_int64(x[0].stride(0)),
               _p(q_state), _p(k_state), _p(v_state), _p(weights[0]), _p(weights[1]),
               _p(weights[2]), _p(rd), c_int64(rd.stride(0)), _p(dt), _p(a), _p(rb),
-              c_int64(rb.stride(0)), c_int64(batch), c_int64(num_heads), c_int64(head_dim),
-              c_float(eps), _p(outs[0]), _p(outs[1]), _p(outs[2]), _p(outs[3]), _p(beta),
-              _stream(q_in.device))
-    return (*outs, beta)
+              c_int64(rb.stride(0)), c_float(eps), _p(state), c_int64(state.stride(0)),
+              c_int64(state.stride(1)), c_int64(state.stride(2)), c_int64(batch),
+              c_int64(num_heads), c_int64(head_dim), c_float(float(scale)), _p(out),
+              _p(out_bf16), _stream(q_in.device))
+    return out
 
 
 def quantise(weight: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:

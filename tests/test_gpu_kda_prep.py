@@ -94,3 +94,56 @@ def test_kda_prepare_rejects_bad_inputs(cuda):
     with pytest.raises(ValueError):
         ops.kda_prepare(x, x, x, st[:, :128], st.clone(), st.clone(), w, w, w, rd, dt, a, rb,
                         num_heads=2, head_dim=128)
+
+
+@pytest.mark.parametrize("batch", [1, 13, 40])
+def test_kda_prepare_step_equals_the_two_calls(cuda, batch):
+    # The fused preparation + step against kb_kda_prepare then
+    # kb_kda_decode_step on the same inputs: identical convolution states, and
+    # identical KDA state and outputs where both step with the streaming
+    # kernel; and against the oracle chain within tolerance.
+    gen = torch.Generator().manual_seed(20261202 + batch)
+    heads, dim = 32, 128
+    c = heads * dim
+    qkv = torch.randn(batch, 3 * c, generator=gen).to(torch.bfloat16)
+    x = [qkv[:, i * c:(i + 1) * c] for i in range(3)]        # one row stride, as the model
+    states = [torch.randn(batch, c, 4, generator=gen).to(torch.bfloat16) for _ in range(3)]
+    weights = [(0.3 * torch.randn(c, 4, generator=gen)).to(torch.bfloat16) for _ in range(3)]
+    raw_decay = torch.randn(batch, c, generator=gen).to(torch.bfloat16)
+    dt_bias = torch.randn(c, generator=gen)
+    a_log = torch.log(1.0 + 15.0 * torch.rand(heads, generator=gen))
+    raw_beta = torch.randn(batch, heads, generator=gen).to(torch.bfloat16)
+    s0 = 0.05 * torch.randn(batch, heads, dim, dim, generator=gen)
+    scale = dim ** -0.5
+    dx = [t.to(cuda) for t in x]
+    dev = [t.to(cuda) for t in (raw_decay, dt_bias, a_log, raw_beta)]
+    dw = [w.to(cuda) for w in weights]
+    st_a = [t.to(cuda) for t in states]
+    kda_a = s0.to(cuda)
+    ob_a = torch.empty(batch, heads, dim, dtype=torch.bfloat16, device=cuda)
+    out_a = ops.kda_prepare_step(kda_a, *dx, *st_a, *dw, *dev, num_heads=heads, head_dim=dim,
+                                 scale=scale, out_bf16=ob_a)
+    st_b = [t.to(cuda) for t in states]
+    kda_b = s0.to(cuda)
+    kin = ops.kda_prepare(*dx, *st_b, *dw, *dev, num_heads=heads, head_dim=dim)
+    ob_b = torch.empty(batch, heads, dim, dtype=torch.bfloat16, device=cuda)
+    out_b = ops.kda_decode_step(kda_b, *kin, scale=scale, out_bf16=ob_b)
+    torch.cuda.synchronize()
+    for sa, sb in zip(st_a, st_b):
+        assert torch.equal(sa, sb)
+    if batch * heads >= 296:
+        # Both paths run the streaming step: identical bits.
+        assert torch.equal(kda_a, kda_b)
+        assert torch.equal(out_a, out_b)
+        assert torch.equal(ob_a, ob_b)
+    else:
+        # The two-call path steps with the column-slice kernel (another order).
+        torch.testing.assert_close(kda_a, kda_b, atol=3e-5, rtol=3e-5)
+        torch.testing.assert_close(out_a, out_b, atol=3e-5, rtol=3e-5)
+    ref_states = [s.clone() for s in states]
+    ref = kda_prep.prepare(*x, *ref_states, *weights, raw_decay, dt_bias, a_log, raw_beta,
+                           num_heads=heads, head_dim=dim)
+    s_ref = s0.clone()
+    o_ref = oref.kda_step(s_ref, *ref[:4], ref[4], scale=scale)
+    torch.testing.assert_close(out_a.cpu(), o_ref, atol=1e-3, rtol=1e-3)
+    torch.testing.assert_close(kda_a.cpu(), s_ref, atol=1e-3, rtol=1e-3)
