@@ -8,6 +8,7 @@ next to this file.  The library exports the C ABI declared in
 
 from __future__ import annotations
 
+import fcntl
 import os
 import shutil
 import subprocess
@@ -53,13 +54,31 @@ def _stale(target: Path, inputs: list[Path]) -> bool:
 
 
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile the library if any source or header is newer than it."""
+    """Compile the library if any source or header is newer than it.
+
+    Safe to call from several processes at once (the ranks of a torchrun
+    launch each call it): the build runs under an exclusive lock on a file in
+    the build directory, and the staleness check is repeated once the lock is
+    held, so one process compiles and the others find the library current.
+    """
     headers = sorted(CSRC.glob("*.cuh")) + sorted((REPO_DIR / "include").glob("*.h"))
     srcs = sources()
     if not force and not _stale(LIB_PATH, srcs + headers):
         return LIB_PATH
-    nvcc = _nvcc()
     BUILD_DIR.mkdir(exist_ok=True)
+    with open(BUILD_DIR / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and not _stale(LIB_PATH, srcs + headers):
+                return LIB_PATH
+            return _compile(srcs, headers, verbose, force, ptxas_verbose)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+def _compile(srcs: list[Path], headers: list[Path], verbose: bool, force: bool,
+             ptxas_verbose: bool) -> Path:
+    nvcc = _nvcc()
     objects = []
     for src in srcs:
         obj = BUILD_DIR / (src.stem + ".o")
@@ -73,7 +92,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = LIB_PATH.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objects)]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
