@@ -35,6 +35,7 @@ host cores, on the same bounded per-step sample, and prints the same metric.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -588,19 +589,64 @@ def _e2e(step_fn, static_x: torch.Tensor, x_host: torch.Tensor, out_buf: torch.T
 
 
 def _capture_all(fn, x, dist):
-    """Capture fn(x) in a CUDA graph (one process).  With several ranks the
-    step runs as eager launches: its NCCL exchanges are not captured."""
-    if dist is not None:
-        return None, None
+    """Capture fn(x) in a CUDA graph on every rank, the NCCL exchanges of the
+    expert-parallel layers included (their sizes are fixed, and nothing in the
+    step reads device data on the host).  The ranks agree on the outcome with
+    an all-reduce of their success flags, so either every rank replays its
+    graph or every rank runs eager launches: all of them always take the same
+    collective steps."""
     graph, out, ok = None, None, 1
     try:
         graph, out = _capture(fn, x)
-    except Exception:
+    except Exception as exc:  # noqa: BLE001 - any capture failure falls back to eager
+        print(f"[bench] graph capture failed: {type(exc).__name__}: {exc}", file=sys.stderr)
         graph, out, ok = None, None, 0
         torch.cuda.synchronize()
+    if dist is not None:
+        flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = int(flag.item())
     if not ok:
         graph, out = None, None
     return graph, out
+
+
+def _recurrent_states(model) -> list[torch.Tensor]:
+    """The tensors a decode step updates in place: KDA and convolution states."""
+    out = []
+    for lw in model.layers:
+        if lw.kda_state is not None:
+            out.append(lw.kda_state)
+        if lw.conv_state is not None:
+            out.extend(lw.conv_state)
+    return out
+
+
+def _graph_parity(model, graph, graph_out, static_x, dist) -> tuple[bool, float]:
+    """One graph replay against one eager step from the same states (restored
+    in between and afterwards): every rank's logits must match its eager
+    step's, within the tolerance of the batch-1 comparison.  The ranks agree
+    on the outcome.  Returns (ok on every rank, this rank's largest |diff|)."""
+    states = _recurrent_states(model)
+    saved = [t.clone() for t in states]
+    graph.replay()
+    torch.cuda.synchronize()
+    ref = graph_out.float().clone()
+    for t, v in zip(states, saved):
+        t.copy_(v)
+    eager = model.step(static_x).float()
+    torch.cuda.synchronize()
+    for t, v in zip(states, saved):
+        t.copy_(v)
+    diff = (eager - ref).abs()
+    tol = torch.maximum(torch.full_like(ref, 1e-3), 2e-2 * ref.abs())
+    ok = int(bool((diff <= tol).all().item()))
+    worst = float(diff.max().item())
+    if dist is not None:
+        flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = int(flag.item())
+    return bool(ok), worst
 
 
 def _ep_step_bytes(model) -> dict[str, int]:
@@ -877,6 +923,15 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     nbytes = _ep_step_bytes(model)
     graph, graph_out = _capture_all(model.step, static_x, dist)
+    graph_check = None
+    if graph is not None:
+        # The replayed graph (at N > 1 with its exchanges) gives an eager step's logits.
+        ok, worst = _graph_parity(model, graph, graph_out, static_x, dist)
+        graph_check = {"graph_vs_eager_max_abs_diff": worst, "agreed": ok}
+        if not ok:
+            print(f"[bench] rank {rank}: graph logits differ from eager (max {worst})",
+                  file=sys.stderr)
+            graph, graph_out = None, None
     if graph is not None:
         step_fn, out_buf, launch = graph.replay, graph_out, "one CUDA graph per step"
     else:
@@ -926,6 +981,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
             "group_size": args.group, "layers": model.nlayers,
             "parallelism": f"ep{world}" if world > 1 else "single",
             "launch": launch,
+            "graph_check": graph_check,
             "l2": "inputs larger than L2 (each step streams GBs of weights and KDA state)",
         },
         "e2e": {"value": round(args.total_batch / e2e_s, 2), "unit": "tok/s",
@@ -941,7 +997,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> dict | None:
         out["cpu_baseline"] = cpu
     out.update(records)
     if dist is not None:
-        del graph
+        # Every reference to a graph that holds NCCL kernels goes before the
+        # process group (the bound replay method keeps the graph alive).
+        torch.cuda.synchronize()
+        step_fn = None
+        del graph, step_fn
+        gc.collect()
         dist.destroy_process_group()
     return out if rank == 0 else None
 
