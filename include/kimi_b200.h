@@ -309,7 +309,7 @@ KB_API int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t T, i
 /* synchronise the device and fail under memory pressure).  Same arguments and */
 /* results as kb_router_topk minus the workspace; it allocates nothing.  Its   */
 /* scratch is one fixed device array per device, kb_router_static_scratch_bytes*/
-/* bytes (528 KiB), which limits T*E to 131072 (e.g. T <= 512 at E = 256);     */
+/* bytes (532,480), which limits T*E to 131072 (e.g. T <= 512 at E = 256);     */
 /* larger calls return KB_ERR_WORKSPACE.  The first call on each device does a */
 /* one-time set-up with that device current (symbol lookup, counter clear on   */
 /* the given stream): make it before any stream capture.  Calls that overlap   */

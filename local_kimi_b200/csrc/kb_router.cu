@@ -9,8 +9,10 @@
 // chosen experts, renormalised by (sum + 1e-20) and multiplied by the scaling
 // factor.
 //
-// Phase 1: CTA (expert block, token block) computes 32 experts x up to 8
-// tokens of logits, each warp 4 experts x 4 tokens per pass (every 16-byte
+// Phase 1: CTA (expert block, token block) computes 32 experts x up to 4
+// tokens of logits (small token blocks: a CTA's latency, not the machine's
+// throughput, sets the kernel's time at decode sizes), each warp 4 experts x
+// 4 tokens per pass (every 16-byte
 // piece it loads feeds four sums), with a fixed reduction order (each lane
 // sums its strided 16-byte pieces in order, then a xor butterfly), so logits
 // are identical run to run.  Phase 2: the CTA that completes a token block
@@ -29,7 +31,7 @@ namespace kb {
 constexpr int RT_WARPS = 8;               // warps per CTA
 constexpr int RT_EW = 4;                  // experts per warp
 constexpr int RT_EXP = RT_WARPS * RT_EW;  // experts per CTA
-constexpr int RT_TOK = 8;                 // tokens per CTA
+constexpr int RT_TOK = 4;                 // tokens per CTA (one pass of each warp)
 constexpr int RT_TQ = 4;                  // tokens per pass of a warp
 
 __global__ void __launch_bounds__(RT_WARPS * 32)
@@ -301,11 +303,11 @@ extern "C" int kb_router_topk(const uint16_t* hidden, int64_t h_stride, int64_t 
 // ---------------------------------------------------------------------------
 namespace kb {
 
-constexpr size_t RT_STATIC_COUNTERS = 1024;                          // token blocks (T <= 8192)
+constexpr size_t RT_STATIC_COUNTERS = 2048;                          // token blocks (T <= 8192)
 constexpr size_t RT_STATIC_LOGITS = 131072;                          // T * E floats (512 KiB)
 constexpr size_t RT_STATIC_COUNTER_BYTES = RT_STATIC_COUNTERS * sizeof(int);
 constexpr size_t RT_STATIC_BYTES =
-    RT_STATIC_COUNTER_BYTES + RT_STATIC_LOGITS * sizeof(float);      // 528 KiB
+    RT_STATIC_COUNTER_BYTES + RT_STATIC_LOGITS * sizeof(float);      // 532,480 bytes
 
 static __device__ __align__(256) uint8_t g_router_static_scratch[RT_STATIC_BYTES];
 
