@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(KS_THREADS, 1)
   int issued = min(KS_STAGES - 1, (BH - (int)blockIdx.x + G - 1) / G);
   int done = 0;
   for (int u = blockIdx.x; u < BH; u += G, ++done) {
-    // One thread waits (bounded); the verdict is shared so that every thread
+    // One thread waits (bounded); its outcome is shared so that every thread
     // leaves the loop together on a timeout.
     if (tid == 0) {
       int ok = 1;
